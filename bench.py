@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the metric path on B200.
+
+Headline (BASELINE.json metric, config 2): SSIM as a training loss, forward +
+backward, fp32 (N=8, C=3, 1080, 1920) per GPU, data_range 1.0, loss =
+1 - ssim(a, b), gradient w.r.t. b -- Gpixel/s over all GPUs (weak scaling:
+every rank scores its own 8-image shard).  Inputs are 398 MB per step, above
+the 126 MB L2, so no flush is needed between steps.
+
+Extra legs on the same line: uint8 PSNR/MSE over config 1 (8x3x1080x1920,
+GB/s against HBM, L2 flushed before every timed call because its 99.5 MB fit
+in L2) and uint8 SSIM forward on the same frames.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N>1) every rank times its own shard on its GPU, the step
+ends with an NCCL all-gather of the per-image loss values, and the reported
+time is the maximum over ranks.  `--impl reference` times the reference's
+CPU implementation on the host cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+SHAPE = (8, 3, 1080, 1920)          # config 2 per GPU
+PIX_SHAPE = (8, 3, 1080, 1920)      # config 1
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def fp32_peak_tflops(sm_mhz: float) -> float:
+    # 148 SMs x 128 FP32 lanes x 2 flop per FMA
+    return 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+
+
+# --------------------------------------------------------------------------- #
+# clocks
+# --------------------------------------------------------------------------- #
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = []
+        for line in Path(self.tmp.name).read_text().splitlines():
+            f = [s.strip() for s in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        load = [r for r in rows if r[2] > 200.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in load for i, v in enumerate(r[3]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in load),
+                "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows),
+                "samples": len(load), "reasons": reasons}
+
+
+# --------------------------------------------------------------------------- #
+# inputs
+# --------------------------------------------------------------------------- #
+
+def cfg2_inputs(seed: int):
+    """Config 2: a ~ U[0,1], b = clamp(a + N(0, 0.05^2), 0, 1), fp32, host."""
+    g = torch.Generator().manual_seed(seed)
+    a = torch.rand(SHAPE, generator=g)
+    b = (a + 0.05 * torch.randn(SHAPE, generator=g)).clamp_(0, 1)
+    return a, b
+
+
+def u8_pair(shape, sigma: float, seed: int):
+    """Configs 0/1/3/4: a ~ U{0..255}, b = clip(a + round(N(0, sigma^2)))."""
+    rng = np.random.default_rng(seed)
+    a = rng.integers(0, 256, shape, dtype=np.uint8)
+    b = np.empty_like(a)
+    fa_, fb = a.reshape(-1), b.reshape(-1)
+    step = 1 << 24
+    for i in range(0, fa_.size, step):
+        n = rng.normal(0, sigma, fa_[i:i + step].size)
+        fb[i:i + step] = np.clip(fa_[i:i + step].astype(np.int16) + np.round(n).astype(np.int16),
+                                 0, 255).astype(np.uint8)
+    return a, b
+
+
+# --------------------------------------------------------------------------- #
+# CPU baseline (oracle/_ref and the C port, both test infrastructure)
+# --------------------------------------------------------------------------- #
+
+def _port_lib():
+    so = REPO / "oracle" / "_build" / "libssim_port.so"
+    if not so.exists():
+        subprocess.run(["make", "-C", str(REPO / "oracle"), "port"], check=False,
+                       stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+    lib = ctypes.CDLL(str(so))
+    lib.ssim_port_fwd_bwd.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                      ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_int]
+    return lib
+
+
+def _ref_cpu_lib(threads: int):
+    so = REPO / "oracle" / "_ref" / "libfa_cpu_ref.so"
+    if not so.exists():
+        return None
+    lib = ctypes.CDLL(str(so))
+    lib.fa_cpu_set_num_threads(threads)
+    return lib
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_fwd_bwd_sample(images: int = 1, threads=None):
+    """SSIM fwd+bwd on `images` config-2 images with the C port, all threads.
+    Returns (Gpixel/s, seconds, threads)."""
+    threads = threads or cpu_threads()
+    lib = _port_lib()
+    a, b = cfg2_inputs(0)
+    a = a[:images].contiguous().numpy()
+    b = b[:images].contiguous().numpy()
+    planes = images * SHAPE[1]
+    w = np.exp(-((np.arange(11) - 5.0) ** 2) / 4.5)
+    w = (w / w.sum()).astype(np.float64)
+    out = np.zeros(planes)
+    dy = np.empty_like(b)
+    hw = (SHAPE[2] - 10) * (SHAPE[3] - 10)
+    t0 = time.perf_counter()
+    rc = lib.ssim_port_fwd_bwd(a.ctypes.data, b.ctypes.data, planes, SHAPE[2], SHAPE[3],
+                               w.ctypes.data, 11, 1e-4, 9e-4, -1.0 / (planes * hw),
+                               out.ctypes.data, None, dy.ctypes.data, threads)
+    dt = time.perf_counter() - t0
+    assert rc == 0
+    return a.size / dt / 1e9, dt, threads
+
+
+def cpu_ref_ssim_fwd_sample(threads=None):
+    """Reference fa_cpu.cpp SSIM forward on one config-2 image (uint8 frames)."""
+    threads = threads or cpu_threads()
+    lib = _ref_cpu_lib(threads)
+    if lib is None:
+        return None
+    a, b = u8_pair((1,) + SHAPE[1:], 8.0, 0)
+    w = np.exp(-((np.arange(11) - 5.0) ** 2) / 4.5)
+    w = (w / w.sum()).astype(np.float32)
+    out = np.zeros(3)
+    args = (a.ctypes.data_as(ctypes.c_void_p), b.ctypes.data_as(ctypes.c_void_p), 0, 1, 3,
+            SHAPE[2], SHAPE[3], w.ctypes.data_as(ctypes.c_void_p), 11, ctypes.c_double(127.5),
+            ctypes.c_double(6.5025), ctypes.c_double(58.5225), None,
+            out.ctypes.data_as(ctypes.c_void_p))
+    lib.fa_cpu_ssim(*args)
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        lib.fa_cpu_ssim(*args)
+    dt = (time.perf_counter() - t0) / reps
+    return a.size / dt / 1e9
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    for _ in range(max(0, args.warmup)):
+        cpu_fwd_bwd_sample(1, threads)
+    times = []
+    for _ in range(args.steps):
+        _, dt, _ = cpu_fwd_bwd_sample(1, threads)
+        times.append(dt)
+    px = int(np.prod(SHAPE[1:]))
+    value = px * len(times) / sum(times) / 1e9
+    sample = (f"1 of the 8 config-2 images per step (3x1080x1920 fp32), SSIM fwd+bwd: "
+              f"C port of the reference's forward and backward (oracle/ssim_port.c), "
+              f"{threads} threads")
+    line = {"impl": "reference", "metric": "ssim_loss_fwd_bwd_gpix_per_s", "value": value,
+            "unit": "Gpixel/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "cfg2 SSIM loss fwd+bwd fp32 8x3x1080x1920 (sampled)"},
+            "cpu_baseline": {"value": value, "unit": "Gpixel/s", "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "Gpixel/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    ref_fwd = cpu_ref_ssim_fwd_sample(threads)
+    if ref_fwd is not None:
+        line["reference_cpu_ssim_forward_u8_gpix_per_s"] = ref_fwd
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- #
+# our arm
+# --------------------------------------------------------------------------- #
+
+def flush_l2(buf: torch.Tensor):
+    buf.add_(1)
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    import frame_analytics_b200 as fa
+    from frame_analytics_b200 import backend
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    backend.lib()  # fail loudly now if the kernels are missing
+
+    hbm, hbm_kind = peaks()
+    a_h, b_h = cfg2_inputs(seed=rank)
+    a_h, b_h = a_h.pin_memory(), b_h.pin_memory()
+    a = a_h.to(dev)
+    b = b_h.to(dev)
+    b.requires_grad_(True)
+    gathered = torch.empty(world, dtype=torch.float64, device=dev)
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(x, y, rec=None):
+        if rec is not None:
+            rec[0].record()
+        loss = 1.0 - fa.ssim(x, y, data_range=1.0)
+        if rec is not None:
+            rec[1].record()
+        (dy,) = torch.autograd.grad(loss, y)
+        if rec is not None:
+            rec[2].record()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, loss.detach().reshape(1))
+        return loss, dy
+
+    for _ in range(args.warmup):
+        step(a, b)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    recs = [(ev(), ev(), ev()) for _ in range(args.steps)]
+    t0, t1 = ev(), ev()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        t0.record()
+        for i in range(args.steps):
+            step(a, b, recs[i])
+        t1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t)
+    px_step = int(np.prod(SHAPE))
+    value = px_step * args.steps * world / (ms / 1e3) / 1e9
+    fwd_ms = statistics.mean(r[0].elapsed_time(r[1]) for r in recs)
+    bwd_ms = statistics.mean(r[1].elapsed_time(r[2]) for r in recs)
+    clocks = clk.summary()
+
+    # algorithmic bytes: forward reads a, b (4 B each); backward reads a, b
+    # and writes d/db (4 B)
+    fwd_bytes, bwd_bytes = 8 * px_step, 12 * px_step
+    dom_ms, dom_bytes, dom_name = (bwd_ms, bwd_bytes, "ssim_bwd") if bwd_ms >= fwd_ms else \
+        (fwd_ms, fwd_bytes, "ssim_fwd")
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    traffic = None
+    tf = REPO / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(dom_name)
+
+    # e2e through the public API from pinned host memory
+    e2e_steps = max(3, args.steps // 2)
+    loss_h = torch.empty(1, dtype=torch.float64).pin_memory()
+
+    def e2e_step():
+        x = a_h.to(dev, non_blocking=True)
+        y = b_h.to(dev, non_blocking=True).requires_grad_(True)
+        loss, _ = step(x, y)
+        loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = ev(), ev()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = px_step * e2e_steps * world / (float(e_ms) / 1e3) / 1e9
+
+    # extra legs (rank-local, reported by rank 0): uint8 PSNR and SSIM forward
+    extra = {}
+    if rank == 0:
+        ua, ub = u8_pair(PIX_SHAPE, 5.0, 0)
+        xu, yu = torch.from_numpy(ua).to(dev), torch.from_numpy(ub).to(dev)
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
+        for _ in range(3):
+            fa.psnr(xu, yu)
+        ts = []
+        for _ in range(max(10, args.steps)):
+            flush_l2(flush)
+            s0, s1 = ev(), ev()
+            s0.record()
+            fa.psnr(xu, yu)
+            s1.record()
+            torch.cuda.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        pm = statistics.median(ts)
+        pbytes = 2 * int(np.prod(PIX_SHAPE))
+        extra["psnr_u8"] = {"workload": "cfg1 PSNR uint8 8x3x1080x1920, L2 flushed",
+                            "ms": pm, "GB/s": pbytes / (pm / 1e3) / 1e9,
+                            "hbm_frac": pbytes / (pm / 1e3) / 1e9 / hbm}
+        for _ in range(3):
+            fa.ssim(xu, yu)
+        ts = []
+        for _ in range(max(5, args.steps // 2)):
+            flush_l2(flush)
+            s0, s1 = ev(), ev()
+            s0.record()
+            fa.ssim(xu, yu)
+            s1.record()
+            torch.cuda.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        sm = statistics.median(ts)
+        extra["ssim_u8_fwd"] = {"workload": "SSIM fwd uint8 8x3x1080x1920, L2 flushed",
+                                "ms": sm, "Gpixel/s": int(np.prod(PIX_SHAPE)) / (sm / 1e3) / 1e9,
+                                "GB/s": pbytes / (sm / 1e3) / 1e9}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gp, dt, thr = cpu_fwd_bwd_sample(1)
+        cpu = {"value": gp, "unit": "Gpixel/s", "cores": thr, "kind": "port",
+               "sample": f"1 config-2 image (3x1080x1920 fp32) SSIM fwd+bwd, C port "
+                         f"(oracle/ssim_port.c), {thr} threads, {dt:.2f} s"}
+        rf = cpu_ref_ssim_fwd_sample(thr)
+        if rf is not None:
+            cpu["reference_ssim_forward_u8_gpix_per_s"] = rf
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    sm_mhz = clocks.get("sm_mhz") or 1965.0
+    line = {
+        "metric": "ssim_loss_fwd_bwd_gpix_per_s",
+        "value": value, "unit": "Gpixel/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 SSIM loss fwd+bwd fp32, 8x3x1080x1920 per GPU, "
+                               "grad w.r.t. b, data_range 1.0",
+                   "global_batch": SHAPE[0] * world, "image": list(SHAPE[1:]),
+                   "parallelism": f"batch shards x{world}",
+                   "l2": "inputs 398 MB/step > 126 MB L2, no flush"},
+        "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": traffic, "peak_source": hbm_kind,
+                     "kernel_ms": dom_ms, "algorithmic_bytes": dom_bytes,
+                     "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                     "fp32_peak_tflops_at_clock": fp32_peak_tflops(sm_mhz)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "Gpixel/s",
+                "h2d_bytes_per_step": 2 * 4 * px_step, "d2h_bytes_per_step": 8,
+                "steps": e2e_steps},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+        "extra": extra,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,320 @@
+"""Marshalling between torch tensors and the C ABI of libfa_b200.so.
+
+Counterpart of the reference's frame_analytics/backend.py, without its tiers:
+there is one backend (the sm_100a kernels) and no fallback.  A call the
+kernels cannot serve raises instead of quietly taking another path.
+
+Every buffer a kernel writes is allocated here through torch's caching
+allocator (outputs per call; scratch once per device and stream), so no
+native call allocates and the calls stay legal inside CUDA-graph capture
+(backend.py:145-153 in the reference states the same rule).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _cabi
+from ._cabi import KernelError, fa_view  # noqa: F401
+
+DTYPE_CODE = {
+    torch.uint8: 0,
+    torch.float16: 1,
+    torch.bfloat16: 2,
+    torch.float32: 3,
+    torch.float64: 4,
+}
+PSNR_NONE = -1.0e300
+OP_MSE, OP_L1, OP_CHARB, OP_HUBER = 0, 1, 2, 3
+KERNEL_WINDOWS = (3, 5, 7, 9, 11)
+
+
+def lib():
+    return _cabi.load()
+
+
+def status() -> dict:
+    try:
+        lib()
+        return {"available": True, "cuda": torch.cuda.is_available(),
+                "library": str(_cabi.library_path()), "error": None}
+    except Exception as exc:  # pragma: no cover - environment dependent
+        return {"available": False, "cuda": False,
+                "library": str(_cabi.library_path()), "error": str(exc)}
+
+
+# --------------------------------------------------------------------------- #
+# input checks
+# --------------------------------------------------------------------------- #
+
+def require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise TypeError(
+                "frame_analytics_b200 computes on CUDA tensors only "
+                f"(got a {t.device} tensor); move the inputs to the GPU")
+
+
+def kernel_dtype(t: torch.Tensor) -> torch.Tensor:
+    """Inputs the kernels read natively pass through; other integer types
+    (int16/int32/uint16) are widened to float32 on the device first."""
+    if t.dtype in DTYPE_CODE:
+        return t
+    return t.to(torch.float32)
+
+
+def _row_ok(t: torch.Tensor) -> bool:
+    return t.shape[-1] == 1 or t.stride(-1) == 1
+
+
+def as_view(t: torch.Tensor) -> Tuple[fa_view, torch.Tensor]:
+    """A 4-D tensor as an ``fa_view`` (strided; W stride must be 1).
+
+    Returns the view and the tensor that owns its memory (a contiguous copy
+    only when the innermost stride is not 1)."""
+    if not _row_ok(t):
+        t = t.contiguous()
+    n, c, h, w = t.shape
+    v = fa_view()
+    v.data = t.data_ptr()
+    v.dtype = DTYPE_CODE[t.dtype]
+    v.n, v.c, v.h, v.w = int(n), int(c), int(h), int(w)
+    v.stride_n, v.stride_c, v.stride_h = int(t.stride(0)), int(t.stride(1)), int(t.stride(2))
+    return v, t
+
+
+def same_layout(x: torch.Tensor, y: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The kernels take one set of strides for both operands."""
+    if x.stride() != y.stride() or not _row_ok(x):
+        x, y = x.contiguous(), y.contiguous()
+    return x, y
+
+
+def _dev(t: torch.Tensor) -> int:
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _luma_arg(luma) -> Optional[ctypes.Array]:
+    if luma is None:
+        return None
+    return (ctypes.c_double * 4)(*[float(v) for v in luma])
+
+
+# --------------------------------------------------------------------------- #
+# scratch
+#
+# Every kernel's first 256 workspace bytes are completion counters that must
+# be zero on entry and are left zero on exit.  One zero-initialised buffer per
+# (device, stream) therefore serves every call issued in order on that stream;
+# it only ever grows.
+# --------------------------------------------------------------------------- #
+
+_ws: dict = {}
+
+
+def workspace(t: torch.Tensor, nbytes: int) -> torch.Tensor:
+    key = (_dev(t), _stream(t))
+    buf = _ws.get(key)
+    if buf is None or buf.numel() < nbytes:
+        size = max(int(nbytes), 1 << 16)
+        if buf is not None:
+            size = max(size, 2 * buf.numel())
+        buf = torch.zeros(size, dtype=torch.uint8, device=t.device)
+        _ws[key] = buf
+    return buf
+
+
+def _drop_workspace(t: torch.Tensor) -> None:
+    # a failed launch may leave a counter non-zero: never reuse that buffer
+    _ws.pop((_dev(t), _stream(t)), None)
+
+
+def _call(t: torch.Tensor, fn, *args) -> None:
+    code = fn(*args)
+    if code != 0:
+        _drop_workspace(t)
+        _cabi.check(code)
+
+
+def _ws_query(fn, *args) -> int:
+    out = ctypes.c_size_t(0)
+    _cabi.check(fn(*args, ctypes.byref(out)))
+    return int(out.value)
+
+
+_wsq_cache: dict = {}
+
+
+def _cached_ws(kind: str, fn, *args) -> int:
+    key = (kind,) + args
+    v = _wsq_cache.get(key)
+    if v is None:
+        v = _ws_query(fn, *args)
+        _wsq_cache[key] = v
+    return v
+
+
+def _f64(t: torch.Tensor, *shape) -> torch.Tensor:
+    return torch.empty(shape, dtype=torch.float64, device=t.device)
+
+
+# --------------------------------------------------------------------------- #
+# pixel reductions
+# --------------------------------------------------------------------------- #
+
+def pixel(x: torch.Tensor, y: torch.Tensor, *, op: int, param: float = 0.0,
+          per_image: bool, psnr_bias: float = PSNR_NONE, luma=None,
+          want_isum: bool = False):
+    """One-launch pixel reduction.  Returns the (N,) or 0-d float64 result
+    (PSNR when ``psnr_bias`` is given) and, if asked, the exact integer sums."""
+    L = lib()
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    n = vx.n
+    dev = _dev(x)
+    nb = _cached_ws("pix", L.fa_b200_pixel_workspace_bytes, n, dev)
+    ws = workspace(x, nb)
+    out = _f64(x, n) if per_image else _f64(x)
+    want_psnr = psnr_bias != PSNR_NONE
+    sinks = [None, None, None, None]
+    sinks[(2 if want_psnr else 0) + (0 if per_image else 1)] = out
+    isum = torch.empty(n, dtype=torch.int64, device=x.device) if want_isum else None
+    _call(x, L.fa_b200_pixel_reduce, ctypes.byref(vx), ctypes.byref(vy),
+          _luma_arg(luma), int(op), float(param), float(psnr_bias),
+          ws.data_ptr(), ws.numel(), _ptr(sinks[0]), _ptr(sinks[1]),
+          _ptr(sinks[2]), _ptr(sinks[3]), _ptr(isum), dev, _stream(x))
+    return (out, isum) if want_isum else out
+
+
+# --------------------------------------------------------------------------- #
+# SSIM
+# --------------------------------------------------------------------------- #
+
+def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
+                 shift: float, C1: float, C2: float, luma=None,
+                 want_map: bool = False, want_plane: bool = False,
+                 want_cs: bool = False, want_per_image: bool = False,
+                 want_total: bool = False) -> dict:
+    """Fused SSIM forward, one launch.  ``win`` is the float32 1-D window on
+    the device.  Returns a dict with the requested outputs."""
+    L = lib()
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    k = int(win.numel())
+    cm = 1 if luma is not None else vx.c
+    hout, wout = vx.h - k + 1, vx.w - k + 1
+    if hout <= 0 or wout <= 0:
+        raise ValueError(f"image {(vx.h, vx.w)} smaller than window {k}x{k}")
+    dev = _dev(x)
+    nb = _cached_ws("ssim", L.fa_b200_ssim_workspace_bytes, vx.n, cm, vx.h, vx.w, k, dev)
+    ws = workspace(x, nb)
+    res = {}
+    res["map"] = (torch.empty((vx.n, cm, hout, wout), dtype=torch.float32,
+                              device=x.device) if want_map else None)
+    res["plane_s"] = _f64(x, vx.n * cm) if (want_plane or want_cs) else None
+    res["plane_cs"] = _f64(x, vx.n * cm) if want_cs else None
+    res["per_image"] = _f64(x, vx.n) if want_per_image else None
+    res["total"] = _f64(x) if want_total else None
+    _call(x, L.fa_b200_ssim, ctypes.byref(vx), ctypes.byref(vy), _luma_arg(luma),
+          win.data_ptr(), k, float(shift), float(C1), float(C2), _ptr(res["map"]),
+          ws.data_ptr(), ws.numel(), _ptr(res["plane_s"]), _ptr(res["plane_cs"]),
+          _ptr(res["per_image"]), _ptr(res["total"]), dev, _stream(x))
+    return res
+
+
+def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
+                  shift: float, C1: float, C2: float,
+                  dmap: Optional[torch.Tensor] = None,
+                  gscalar: Optional[torch.Tensor] = None,
+                  gs: Optional[torch.Tensor] = None,
+                  gcs: Optional[torch.Tensor] = None,
+                  need_dx: bool = True, need_dy: bool = True):
+    """Fused SSIM backward (no scratch).  x, y: float32 (N,C,H,W)."""
+    L = lib()
+    x = x.detach().to(torch.float32).contiguous()
+    y = y.detach().to(torch.float32).contiguous()
+    n, c, h, w = x.shape
+    k = int(win.numel())
+    dx = torch.empty_like(x) if need_dx else None
+    dy = torch.empty_like(y) if need_dy else None
+    if dmap is not None:
+        dmap = dmap.to(torch.float32).contiguous()
+    if gscalar is not None:
+        gscalar = gscalar.to(torch.float32).reshape(1).contiguous()
+    if gs is not None:
+        gs = gs.to(torch.float32).reshape(-1).contiguous()
+        gcs = gcs.to(torch.float32).reshape(-1).contiguous()
+    _call(x, L.fa_b200_ssim_backward, x.data_ptr(), y.data_ptr(), n, c, h, w,
+          win.data_ptr(), k, float(shift), float(C1), float(C2), _ptr(dmap),
+          _ptr(gscalar), _ptr(gs), _ptr(gcs), _ptr(dx), _ptr(dy), _dev(x), _stream(x))
+    return dx, dy
+
+
+# --------------------------------------------------------------------------- #
+# GMSD
+# --------------------------------------------------------------------------- #
+
+def gmsd(x: torch.Tensor, y: torch.Tensor, *, T: float, eps: float,
+         downsample: bool, luma=None, want_map: bool = False):
+    """``(gms_mean, gmsd)`` per image, float64, one launch (plus the float32
+    GMS map when ``want_map``)."""
+    L = lib()
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    cm = 1 if luma is not None else vx.c
+    dev = _dev(x)
+    nb = _cached_ws("gmsd", L.fa_b200_gmsd_workspace_bytes, vx.n, cm, vx.h, vx.w,
+                    int(bool(downsample)), dev)
+    ws = workspace(x, nb)
+    mean = _f64(x, vx.n)
+    std = _f64(x, vx.n)
+    qmap = None
+    if want_map:
+        hd = vx.h // 2 if downsample else vx.h
+        wd = vx.w // 2 if downsample else vx.w
+        qmap = torch.empty((vx.n, cm, hd - 2, wd - 2), dtype=torch.float32, device=x.device)
+    _call(x, L.fa_b200_gmsd, ctypes.byref(vx), ctypes.byref(vy), _luma_arg(luma),
+          float(T), float(eps), int(bool(downsample)), ws.data_ptr(), ws.numel(),
+          _ptr(qmap), mean.data_ptr(), std.data_ptr(), dev, _stream(x))
+    if want_map:
+        return mean, std, qmap
+    return mean, std
+
+
+def gms_map(x, y, *, T: float, eps: float, downsample: bool, luma=None) -> torch.Tensor:
+    """The (N, C', H'-2, W'-2) float32 GMS map."""
+    return gmsd(x, y, T=T, eps=eps, downsample=downsample, luma=luma, want_map=True)[2]
+
+
+# --------------------------------------------------------------------------- #
+# pixel-loss backward
+# --------------------------------------------------------------------------- #
+
+def pixel_backward(x, y, g, *, op: int, param: float, per_image: bool, luma=None,
+                   need_dx: bool = True, need_dy: bool = True):
+    """Gradients of a pixel reduction w.r.t. x and y, in the inputs' dtypes."""
+    L = lib()
+    xf = x.detach().to(torch.float32).contiguous()
+    yf = y.detach().to(torch.float32).contiguous()
+    n, c, h, w = xf.shape
+    gd = g.detach().to(torch.float64).reshape(-1).contiguous()
+    dx = torch.empty_like(xf) if need_dx else None
+    dy = torch.empty_like(yf) if need_dy else None
+    _call(xf, L.fa_b200_pixel_backward, xf.data_ptr(), yf.data_ptr(), n, c, h, w,
+          _luma_arg(luma), int(op), float(param), gd.data_ptr(), int(bool(per_image)),
+          _ptr(dx), _ptr(dy), _dev(xf), _stream(xf))
+    return (dx.to(x.dtype) if need_dx else None, dy.to(y.dtype) if need_dy else None)

@@ -1,0 +1,313 @@
+// extern "C" boundary of libfa_b200.so.  Every entry point validates its
+// arguments on the host, sets the device, and enqueues on the caller's stream;
+// none allocates and none synchronises.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace fab {
+
+int pixel_reduce_impl(const View& a, const View& b, int dtype, const double* luma, int op,
+                      double param, double psnr_bias, void* ws, size_t ws_bytes,
+                      double* out_pi, double* out_tot, double* out_ppi, double* out_ptot,
+                      unsigned long long* out_isum, int device, cudaStream_t st);
+size_t pixel_ws_bytes(int n_images, int device);
+int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, const float* win,
+                  int K, double shift, double C1, double C2, float* map_out, void* ws,
+                  size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
+                  double* out_per_image, double* out_total, int device, cudaStream_t st);
+size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device);
+int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* win,
+                  int K, double shift, double C1, double C2, const float* dmap,
+                  const float* gscalar, const float* gs, const float* gcs, float* dx, float* dy,
+                  int device, cudaStream_t st);
+int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, double T, double eps,
+              int down, void* ws, size_t ws_bytes, float* map_out, double* out_mean,
+              double* out_std, int device, cudaStream_t st);
+int pixel_backward_impl(const float* x, const float* y, int N, int C, int H, int W,
+                        const double* luma, int op, double param, const double* g,
+                        int per_image, float* dx, float* dy, int device, cudaStream_t st);
+size_t gmsd_ws_bytes(int planes, int h, int w, int down, int device);
+
+// The multiprocessor count sizes every grid; cudaDeviceGetAttribute costs
+// microseconds, so it is read once per device.
+int sm_count(int device) {
+  constexpr int MAXD = 64;
+  static int cache[MAXD] = {0};
+  if (device < 0) {
+    if (cudaGetDevice(&device) != cudaSuccess) device = 0;
+  }
+  if (device < MAXD && cache[device] > 0) return cache[device];
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0)
+    v = 148;
+  if (device < MAXD) cache[device] = v;
+  return v;
+}
+
+static View contiguous_view(const void* p, int n, int c, int h, int w) {
+  View v;
+  v.data = p;
+  v.n = n; v.c = c; v.h = h; v.w = w;
+  v.sh = w;
+  v.sc = (long long)h * w;
+  v.sn = (long long)c * h * w;
+  return v;
+}
+
+static bool view_ok(const fa_view* v) {
+  return v && v->data && v->w > 0 && v->h > 0 && v->c > 0 && v->n > 0;
+}
+
+}  // namespace fab
+
+using namespace fab;
+
+extern "C" {
+
+// ---------------------------------------------------------------------------
+// reference-compatible block
+// ---------------------------------------------------------------------------
+
+FA_B200_API int fa_cuda_abi_version(void) { return FA_ABI_VERSION; }
+
+FA_B200_API const char* fa_cuda_error_string(int code) {
+  if (code < 0) return cudaGetErrorString(static_cast<cudaError_t>(-code));
+  switch (code) {
+    case FA_OK: return "ok";
+    case FA_E_DTYPE: return "unsupported dtype";
+    case FA_E_SHAPE: return "unsupported shape";
+    case FA_E_WINDOW: return "unsupported window size";
+    case FA_E_OP: return "unknown pixel op";
+    case FA_E_ARG: return "invalid argument";
+    case FA_E_NOCUDA: return "no CUDA device";
+    default: return "internal error";
+  }
+}
+
+FA_B200_API int fa_cuda_device_count(int* out_count) {
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    if (out_count) *out_count = 0;
+    return -static_cast<int>(e);
+  }
+  if (out_count) *out_count = n;
+  return FA_OK;
+}
+
+FA_B200_API int fa_cuda_pixel_workspace(int64_t n_images, int64_t n_per_image, int device,
+                                        int* out_bpi) {
+  if (!out_bpi) return FA_E_ARG;
+  if (n_images <= 0 || n_per_image <= 0 || n_images > INT32_MAX) return FA_E_SHAPE;
+  const size_t bytes = pixel_ws_bytes((int)n_images, device);
+  const size_t row = (size_t)n_images * 8;
+  *out_bpi = (int)((bytes + row - 1) / row);
+  return FA_OK;
+}
+
+FA_B200_API int fa_cuda_pixel_reduce(const void* a, const void* b, int dtype, int64_t n_images,
+                                     int64_t n_per_image, int op, double param,
+                                     double psnr_bias, double* partial, int bpi,
+                                     double* out_per_image, double* out_total,
+                                     double* out_psnr_per_image, double* out_psnr_total,
+                                     int device, void* stream) {
+  if (!a || !b || !partial) return FA_E_ARG;
+  if (op < 0 || op > 3) return FA_E_OP;
+  if (n_images <= 0 || n_per_image <= 0 || bpi <= 0 || n_images > INT32_MAX ||
+      n_per_image > INT32_MAX)
+    return FA_E_SHAPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the caller's scratch comes from torch.empty: clear the counters
+  FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
+  View va = contiguous_view(a, (int)n_images, 1, 1, (int)n_per_image);
+  View vb = contiguous_view(b, (int)n_images, 1, 1, (int)n_per_image);
+  return pixel_reduce_impl(va, vb, dtype, nullptr, op, param, psnr_bias, partial,
+                           (size_t)n_images * bpi * 8, out_per_image, out_total,
+                           out_psnr_per_image, out_psnr_total, nullptr, device, st);
+}
+
+FA_B200_API int fa_cuda_ssim_workspace(int H, int W, int K, int* out_bpp) {
+  if (!out_bpp) return FA_E_ARG;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  const int Hout = H - K + 1, Wout = W - K + 1;
+  if (Hout <= 0 || Wout <= 0) return FA_E_SHAPE;
+  // per plane: two partial arrays at the most-chunked plan (one plane), plus
+  // the counter block spread over planes
+  const size_t per_plane = ssim_ws_bytes(1, Hout, Wout, K, -1);
+  *out_bpp = (int)((per_plane + 7) / 8);
+  return FA_OK;
+}
+
+FA_B200_API int fa_cuda_ssim(const void* x, const void* y, int dtype, int N, int C, int H, int W,
+                             const float* win, int K, double shift, double C1, double C2,
+                             float* map_out, double* partial, int bpp, double* out_per_image,
+                             double* out_total, int device, void* stream) {
+  if (!x || !y || !win || !partial) return FA_E_ARG;
+  if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
+  View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
+  return ssim_fwd_impl(vx, vy, dtype, nullptr, win, K, shift, C1, C2, map_out, partial,
+                       (size_t)N * C * bpp * 8, nullptr, nullptr, out_per_image, out_total,
+                       device, st);
+}
+
+FA_B200_API int fa_cuda_ssim_cs(const void* x, const void* y, int dtype, int N, int C, int H,
+                                int W, const float* win, int K, double shift, double C1,
+                                double C2, double* partial, double* partial_cs, int bpp,
+                                double* out_s, double* out_cs, int device, void* stream) {
+  if (!x || !y || !win || !partial || !partial_cs || !out_s || !out_cs) return FA_E_ARG;
+  if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
+  View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
+  return ssim_fwd_impl(vx, vy, dtype, nullptr, win, K, shift, C1, C2, nullptr, partial,
+                       (size_t)N * C * bpp * 8, out_s, out_cs, nullptr, nullptr, device, st);
+}
+
+FA_B200_API int fa_cuda_ssim_backward(const float* x, const float* y, const float* dL_dmap,
+                                      const float* grad_scalar, const float* win, int K, int N,
+                                      int C, int H, int W, double shift, double C1, double C2,
+                                      float* aux, float* dx, float* dy, int device,
+                                      void* stream) {
+  (void)aux;
+  if (dL_dmap && grad_scalar) grad_scalar = nullptr;  // the map wins, as in the reference
+  FAB_DEVICE_SCOPE(device);
+  return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, dL_dmap, grad_scalar, nullptr,
+                       nullptr, dx, dy, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_cuda_ssim_cs_backward(const float* x, const float* y, const float* gs,
+                                         const float* gcs, const float* win, int K, int N, int C,
+                                         int H, int W, double shift, double C1, double C2,
+                                         float* aux, float* dx, float* dy, int device,
+                                         void* stream) {
+  (void)aux;
+  if (!gs || !gcs) return FA_E_ARG;
+  FAB_DEVICE_SCOPE(device);
+  return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, nullptr, nullptr, gs, gcs, dx,
+                       dy, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_cuda_gmsd_workspace(int H, int W, int downsample, int* out_bpp) {
+  if (!out_bpp) return FA_E_ARG;
+  if (H <= 0 || W <= 0) return FA_E_SHAPE;
+  const int hd = downsample ? H / 2 : H, wd = downsample ? W / 2 : W;
+  if (hd < 3 || wd < 3) return FA_E_SHAPE;
+  const size_t per_plane = gmsd_ws_bytes(1, H, W, downsample, -1);
+  *out_bpp = (int)((per_plane + 7) / 8);
+  return FA_OK;
+}
+
+FA_B200_API int fa_cuda_gmsd(const void* x, const void* y, int dtype, int N, int C, int H, int W,
+                             double Tc, double eps, int downsample, double* psum,
+                             double* psumsq, int bpp, double* out_mean, double* out_std,
+                             int device, void* stream) {
+  (void)psumsq;
+  if (!x || !y || !psum || !out_mean || !out_std) return FA_E_ARG;
+  if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FAB_TRY(cudaMemsetAsync(psum, 0, FAB_COUNTER_BYTES, st));
+  View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
+  return gmsd_impl(vx, vy, dtype, nullptr, Tc, eps, downsample, psum, (size_t)N * C * bpp * 8,
+                   nullptr, out_mean, out_std, device, st);
+}
+
+// ---------------------------------------------------------------------------
+// extended block
+// ---------------------------------------------------------------------------
+
+FA_B200_API int fa_b200_abi_version(void) { return FA_B200_ABI_VERSION; }
+
+FA_B200_API int fa_b200_pixel_workspace_bytes(int n_images, int device, size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (n_images <= 0) return FA_E_SHAPE;
+  *out_bytes = pixel_ws_bytes(n_images, device);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_pixel_reduce(const fa_view* a, const fa_view* b, const double* luma,
+                                     int op, double param, double psnr_bias, void* workspace,
+                                     size_t workspace_bytes, double* out_per_image,
+                                     double* out_total, double* out_psnr_per_image,
+                                     double* out_psnr_total, uint64_t* out_isum_per_image,
+                                     int device, void* stream) {
+  if (!view_ok(a) || !view_ok(b)) return FA_E_ARG;
+  if (a->dtype != b->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  return pixel_reduce_impl(to_view(*a), to_view(*b), a->dtype, luma, op, param, psnr_bias,
+                           workspace, workspace_bytes, out_per_image, out_total,
+                           out_psnr_per_image, out_psnr_total,
+                           reinterpret_cast<unsigned long long*>(out_isum_per_image), device,
+                           static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_ssim_workspace_bytes(int n, int c, int h, int w, int K, int device,
+                                             size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  if (n <= 0 || c <= 0 || h - K + 1 <= 0 || w - K + 1 <= 0) return FA_E_SHAPE;
+  *out_bytes = ssim_ws_bytes(n * c, h - K + 1, w - K + 1, K, device);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y, const double* luma,
+                             const float* win, int K, double shift, double C1, double C2,
+                             float* map_out, void* workspace, size_t workspace_bytes,
+                             double* out_plane_s, double* out_plane_cs, double* out_per_image,
+                             double* out_total, int device, void* stream) {
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  return ssim_fwd_impl(to_view(*x), to_view(*y), x->dtype, luma, win, K, shift, C1, C2, map_out,
+                       workspace, workspace_bytes, out_plane_s, out_plane_cs, out_per_image,
+                       out_total, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_ssim_backward(const float* x, const float* y, int N, int C, int H, int W,
+                                      const float* win, int K, double shift, double C1,
+                                      double C2, const float* dL_dmap, const float* g_scalar,
+                                      const float* gs, const float* gcs, float* dx, float* dy,
+                                      int device, void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, dL_dmap, g_scalar, gs, gcs, dx,
+                       dy, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_gmsd_workspace_bytes(int n, int c, int h, int w, int downsample,
+                                             int device, size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return FA_E_SHAPE;
+  const int hd = downsample ? h / 2 : h, wd = downsample ? w / 2 : w;
+  if (hd < 3 || wd < 3) return FA_E_SHAPE;
+  *out_bytes = gmsd_ws_bytes(n * c, h, w, downsample, device);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_gmsd(const fa_view* x, const fa_view* y, const double* luma, double T,
+                             double eps, int downsample, void* workspace,
+                             size_t workspace_bytes, float* map_out, double* out_mean,
+                             double* out_std, int device, void* stream) {
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  return gmsd_impl(to_view(*x), to_view(*y), x->dtype, luma, T, eps, downsample, workspace,
+                   workspace_bytes, map_out, out_mean, out_std, device,
+                   static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N, int C, int H,
+                                       int W, const double* luma, int op, double param,
+                                       const double* g, int per_image, float* dx, float* dy,
+                                       int device, void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return pixel_backward_impl(x, y, N, C, H, W, luma, op, param, g, per_image, dx, dy, device,
+                             static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,553 @@
+"""Public metric functions: the drop-in surface of frame_analytics.functional.
+
+Same names, arguments, defaults, shapes and error behaviour as the reference
+(frame_analytics/functional.py), computed by the sm_100a kernels of
+libfa_b200.so.  Luma projection and border cropping are folded into the kernel
+loads; there is no portable/torch path, so a call the kernels cannot serve
+raises instead of falling back.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import backend
+
+__all__ = [
+    "mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier",
+    "huber", "rgb_to_luma", "gaussian_window_1d", "set_compile_enabled",
+    "MS_SSIM_WEIGHTS", "LUMA_COEFFS",
+]
+
+# Wang et al. 2003, table 1 (functional.py:697 in the reference).
+MS_SSIM_WEIGHTS = (0.0448, 0.2856, 0.3001, 0.2363, 0.1333)
+
+# (r, g, b, offset as a fraction of the data range) -- functional.py:193-197.
+LUMA_COEFFS = {
+    "bt601": (0.299, 0.587, 0.114, 0.0),
+    "bt709": (0.2126, 0.7152, 0.0722, 0.0),
+    "matlab": (65.481 / 255.0, 128.553 / 255.0, 24.966 / 255.0, 16.0 / 255.0),
+}
+
+
+def set_compile_enabled(flag: bool) -> None:
+    """Accepted for drop-in compatibility (functional.py:55-59); the kernels
+    here are compiled ahead of time, so there is nothing to switch."""
+
+
+# --------------------------------------------------------------------------- #
+# input handling (functional.py:141-271)
+# --------------------------------------------------------------------------- #
+
+def _infer_data_range(t: torch.Tensor) -> float:
+    if t.dtype == torch.uint8:
+        return 255.0
+    if t.dtype in (torch.int16, torch.int32):
+        return 65535.0
+    if getattr(torch, "uint16", None) is not None and t.dtype == torch.uint16:
+        return 65535.0
+    return 1.0
+
+
+def _as_nchw(t: torch.Tensor) -> torch.Tensor:
+    if t.ndim == 2:
+        return t.unsqueeze(0).unsqueeze(0)
+    if t.ndim == 3:
+        return t.unsqueeze(0)
+    if t.ndim == 4:
+        return t
+    raise ValueError(f"expected 2/3/4-D tensor, got shape {tuple(t.shape)}")
+
+
+def _check_pair(x: torch.Tensor, y: torch.Tensor):
+    if x.shape != y.shape:
+        raise ValueError(f"shape mismatch: {tuple(x.shape)} vs {tuple(y.shape)}")
+    if x.device != y.device:
+        raise ValueError(f"device mismatch: {x.device} vs {y.device}")
+    return _as_nchw(x), _as_nchw(y)
+
+
+def _resolve_luma(luma) -> Optional[str]:
+    if luma is None or luma is False:
+        return None
+    if luma is True:
+        return "bt601"
+    if isinstance(luma, str):
+        if luma not in LUMA_COEFFS:
+            raise ValueError(f"unknown luma mode {luma!r}; "
+                             f"expected one of {sorted(LUMA_COEFFS)}")
+        return luma
+    raise TypeError(f"luma must be None, a bool or a string, got {type(luma).__name__}")
+
+
+def _crop_border(t: torch.Tensor, b: int) -> torch.Tensor:
+    if not b:
+        return t
+    if b < 0:
+        raise ValueError(f"crop_border must be >= 0, got {b}")
+    h, w = t.shape[-2], t.shape[-1]
+    if h <= 2 * b or w <= 2 * b:
+        raise ValueError(f"crop_border={b} removes the whole {h}x{w} image")
+    return t[..., b:h - b, b:w - b]
+
+
+def _prep(x, y, luma, crop_border, data_range):
+    """Shape check, border crop (a view), luma resolution -> (x4, y4, L, mode)."""
+    x4, y4 = _check_pair(x, y)
+    L = float(data_range) if data_range is not None else _infer_data_range(x4)
+    mode = _resolve_luma(luma)
+    x4 = _crop_border(x4, crop_border)
+    y4 = _crop_border(y4, crop_border)
+    if mode is not None and x4.shape[1] != 3:
+        raise ValueError(f"luma needs a 3-channel image, got {x4.shape[1]} channels")
+    return x4, y4, L, mode
+
+
+def _luma_k(mode: Optional[str], L: float):
+    """Luma coefficients in the metric's units: (cr, cg, cb, offset * L)."""
+    if mode is None:
+        return None
+    cr, cg, cb, off = LUMA_COEFFS[mode]
+    return (cr, cg, cb, off * L)
+
+
+def _check_reduction(reduction: str) -> None:
+    if reduction not in ("mean", "none"):
+        raise ValueError(f"reduction must be 'mean' or 'none', got {reduction!r}")
+
+
+def _check_hint(backend_hint: str) -> None:
+    if backend_hint not in ("auto", "native", "torch"):
+        raise ValueError(f"backend_hint must be 'auto', 'native' or 'torch', got {backend_hint!r}")
+    if backend_hint == "torch":
+        raise NotImplementedError(
+            "frame_analytics_b200 has no portable torch path; every metric runs on the "
+            "sm_100a kernels (backend_hint='auto' or 'native')")
+
+
+def _grad_wanted(*ts: torch.Tensor) -> bool:
+    return torch.is_grad_enabled() and any(t.requires_grad for t in ts)
+
+
+def rgb_to_luma(t: torch.Tensor, mode: str = "bt601", *,
+                data_range: Optional[float] = None,
+                dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """``(N,3,H,W)`` RGB -> ``(N,1,H,W)`` luma (functional.py:213-237).
+
+    The metric functions never call this: their kernels apply the same
+    projection while loading.  It is kept for callers that want the plane."""
+    t4 = _as_nchw(t)
+    if t4.shape[1] != 3:
+        raise ValueError(f"luma needs a 3-channel image, got {t4.shape[1]} channels")
+    m = _resolve_luma(mode)
+    if m is None:
+        raise ValueError("rgb_to_luma needs a luma convention, not None/False")
+    cr, cg, cb, off = LUMA_COEFFS[m]
+    L = float(data_range) if data_range is not None else _infer_data_range(t4)
+    wdt = dtype if dtype is not None else (torch.float64 if t4.dtype == torch.float64
+                                           else torch.float32)
+    v = t4.to(wdt)
+    out = cr * v[:, 0:1] + cg * v[:, 1:2] + cb * v[:, 2:3]
+    if off:
+        out = out + off * L
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# pixel reductions with autograd
+# --------------------------------------------------------------------------- #
+
+class _PixelLoss(torch.autograd.Function):
+    """Differentiable pixel reduction: forward by the fused kernel, backward by
+    the elementwise derivative of the penalty (nothing is saved but x, y)."""
+
+    @staticmethod
+    def forward(ctx, x, y, op, param, per_image, luma):
+        out = backend.pixel(x, y, op=op, param=param, per_image=per_image, luma=luma)
+        ctx.save_for_backward(x, y)
+        ctx.op, ctx.param, ctx.per_image, ctx.luma = op, param, per_image, luma
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        _reject_double_backward()
+        x, y = ctx.saved_tensors
+        dx, dy = backend.pixel_backward(x, y, g, op=ctx.op, param=ctx.param,
+                                        per_image=ctx.per_image, luma=ctx.luma,
+                                        need_dx=ctx.needs_input_grad[0],
+                                        need_dy=ctx.needs_input_grad[1])
+        return dx, dy, None, None, None, None
+
+
+def _pixel(x4, y4, op, param, per_image, luma_k, psnr_bias=backend.PSNR_NONE):
+    backend.require_cuda(x4)
+    if _grad_wanted(x4, y4):
+        if psnr_bias != backend.PSNR_NONE:
+            m = _PixelLoss.apply(x4, y4, op, param, per_image, luma_k)
+            return psnr_bias - 10.0 * torch.log10(m)
+        return _PixelLoss.apply(x4, y4, op, param, per_image, luma_k)
+    return backend.pixel(x4.detach(), y4.detach(), op=op, param=param,
+                         per_image=per_image, psnr_bias=psnr_bias, luma=luma_k)
+
+
+def mse(x: torch.Tensor, y: torch.Tensor, *, reduction: str = "mean",
+        dtype: Optional[torch.dtype] = None, out_dtype: torch.dtype = torch.float64,
+        luma=None, crop_border: int = 0) -> torch.Tensor:
+    """Mean squared error (functional.py:289-343).  uint8 input is summed in
+    64-bit integers on the device, so the result is exact."""
+    x4, y4, L, mode = _prep(x, y, luma, crop_border, None)
+    _check_reduction(reduction)
+    out = _pixel(x4, y4, backend.OP_MSE, 0.0, reduction == "none", _luma_k(mode, L))
+    return out.to(out_dtype)
+
+
+def psnr(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
+         reduction: str = "mean", dtype: Optional[torch.dtype] = None,
+         out_dtype: torch.dtype = torch.float64, eps: float = 0.0, luma=None,
+         crop_border: int = 0) -> torch.Tensor:
+    """PSNR in dB (functional.py:345-387); +inf for identical inputs unless
+    ``eps`` clamps the MSE.  The dB conversion happens inside the kernel."""
+    _check_reduction(reduction)
+    x4, y4, L, mode = _prep(x, y, luma, crop_border, data_range)
+    bias = math.log10(L * L) * 10.0
+    if not eps:
+        return _pixel(x4, y4, backend.OP_MSE, 0.0, reduction == "none",
+                      _luma_k(mode, L), psnr_bias=bias).to(out_dtype)
+    m = _pixel(x4, y4, backend.OP_MSE, 0.0, reduction == "none", _luma_k(mode, L))
+    m = m.clamp_min(eps)
+    return (bias - 10.0 * torch.log10(m)).to(out_dtype)
+
+
+def _pixel_loss(op, x, y, param, reduction, out_dtype, luma, crop_border, backend_hint):
+    _check_reduction(reduction)
+    _check_hint(backend_hint)
+    x4, y4, L, mode = _prep(x, y, luma, crop_border, None)
+    return _pixel(x4, y4, op, param, reduction == "none", _luma_k(mode, L)).to(out_dtype)
+
+
+def l1(x: torch.Tensor, y: torch.Tensor, *, reduction: str = "mean",
+       dtype: Optional[torch.dtype] = None, out_dtype: torch.dtype = torch.float64,
+       luma=None, crop_border: int = 0, backend_hint: str = "auto") -> torch.Tensor:
+    """Mean absolute error (functional.py:1157-1170)."""
+    return _pixel_loss(backend.OP_L1, x, y, 0.0, reduction, out_dtype, luma,
+                       crop_border, backend_hint)
+
+
+def charbonnier(x: torch.Tensor, y: torch.Tensor, *, eps: float = 1e-3,
+                reduction: str = "mean", dtype: Optional[torch.dtype] = None,
+                out_dtype: torch.dtype = torch.float64, luma=None, crop_border: int = 0,
+                backend_hint: str = "auto") -> torch.Tensor:
+    """``mean sqrt((x-y)^2 + eps^2)`` (functional.py:1173-1191)."""
+    return _pixel_loss(backend.OP_CHARB, x, y, float(eps) ** 2, reduction, out_dtype,
+                       luma, crop_border, backend_hint)
+
+
+def huber(x: torch.Tensor, y: torch.Tensor, *, delta: float = 1.0,
+          reduction: str = "mean", dtype: Optional[torch.dtype] = None,
+          out_dtype: torch.dtype = torch.float64, luma=None, crop_border: int = 0,
+          backend_hint: str = "auto") -> torch.Tensor:
+    """Huber loss matching ``torch.nn.HuberLoss`` (functional.py:1194-1210)."""
+    if delta <= 0:
+        raise ValueError(f"delta must be > 0, got {delta}")
+    return _pixel_loss(backend.OP_HUBER, x, y, float(delta), reduction, out_dtype,
+                       luma, crop_border, backend_hint)
+
+
+# --------------------------------------------------------------------------- #
+# SSIM
+# --------------------------------------------------------------------------- #
+
+_window_cache: dict = {}
+
+
+def gaussian_window_1d(win_size: int = 11, sigma: float = 1.5, *, device=None,
+                       dtype=torch.float32) -> torch.Tensor:
+    """Sum-normalised 1-D Gaussian (functional.py:397-420); the 2-D window is
+    its outer product.  Cached per (size, sigma, device, dtype)."""
+    key = (win_size, sigma, str(device), dtype)
+    w = _window_cache.get(key)
+    if w is not None:
+        return w
+    r = (win_size - 1) / 2.0
+    coords = torch.arange(win_size, dtype=torch.float64) - r
+    g = torch.exp(-(coords * coords) / (2.0 * sigma * sigma))
+    g = g / g.sum()
+    w = g.to(device=device, dtype=dtype)
+    _window_cache[key] = w
+    return w
+
+
+def _reject_double_backward() -> None:
+    """Refuse ``create_graph=True`` through a fused kernel (functional.py:496-518)."""
+    if torch.is_grad_enabled():
+        raise RuntimeError(
+            "frame_analytics_b200's fused backward kernels are not twice "
+            "differentiable, so create_graph=True (gradient penalties, "
+            "Hessian-vector products, torch.func.hessian) cannot use them.")
+
+
+def _kernel_window(win_size: int, sigma: float, device) -> torch.Tensor:
+    if win_size not in backend.KERNEL_WINDOWS:
+        raise ValueError(f"win_size must be one of {backend.KERNEL_WINDOWS}, got {win_size}")
+    return gaussian_window_1d(win_size, sigma, device=device, dtype=torch.float32)
+
+
+class _FusedSSIM(torch.autograd.Function):
+    """Differentiable SSIM (functional.py:521-572).  Forward: the fused
+    kernel.  Backward: one fused kernel that recomputes the moments; only x,
+    y and the window are saved.
+
+    ``mode``: "mean" (batch mean scalar), "none" (per image) or "map"."""
+
+    @staticmethod
+    def forward(ctx, x, y, win, shift, C1, C2, mode):
+        res = backend.ssim_forward(x, y, win, shift=shift, C1=C1, C2=C2,
+                                   want_map=(mode == "map"),
+                                   want_per_image=(mode == "none"),
+                                   want_total=(mode == "mean"))
+        ctx.save_for_backward(x, y, win)
+        ctx.consts = (shift, C1, C2)
+        ctx.mode = mode
+        if mode == "map":
+            return res["map"]
+        return res["per_image"] if mode == "none" else res["total"]
+
+    @staticmethod
+    def backward(ctx, g):
+        _reject_double_backward()
+        x, y, win = ctx.saved_tensors
+        shift, C1, C2 = ctx.consts
+        nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (nx or ny):
+            return (None,) * 7
+        kw = dict(shift=shift, C1=C1, C2=C2, need_dx=nx, need_dy=ny)
+        if ctx.mode == "map":
+            dx, dy = backend.ssim_backward(x, y, win, dmap=g, **kw)
+        elif ctx.mode == "mean":
+            # the scalar upstream gradient stays on the device: no host sync
+            dx, dy = backend.ssim_backward(x, y, win, gscalar=g, **kw)
+        else:
+            n, c = x.shape[0], x.shape[1]
+            gs = (g.to(torch.float32) / c).repeat_interleave(c)
+            dx, dy = backend.ssim_backward(x, y, win, gs=gs, gcs=torch.zeros_like(gs), **kw)
+        return (dx.to(x.dtype) if nx else None, dy.to(y.dtype) if ny else None,
+                None, None, None, None, None)
+
+
+def _matlab_downsample(x: torch.Tensor, f: int) -> torch.Tensor:
+    """MATLAB ssim.m's automatic box downsample (functional.py:575-586)."""
+    if f <= 1:
+        return x
+    n, c, h, w = x.shape
+    ker = x.new_full((1, 1, f, f), 1.0 / (f * f))
+    pad = f // 2
+    xp = F.pad(x.reshape(n * c, 1, h, w), (pad, pad, pad, pad), mode="replicate")
+    with torch.autocast(device_type=x.device.type, enabled=False):
+        lp = F.conv2d(xp, ker)
+    lp = lp.reshape(n, c, lp.shape[-2], lp.shape[-1])
+    return lp[:, :, ::f, ::f].contiguous()
+
+
+def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
+         win_size: int = 11, sigma: float = 1.5, K: Sequence[float] = (0.01, 0.03),
+         reduction: str = "mean", return_map: bool = False,
+         dtype: Optional[torch.dtype] = None, downsample: bool = False,
+         backend_hint: str = "auto", luma=None, crop_border: int = 0) -> torch.Tensor:
+    """Structural similarity (functional.py:589-689): 11x11 Gaussian, sigma
+    1.5, K = (0.01, 0.03), valid support.  ``reduction`` 'mean' -> scalar,
+    'none' -> (N,); ``return_map`` -> (N, C, H-10, W-10) float32."""
+    _check_reduction(reduction)
+    _check_hint(backend_hint)
+    x4, y4, L, mode = _prep(x, y, luma, crop_border, data_range)
+    backend.require_cuda(x4)
+    K1, K2 = float(K[0]), float(K[1])
+    C1, C2 = (K1 * L) ** 2, (K2 * L) ** 2
+    shift = 0.5 * L
+    lk = _luma_k(mode, L)
+    grad = _grad_wanted(x4, y4)
+
+    if downsample:
+        if lk is not None:
+            x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
+            lk = None
+        f = max(1, int(round(min(x4.shape[-2], x4.shape[-1]) / 256.0)))
+        if f > 1:
+            x4 = _matlab_downsample(x4.to(torch.float32), f)
+            y4 = _matlab_downsample(y4.to(torch.float32), f)
+
+    if x4.shape[-2] < win_size or x4.shape[-1] < win_size:
+        raise ValueError(f"image {tuple(x4.shape[-2:])} smaller than window {win_size}x{win_size}")
+    win = _kernel_window(win_size, sigma, x4.device)
+
+    if grad:
+        # the fused backward reads float32 planes: luma/crop/cast are applied
+        # with differentiable torch ops first
+        if lk is not None:
+            x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
+        xf = x4 if x4.dtype == torch.float32 else x4.to(torch.float32)
+        yf = y4 if y4.dtype == torch.float32 else y4.to(torch.float32)
+        m = "map" if return_map else reduction
+        return _FusedSSIM.apply(xf.contiguous(), yf.contiguous(), win, shift, C1, C2, m)
+
+    x4, y4 = x4.detach(), y4.detach()
+    res = backend.ssim_forward(x4, y4, win, shift=shift, C1=C1, C2=C2, luma=lk,
+                               want_map=return_map,
+                               want_per_image=(not return_map and reduction == "none"),
+                               want_total=(not return_map and reduction == "mean"))
+    if return_map:
+        out = res["map"]
+        if x4.dtype == torch.float64 or dtype == torch.float64:
+            out = out.to(torch.float64)
+        return out
+    return res["per_image"] if reduction == "none" else res["total"]
+
+
+# --------------------------------------------------------------------------- #
+# MS-SSIM
+# --------------------------------------------------------------------------- #
+
+class _FusedSSIMCS(torch.autograd.Function):
+    """Differentiable per-plane ``(ssim, cs)`` means (functional.py:749-783)."""
+
+    @staticmethod
+    def forward(ctx, x, y, win, shift, C1, C2):
+        res = backend.ssim_forward(x, y, win, shift=shift, C1=C1, C2=C2, want_cs=True)
+        ctx.save_for_backward(x, y, win)
+        ctx.consts = (shift, C1, C2)
+        return res["plane_s"], res["plane_cs"]
+
+    @staticmethod
+    def backward(ctx, g_s, g_cs):
+        _reject_double_backward()
+        x, y, win = ctx.saved_tensors
+        shift, C1, C2 = ctx.consts
+        nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (nx or ny):
+            return (None,) * 6
+        if g_s is None:
+            g_s = torch.zeros(x.shape[0] * x.shape[1], dtype=torch.float32, device=x.device)
+        if g_cs is None:
+            g_cs = torch.zeros_like(g_s)
+        dx, dy = backend.ssim_backward(x, y, win, shift=shift, C1=C1, C2=C2,
+                                       gs=g_s, gcs=g_cs, need_dx=nx, need_dy=ny)
+        return (dx if nx else None, dy if ny else None, None, None, None, None)
+
+
+def _ms_weights(w, device) -> torch.Tensor:
+    key = (w, str(device))
+    t = _ms_weight_cache.get(key)
+    if t is None:
+        t = torch.tensor(w, dtype=torch.float64, device=device).view(-1, 1, 1)
+        _ms_weight_cache[key] = t
+    return t
+
+
+_ms_weight_cache: dict = {}
+
+
+def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
+            win_size: int = 11, sigma: float = 1.5, K: Sequence[float] = (0.01, 0.03),
+            weights: Optional[Sequence[float]] = None, reduction: str = "mean",
+            dtype: Optional[torch.dtype] = None, backend_hint: str = "auto", luma=None,
+            crop_border: int = 0) -> torch.Tensor:
+    """Multi-scale SSIM (functional.py:811-901): per channel
+    prod_j max(cs_j, 0)^w_j (the coarsest scale contributes full SSIM),
+    channels averaged after the product, 2x2 mean pooling between scales."""
+    _check_reduction(reduction)
+    _check_hint(backend_hint)
+    w = tuple(float(v) for v in (weights if weights is not None else MS_SSIM_WEIGHTS))
+    if not w:
+        raise ValueError("weights must not be empty")
+    x4, y4, L, mode = _prep(x, y, luma, crop_border, data_range)
+    backend.require_cuda(x4)
+    K1, K2 = float(K[0]), float(K[1])
+    C1, C2 = (K1 * L) ** 2, (K2 * L) ** 2
+    shift = 0.5 * L
+    need = (win_size - 1) * (1 << (len(w) - 1)) + (1 << (len(w) - 1))
+    if min(x4.shape[-2], x4.shape[-1]) < need:
+        raise ValueError(
+            f"image {tuple(x4.shape[-2:])} is too small for {len(w)} scales with a "
+            f"{win_size}x{win_size} window; needs at least {need} px on a side")
+    win = _kernel_window(win_size, sigma, x4.device)
+    lk = _luma_k(mode, L)
+    grad = _grad_wanted(x4, y4)
+    if lk is not None and (grad or len(w) > 1):
+        x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
+        lk = None
+    n, c = x4.shape[0], x4.shape[1]
+    cx, cy = x4, y4
+    terms = []
+    for i in range(len(w)):
+        if i:
+            cx = F.avg_pool2d(cx.to(torch.float32), 2)
+            cy = F.avg_pool2d(cy.to(torch.float32), 2)
+        if grad:
+            xf = cx.to(torch.float32).contiguous()
+            yf = cy.to(torch.float32).contiguous()
+            s, cs = _FusedSSIMCS.apply(xf, yf, win, shift, C1, C2)
+        else:
+            res = backend.ssim_forward(cx.detach(), cy.detach(), win, shift=shift, C1=C1,
+                                       C2=C2, luma=lk, want_cs=True)
+            s, cs = res["plane_s"], res["plane_cs"]
+        terms.append((s if i == len(w) - 1 else cs).view(n, -1))
+    stacked = torch.stack(terms).clamp_min(0.0)
+    per_plane = stacked.pow(_ms_weights(w, x4.device)).prod(dim=0)
+    per_image = per_plane.mean(dim=1)
+    return per_image if reduction == "none" else per_image.mean()
+
+
+# --------------------------------------------------------------------------- #
+# GMSD / GMS
+# --------------------------------------------------------------------------- #
+
+def _gmsd_common(x, y, data_range, T, eps, downsample, luma, crop_border, reduction,
+                 return_map, backend_hint):
+    _check_reduction(reduction)
+    _check_hint(backend_hint)
+    x4, y4, L, mode = _prep(x, y, luma, crop_border, data_range)
+    backend.require_cuda(x4)
+    Tv = float(T) if T is not None else 170.0 * (L / 255.0) ** 2
+    ev = float(eps) if eps is not None else (1e-6 * L) ** 2
+    lk = _luma_k(mode, L)
+    if return_map:
+        q = backend.gms_map(x4, y4, T=Tv, eps=ev, downsample=downsample, luma=lk)
+        return q, None
+    if _grad_wanted(x4, y4):
+        raise NotImplementedError("GMS/GMSD gradients are not implemented yet")
+    hd = x4.shape[-2] // 2 if downsample else x4.shape[-2]
+    wd = x4.shape[-1] // 2 if downsample else x4.shape[-1]
+    if hd < 3 or wd < 3:
+        raise ValueError(f"image {hd}x{wd} is smaller than the 3x3 Prewitt window")
+    return None, backend.gmsd(x4.detach(), y4.detach(), T=Tv, eps=ev,
+                              downsample=downsample, luma=lk)
+
+
+def gms(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
+        T: Optional[float] = None, eps: Optional[float] = None, downsample: bool = True,
+        reduction: str = "mean", return_map: bool = False,
+        dtype: Optional[torch.dtype] = None, luma=None, crop_border: int = 0,
+        backend_hint: str = "auto") -> torch.Tensor:
+    """Mean gradient-magnitude similarity (functional.py:1016-1038)."""
+    q, stats = _gmsd_common(x, y, data_range, T, eps, downsample, luma, crop_border,
+                            reduction, return_map, backend_hint)
+    if q is not None:
+        return q
+    return stats[0] if reduction == "none" else stats[0].mean()
+
+
+def gmsd(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
+         T: Optional[float] = None, eps: Optional[float] = None, downsample: bool = True,
+         reduction: str = "mean", return_map: bool = False,
+         dtype: Optional[torch.dtype] = None, luma=None, crop_border: int = 0,
+         backend_hint: str = "auto") -> torch.Tensor:
+    """Gradient magnitude similarity deviation (functional.py:1041-1082):
+    population std of the GMS map, pooled over every channel of an image."""
+    q, stats = _gmsd_common(x, y, data_range, T, eps, downsample, luma, crop_border,
+                            reduction, return_map, backend_hint)
+    if q is not None:
+        return q
+    return stats[1] if reduction == "none" else stats[1].mean()

@@ -1,0 +1,272 @@
+/*
+ * frame_analytics_b200 -- C ABI of the B200 (sm_100a) full-reference metric kernels.
+ *
+ * Two blocks of entry points live in libfa_b200.so:
+ *
+ *  1. `fa_cuda_*`: drop-in replacements for every CUDA entry point the
+ *     reference binds through ctypes (frame_analytics/csrc/fa_abi.h:118-200,
+ *     prototypes in frame_analytics/_cabi.py:414-462).  Same names, same
+ *     argument meaning, same status codes, so the reference's own loader can
+ *     bind this library in place of its libfa_cuda.  Scratch arguments the
+ *     reference needs (`partial`, `aux`) are accepted; `aux` is unused because
+ *     the backward here recomputes the moments instead of staging them.
+ *
+ *  2. `fa_b200_*`: the extended boundary the Python layer in this package
+ *     uses.  Inputs are strided views (crop_border needs no copy), luma is
+ *     folded into the loads, finalisation happens inside the reduction launch,
+ *     integer sums come back as exact uint64, and the backward has no
+ *     frame-sized temporaries.
+ *
+ * Conventions (kept from the reference, fa_abi.h:12-21):
+ *   - every entry point returns an int: 0 = ok, 1..7 = library codes below,
+ *     negative = -(cudaError_t);
+ *   - the caller owns every buffer, scratch included; nothing here calls
+ *     cudaMalloc/cudaFree and nothing synchronises the host;
+ *   - `device` is an explicit ordinal (set and restored around the launch),
+ *     `stream` is a cudaStream_t passed as void*;
+ *   - launches are asynchronous on `stream`.
+ *
+ * Scratch ("workspace") of the fa_b200_* calls: a byte buffer whose size the
+ * matching *_workspace_bytes query returns.  Its first 256 bytes hold the
+ * grid-completion counters the single-launch finalisers use; they must be
+ * zero when the call starts, and every call leaves them zero again, so a
+ * workspace zeroed once can be reused by any number of calls issued in order
+ * on one stream.  Two calls that may run concurrently need two workspaces.
+ */
+#ifndef FA_B200_H
+#define FA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define FA_B200_API __declspec(dllexport)
+#else
+#define FA_B200_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same value as the reference's FA_ABI_VERSION (fa_abi.h:41): the fa_cuda_*
+ * block below keeps that ABI. */
+#define FA_ABI_VERSION 1
+/* Version of the fa_b200_* block. */
+#define FA_B200_ABI_VERSION 1
+
+/* dtype codes (fa_abi.h:43-48) */
+#define FA_U8 0
+#define FA_F16 1
+#define FA_BF16 2
+#define FA_F32 3
+#define FA_F64 4
+
+/* pixel-loss selector (fa_abi.h:50-54) */
+#define FA_OP_MSE 0
+#define FA_OP_L1 1
+#define FA_OP_CHARB 2 /* param = eps^2 */
+#define FA_OP_HUBER 3 /* param = delta */
+
+/* status codes (fa_abi.h:56-64); negative returns are -(cudaError_t) */
+#define FA_OK 0
+#define FA_E_DTYPE 1
+#define FA_E_SHAPE 2
+#define FA_E_WINDOW 3
+#define FA_E_OP 4
+#define FA_E_ARG 5
+#define FA_E_INTERNAL 6
+#define FA_E_NOCUDA 7
+
+/* "not an MSE reduction, skip the dB conversion" (fa_abi.h:67) */
+#define FA_PSNR_NONE (-1.0e300)
+
+/* largest Gaussian window; odd widths 3..11 are instantiated (fa_abi.h:71) */
+#define FA_MAX_WIN 11
+
+/* ======================================================================= */
+/* 1. reference-compatible block                                            */
+/* ======================================================================= */
+
+/* replaces fa_cuda_abi_version, fa_abi.h:118 */
+FA_B200_API int fa_cuda_abi_version(void);
+/* replaces fa_cuda_error_string, fa_abi.h:119 */
+FA_B200_API const char* fa_cuda_error_string(int code);
+/* replaces fa_cuda_device_count, fa_abi.h:120 */
+FA_B200_API int fa_cuda_device_count(int* out_count);
+
+/* replaces fa_cuda_pixel_workspace, fa_abi.h:122-123.
+ * out_bpi: columns of the [n_images, bpi] float64 `partial` scratch. */
+FA_B200_API int fa_cuda_pixel_workspace(int64_t n_images, int64_t n_per_image,
+                                        int device, int* out_bpi);
+
+/* replaces fa_cuda_pixel_reduce, fa_abi.h:127-134.  Contiguous images. */
+FA_B200_API int fa_cuda_pixel_reduce(const void* a, const void* b, int dtype,
+                                     int64_t n_images, int64_t n_per_image,
+                                     int op, double param, double psnr_bias,
+                                     double* partial, int bpi,
+                                     double* out_per_image, double* out_total,
+                                     double* out_psnr_per_image,
+                                     double* out_psnr_total, int device,
+                                     void* stream);
+
+/* replaces fa_cuda_ssim_workspace, fa_abi.h:136 */
+FA_B200_API int fa_cuda_ssim_workspace(int H, int W, int K, int* out_bpp);
+
+/* replaces fa_cuda_ssim, fa_abi.h:139-146.  partial: [N*C, bpp] float64. */
+FA_B200_API int fa_cuda_ssim(const void* x, const void* y, int dtype, int N,
+                             int C, int H, int W, const float* win, int K,
+                             double shift, double C1, double C2,
+                             float* map_out, double* partial, int bpp,
+                             double* out_per_image, double* out_total,
+                             int device, void* stream);
+
+/* replaces fa_cuda_ssim_cs, fa_abi.h:149-155.  out_s/out_cs: N*C plane means. */
+FA_B200_API int fa_cuda_ssim_cs(const void* x, const void* y, int dtype, int N,
+                                int C, int H, int W, const float* win, int K,
+                                double shift, double C1, double C2,
+                                double* partial, double* partial_cs, int bpp,
+                                double* out_s, double* out_cs, int device,
+                                void* stream);
+
+/* replaces fa_cuda_ssim_backward, fa_abi.h:161-168.  `aux` is accepted and
+ * ignored (may be null): the fused backward keeps no frame-sized scratch. */
+FA_B200_API int fa_cuda_ssim_backward(const float* x, const float* y,
+                                      const float* dL_dmap,
+                                      const float* grad_scalar,
+                                      const float* win, int K, int N, int C,
+                                      int H, int W, double shift, double C1,
+                                      double C2, float* aux, float* dx,
+                                      float* dy, int device, void* stream);
+
+/* replaces fa_cuda_ssim_cs_backward, fa_abi.h:171-177.  `aux` ignored. */
+FA_B200_API int fa_cuda_ssim_cs_backward(const float* x, const float* y,
+                                         const float* gs, const float* gcs,
+                                         const float* win, int K, int N,
+                                         int C, int H, int W, double shift,
+                                         double C1, double C2, float* aux,
+                                         float* dx, float* dy, int device,
+                                         void* stream);
+
+/* replaces fa_cuda_gmsd_workspace, fa_abi.h:179 */
+FA_B200_API int fa_cuda_gmsd_workspace(int H, int W, int downsample,
+                                       int* out_bpp);
+
+/* replaces fa_cuda_gmsd, fa_abi.h:182-187 */
+FA_B200_API int fa_cuda_gmsd(const void* x, const void* y, int dtype, int N,
+                             int C, int H, int W, double Tc, double eps,
+                             int downsample, double* psum, double* psumsq,
+                             int bpp, double* out_mean, double* out_std,
+                             int device, void* stream);
+
+/* ======================================================================= */
+/* 2. extended block                                                        */
+/* ======================================================================= */
+
+/* A batch of images as a strided 4-D view (N, C, H, W).  Strides are in
+ * elements; the W stride is 1.  `data` points at element (0,0,0,0). */
+typedef struct fa_view {
+  const void* data;
+  int32_t dtype;
+  int32_t n, c, h, w;
+  int32_t pad_;
+  int64_t stride_n, stride_c, stride_h;
+} fa_view;
+
+/* Luma projection folded into the loads: Y = k[0]*R + k[1]*G + k[2]*B + k[3]
+ * (k[3] is the offset already multiplied by the data range).  Pass NULL for
+ * "no luma"; with luma the view must have c == 3 and the metric sees one
+ * channel.  Mirrors functional.rgb_to_luma (functional.py:213-237). */
+
+FA_B200_API int fa_b200_abi_version(void);
+
+/* Bytes of workspace fa_b200_pixel_reduce needs for `n_images` images. */
+FA_B200_API int fa_b200_pixel_workspace_bytes(int n_images, int device,
+                                              size_t* out_bytes);
+
+/* One-launch pixel reduction (MSE / L1 / Charbonnier / Huber), PSNR on top.
+ * Replaces the pair fa_cuda_pixel_reduce + finalize (fa_cuda.cu:1078-1156)
+ * and the torch luma materialisation (functional.py:267-271).
+ *   out_per_image[n], out_total[0]       : means (nullable)
+ *   out_psnr_per_image[n], out_psnr_total: dB, when psnr_bias != FA_PSNR_NONE
+ *   out_isum_per_image[n]                : exact integer sums (uint8 MSE/L1
+ *                                          without luma only; else ignored) */
+FA_B200_API int fa_b200_pixel_reduce(const fa_view* a, const fa_view* b,
+                                     const double* luma, int op, double param,
+                                     double psnr_bias, void* workspace,
+                                     size_t workspace_bytes,
+                                     double* out_per_image, double* out_total,
+                                     double* out_psnr_per_image,
+                                     double* out_psnr_total,
+                                     uint64_t* out_isum_per_image, int device,
+                                     void* stream);
+
+/* Bytes of workspace fa_b200_ssim needs. */
+FA_B200_API int fa_b200_ssim_workspace_bytes(int n, int c, int h, int w, int K,
+                                             int device, size_t* out_bytes);
+
+/* Fused SSIM forward in one launch.  Replaces fa_cuda_ssim / fa_cuda_ssim_cs
+ * + finalize (fa_cuda.cu:1167-1283).  All outputs nullable:
+ *   map_out          [N, C', Hout, Wout] float32 SSIM map
+ *   out_plane_s/cs   [N*C'] per-plane means of SSIM and of its cs factor
+ *   out_per_image    [N] mean over C' planes; out_total: batch mean
+ * (C' = 1 with luma, else C). */
+FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y,
+                             const double* luma, const float* win, int K,
+                             double shift, double C1, double C2,
+                             float* map_out, void* workspace,
+                             size_t workspace_bytes, double* out_plane_s,
+                             double* out_plane_cs, double* out_per_image,
+                             double* out_total, int device, void* stream);
+
+/* Fused SSIM backward, one launch, no scratch.  Replaces fa_cuda_ssim_backward
+ * and fa_cuda_ssim_cs_backward (fa_cuda.cu:1299-1414, backend.py:429-455).
+ * Upstream gradient, exactly one form:
+ *   dL_dmap   [N, C, Hout, Wout]  : per map position
+ *   g_scalar  [1] (device)        : d loss / d (batch-mean SSIM); scaled by
+ *                                   1/(N*C*Hout*Wout) inside
+ *   gs, gcs   [N*C] (device)      : d loss / d (plane-mean SSIM) and
+ *                                   d loss / d (plane-mean cs) (MS-SSIM)
+ * x, y: float32 contiguous [N, C, H, W].  dx / dy nullable (not both). */
+FA_B200_API int fa_b200_ssim_backward(const float* x, const float* y, int N,
+                                      int C, int H, int W, const float* win,
+                                      int K, double shift, double C1,
+                                      double C2, const float* dL_dmap,
+                                      const float* g_scalar, const float* gs,
+                                      const float* gcs, float* dx, float* dy,
+                                      int device, void* stream);
+
+/* Bytes of workspace fa_b200_gmsd needs. */
+FA_B200_API int fa_b200_gmsd_workspace_bytes(int n, int c, int h, int w,
+                                             int downsample, int device,
+                                             size_t* out_bytes);
+
+/* Fused GMSD in one launch: optional 2x2 mean pool, Prewitt/3, GMS map, per
+ * image mean and population std pooled over all channels.  Replaces
+ * fa_cuda_gmsd + gmsd_finalize (fa_cuda.cu:926-1026, 1426-1466) and, with
+ * map_out, the portable GMS map of functional._gms_map (functional.py:925-947).
+ *   map_out [N, C', Hout, Wout] float32 (nullable); out_mean (GMS) / out_std
+ *   (GMSD): [N] float64. */
+FA_B200_API int fa_b200_gmsd(const fa_view* x, const fa_view* y,
+                             const double* luma, double T, double eps,
+                             int downsample, void* workspace,
+                             size_t workspace_bytes, float* map_out,
+                             double* out_mean, double* out_std, int device,
+                             void* stream);
+
+/* Gradient of a pixel reduction (mse / l1 / charbonnier / huber) w.r.t. its
+ * inputs.  Replaces the torch autograd the reference uses for these
+ * (functional.py:1097-1141).  x, y: float32 contiguous [N, C, H, W];
+ * g: device float64, [N] when per_image else [1] (d loss / d output);
+ * luma as for fa_b200_pixel_reduce.  dx / dy nullable (not both). */
+FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N,
+                                       int C, int H, int W, const double* luma,
+                                       int op, double param, const double* g,
+                                       int per_image, float* dx, float* dy,
+                                       int device, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* FA_B200_H */

@@ -1,0 +1,65 @@
+"""GMSD / GMS on the GPU against the reference's goldens and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import fa_oracle as O
+from conftest import baseline_pair
+
+import frame_analytics_b200 as fa
+
+pytestmark = pytest.mark.gpu
+EPS_G = (1e-6 * 255.0) ** 2
+
+
+def T(a, dt=torch.uint8):
+    return torch.as_tensor(np.asarray(a), dtype=dt, device="cuda")
+
+
+@pytest.mark.parametrize("k", ["v0", "v1", "v2", "v3", "m0", "m1", "m2"])
+@pytest.mark.parametrize("dt", [torch.uint8, torch.float32])
+def test_gmsd_matches_golden(golden, k, dt):
+    a, b = T(golden[f"{k}_a"], dt), T(golden[f"{k}_b"], dt)
+    assert abs(float(fa.gmsd(a, b, data_range=255.0)) - float(golden[f"{k}_gmsd"])) < 5e-6
+    if f"{k}_gmsd_nodown" in golden:
+        got = float(fa.gmsd(a, b, data_range=255.0, downsample=False))
+        assert abs(got - float(golden[f"{k}_gmsd_nodown"])) < 5e-6
+
+
+@pytest.mark.parametrize("down", [1, 0])
+def test_multichannel_pooling(golden, down):
+    a, b = T(golden["gm3_a"]), T(golden["gm3_b"])
+    m = fa.gms(a, b, downsample=bool(down), reduction="none").cpu().numpy()
+    s = fa.gmsd(a, b, downsample=bool(down), reduction="none").cpu().numpy()
+    np.testing.assert_allclose(m, golden[f"gm3_cpu_mean_d{down}"], atol=1e-6)
+    np.testing.assert_allclose(s, golden[f"gm3_cpu_std_d{down}"], atol=1e-6)
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 6, 6), (1, 1, 7, 1031), (2, 3, 1031, 9),
+                                   (1, 2, 517, 1029), (3, 1, 64, 1024)])
+@pytest.mark.parametrize("down", [True, False])
+def test_shapes_vs_oracle(shape, down):
+    a, b = baseline_pair(shape, 13.0, seed=shape[-1])
+    m, s = O.gmsd(a, b, downsample=down, eps=EPS_G)
+    np.testing.assert_allclose(fa.gms(T(a), T(b), downsample=down, reduction="none").cpu().numpy(), m, atol=1e-6)
+    np.testing.assert_allclose(fa.gmsd(T(a), T(b), downsample=down, reduction="none").cpu().numpy(), s, atol=5e-6)
+
+
+def test_map_and_identity():
+    a, b = baseline_pair((2, 3, 50, 61), 8.0, seed=3)
+    q = fa.gms(T(a), T(b), return_map=True)
+    assert tuple(q.shape) == (2, 3, 23, 28)
+    np.testing.assert_allclose(q.double().cpu().numpy(), O.gms_map(a, b), atol=1e-6)
+    x = T(a)
+    assert float(fa.gmsd(x, x)) < 1e-6
+    assert abs(float(fa.gms(x, x)) - 1.0) < 1e-7
+
+
+def test_luma_and_crop():
+    a, b = baseline_pair((2, 3, 90, 70), 10.0, seed=6)
+    m, s = O.gmsd(a, b, luma="bt709", crop_border=3, eps=EPS_G)
+    np.testing.assert_allclose(fa.gmsd(T(a), T(b), luma="bt709", crop_border=3,
+                                       reduction="none").cpu().numpy(), s, atol=5e-6)
