@@ -36,7 +36,7 @@ import numpy as np
 import torch
 
 REPO = Path(__file__).resolve().parent
-SHAPE = (8, 3, 1080, 1920)          # config 2 per GPU
+SHAPE = (8, 3, 1080, 1920)          # config 2 per GPU (--images overrides N)
 PIX_SHAPE = (8, 3, 1080, 1920)      # config 1
 FALLBACK_HBM_GBS = 6650.0
 
@@ -261,6 +261,18 @@ def flush_l2(buf: torch.Tensor):
     buf.add_(1)
 
 
+def timed_call(fn, ev):
+    """Device time of fn()'s launches alone: the stream is held by a short
+    sleep kernel while the host enqueues them, so no host latency is timed."""
+    s0, s1 = ev(), ev()
+    torch.cuda._sleep(2_000_000)
+    s0.record()
+    fn()
+    s1.record()
+    torch.cuda.synchronize()
+    return s0.elapsed_time(s1)
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -338,7 +350,7 @@ def run_ours(args):
         traffic = json.loads(tf.read_text()).get(dom_name)
 
     # e2e through the public API from pinned host memory
-    e2e_steps = max(3, args.steps // 2)
+    e2e_steps = 0 if args.no_extra else max(3, args.steps // 2)
     loss_h = torch.empty(1, dtype=torch.float64).pin_memory()
 
     def e2e_step():
@@ -347,24 +359,26 @@ def run_ours(args):
         loss, _ = step(x, y)
         loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = ev(), ev()
-    e0.record()
-    for _ in range(e2e_steps):
+    e2e_value = None
+    if e2e_steps:
         e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = px_step * e2e_steps * world / (float(e_ms) / 1e3) / 1e9
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e_value = px_step * e2e_steps * world / (float(e_ms) / 1e3) / 1e9
 
     # extra legs (rank-local, reported by rank 0): uint8 PSNR and SSIM forward
     extra = {}
-    if rank == 0:
+    if rank == 0 and not args.no_extra:
         ua, ub = u8_pair(PIX_SHAPE, 5.0, 0)
         xu, yu = torch.from_numpy(ua).to(dev), torch.from_numpy(ub).to(dev)
         flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
@@ -373,12 +387,7 @@ def run_ours(args):
         ts = []
         for _ in range(max(10, args.steps)):
             flush_l2(flush)
-            s0, s1 = ev(), ev()
-            s0.record()
-            fa.psnr(xu, yu)
-            s1.record()
-            torch.cuda.synchronize()
-            ts.append(s0.elapsed_time(s1))
+            ts.append(timed_call(lambda: fa.psnr(xu, yu), ev))
         pm = statistics.median(ts)
         pbytes = 2 * int(np.prod(PIX_SHAPE))
         extra["psnr_u8"] = {"workload": "cfg1 PSNR uint8 8x3x1080x1920, L2 flushed",
@@ -389,19 +398,14 @@ def run_ours(args):
         ts = []
         for _ in range(max(5, args.steps // 2)):
             flush_l2(flush)
-            s0, s1 = ev(), ev()
-            s0.record()
-            fa.ssim(xu, yu)
-            s1.record()
-            torch.cuda.synchronize()
-            ts.append(s0.elapsed_time(s1))
+            ts.append(timed_call(lambda: fa.ssim(xu, yu), ev))
         sm = statistics.median(ts)
         extra["ssim_u8_fwd"] = {"workload": "SSIM fwd uint8 8x3x1080x1920, L2 flushed",
                                 "ms": sm, "Gpixel/s": int(np.prod(PIX_SHAPE)) / (sm / 1e3) / 1e9,
                                 "GB/s": pbytes / (sm / 1e3) / 1e9}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and not args.no_extra:
         gp, dt, thr = cpu_fwd_bwd_sample(1)
         cpu = {"value": gp, "unit": "Gpixel/s", "cores": thr, "kind": "port",
                "sample": f"1 config-2 image (3x1080x1920 fp32) SSIM fwd+bwd, C port "
@@ -450,7 +454,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="time only the headline step (profiling runs)")
+    ap.add_argument("--images", type=int, default=8,
+                    help="images per GPU (8 = config 2; smaller for ncu captures)")
     args = ap.parse_args()
+    global SHAPE
+    SHAPE = (args.images,) + SHAPE[1:]
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -492,10 +492,10 @@ static constexpr size_t bwd_smem() {
          sizeof(float) * 2 * KW * Geo<KW>::SW;
 }
 
-// cudaFuncSetAttribute once per (kernel, device)
+// cudaFuncSetAttribute once per (kernel, device): `done` must belong to one
+// kernel, so each launch_* instantiation passes its own flag array.
 template <typename K>
-static cudaError_t ensure_smem(K* kern, size_t bytes, int device) {
-  static bool done[64] = {false};
+static cudaError_t ensure_smem(K* kern, size_t bytes, int device, bool (&done)[64]) {
   if (device >= 0 && device < 64 && done[device]) return cudaSuccess;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)bytes);
@@ -533,7 +533,8 @@ template <typename T, int KW, int FLAGS, bool LUMA>
 static int launch_fwd(SsimArgs& p, int device, cudaStream_t st) {
   auto kern = ssim_fwd_kernel<T, KW, FLAGS, LUMA>;
   const size_t sm = fwd_smem<KW>();
-  FAB_TRY(ensure_smem(kern, sm, device));
+  static bool done[64] = {false};
+  FAB_TRY(ensure_smem(kern, sm, device, done));
   dim3 grid(p.strips, p.chunks, p.P);
   kern<<<grid, 32 * KW, sm, st>>>(p);
   FAB_LAUNCH_CHECK();
@@ -620,7 +621,8 @@ template <int KW, bool DX, bool DY, int GMODE>
 static int launch_bwd(SsimArgs& p, int device, cudaStream_t st) {
   auto kern = ssim_bwd_kernel<KW, DX, DY, GMODE>;
   const size_t sm = bwd_smem<KW>();
-  FAB_TRY(ensure_smem(kern, sm, device));
+  static bool done[64] = {false};
+  FAB_TRY(ensure_smem(kern, sm, device, done));
   dim3 grid(p.strips, p.chunks, p.P);
   kern<<<grid, 32 * KW, sm, st>>>(p);
   FAB_LAUNCH_CHECK();
