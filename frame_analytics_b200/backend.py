@@ -202,18 +202,47 @@ def pixel(x: torch.Tensor, y: torch.Tensor, *, op: int, param: float = 0.0,
 # SSIM
 # --------------------------------------------------------------------------- #
 
-def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
+class Taps:
+    """The 1-D Gaussian window as host float32 taps: the kernels take them by
+    value in their launch parameters, so no device window is read."""
+
+    __slots__ = ("k", "arr", "values")
+
+    def __init__(self, values):
+        self.values = tuple(float(v) for v in values)
+        self.k = len(self.values)
+        self.arr = (ctypes.c_float * self.k)(*self.values)
+
+
+_taps_cache: dict = {}
+
+
+def host_taps(win_size: int, sigma: float) -> Taps:
+    """Same numbers as functional.gaussian_window_1d(..., dtype=float32):
+    float64 Gaussian, sum-normalised, rounded to float32 (functional.py:397-420)."""
+    key = (int(win_size), float(sigma))
+    t = _taps_cache.get(key)
+    if t is None:
+        r = (win_size - 1) / 2.0
+        c = torch.arange(win_size, dtype=torch.float64) - r
+        g = torch.exp(-(c * c) / (2.0 * sigma * sigma))
+        g = (g / g.sum()).to(torch.float32)
+        t = Taps(g.tolist())
+        _taps_cache[key] = t
+    return t
+
+def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                  shift: float, C1: float, C2: float, luma=None,
                  want_map: bool = False, want_plane: bool = False,
                  want_cs: bool = False, want_per_image: bool = False,
                  want_total: bool = False) -> dict:
-    """Fused SSIM forward, one launch.  ``win`` is the float32 1-D window on
-    the device.  Returns a dict with the requested outputs."""
+    """Fused SSIM forward, one launch.  ``win`` holds the window taps.
+    Returns a dict with the requested outputs."""
     L = lib()
     x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
     vx, x = as_view(x)
     vy, y = as_view(y)
-    k = int(win.numel())
+    k = win.k
     cm = 1 if luma is not None else vx.c
     hout, wout = vx.h - k + 1, vx.w - k + 1
     if hout <= 0 or wout <= 0:
@@ -229,13 +258,13 @@ def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
     res["per_image"] = _f64(x, vx.n) if want_per_image else None
     res["total"] = _f64(x) if want_total else None
     _call(x, L.fa_b200_ssim, ctypes.byref(vx), ctypes.byref(vy), _luma_arg(luma),
-          win.data_ptr(), k, float(shift), float(C1), float(C2), _ptr(res["map"]),
+          win.arr, k, float(shift), float(C1), float(C2), _ptr(res["map"]),
           ws.data_ptr(), ws.numel(), _ptr(res["plane_s"]), _ptr(res["plane_cs"]),
           _ptr(res["per_image"]), _ptr(res["total"]), dev, _stream(x))
     return res
 
 
-def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
+def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                   shift: float, C1: float, C2: float,
                   dmap: Optional[torch.Tensor] = None,
                   gscalar: Optional[torch.Tensor] = None,
@@ -247,7 +276,7 @@ def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
     x = x.detach().to(torch.float32).contiguous()
     y = y.detach().to(torch.float32).contiguous()
     n, c, h, w = x.shape
-    k = int(win.numel())
+    k = win.k
     dx = torch.empty_like(x) if need_dx else None
     dy = torch.empty_like(y) if need_dy else None
     if dmap is not None:
@@ -258,7 +287,7 @@ def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: torch.Tensor, *,
         gs = gs.to(torch.float32).reshape(-1).contiguous()
         gcs = gcs.to(torch.float32).reshape(-1).contiguous()
     _call(x, L.fa_b200_ssim_backward, x.data_ptr(), y.data_ptr(), n, c, h, w,
-          win.data_ptr(), k, float(shift), float(C1), float(C2), _ptr(dmap),
+          win.arr, k, float(shift), float(C1), float(C2), _ptr(dmap),
           _ptr(gscalar), _ptr(gs), _ptr(gcs), _ptr(dx), _ptr(dy), _dev(x), _stream(x))
     return dx, dy
 

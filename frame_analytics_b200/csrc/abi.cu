@@ -4,6 +4,10 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
+#include <array>
 
 namespace fab {
 
@@ -57,6 +61,34 @@ static View contiguous_view(const void* p, int n, int c, int h, int w) {
 
 static bool view_ok(const fa_view* v) {
   return v && v->data && v->w > 0 && v->h > 0 && v->c > 0 && v->n > 0;
+}
+
+
+// The reference-compatible SSIM entry points receive the window as a device
+// pointer, while the kernels take their taps by value.  The taps are read
+// once per (device, pointer, size) with a blocking 44-byte copy and cached;
+// the reference caches its windows for the life of the process
+// (functional.py:397-420), so in practice this happens once.  That first
+// read synchronises, so make the first call outside any stream capture.
+static int host_taps(const float* win_dev, int K, int device, float* out) {
+  static std::mutex mu;
+  static std::map<std::pair<std::pair<int, uintptr_t>, int>, std::array<float, 12>> cache;
+  if (K < 1 || K > 12) return FA_E_WINDOW;
+  const auto key = std::make_pair(std::make_pair(device, reinterpret_cast<uintptr_t>(win_dev)), K);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      for (int j = 0; j < K; ++j) out[j] = it->second[j];
+      return FA_OK;
+    }
+  }
+  std::array<float, 12> t{};
+  FAB_TRY(cudaMemcpy(t.data(), win_dev, sizeof(float) * K, cudaMemcpyDeviceToHost));
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = t;
+  for (int j = 0; j < K; ++j) out[j] = t[j];
+  return FA_OK;
 }
 
 }  // namespace fab
@@ -148,9 +180,12 @@ FA_B200_API int fa_cuda_ssim(const void* x, const void* y, int dtype, int N, int
   if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
   FAB_DEVICE_SCOPE(device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float taps[12];
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
   FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
   View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
-  return ssim_fwd_impl(vx, vy, dtype, nullptr, win, K, shift, C1, C2, map_out, partial,
+  return ssim_fwd_impl(vx, vy, dtype, nullptr, taps, K, shift, C1, C2, map_out, partial,
                        (size_t)N * C * bpp * 8, nullptr, nullptr, out_per_image, out_total,
                        device, st);
 }
@@ -163,9 +198,12 @@ FA_B200_API int fa_cuda_ssim_cs(const void* x, const void* y, int dtype, int N, 
   if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
   FAB_DEVICE_SCOPE(device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float taps[12];
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
   FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
   View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
-  return ssim_fwd_impl(vx, vy, dtype, nullptr, win, K, shift, C1, C2, nullptr, partial,
+  return ssim_fwd_impl(vx, vy, dtype, nullptr, taps, K, shift, C1, C2, nullptr, partial,
                        (size_t)N * C * bpp * 8, out_s, out_cs, nullptr, nullptr, device, st);
 }
 
@@ -176,8 +214,12 @@ FA_B200_API int fa_cuda_ssim_backward(const float* x, const float* y, const floa
                                       void* stream) {
   (void)aux;
   if (dL_dmap && grad_scalar) grad_scalar = nullptr;  // the map wins, as in the reference
+  if (!win) return FA_E_ARG;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
   FAB_DEVICE_SCOPE(device);
-  return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, dL_dmap, grad_scalar, nullptr,
+  float taps[12];
+  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
+  return ssim_bwd_impl(x, y, N, C, H, W, taps, K, shift, C1, C2, dL_dmap, grad_scalar, nullptr,
                        nullptr, dx, dy, device, static_cast<cudaStream_t>(stream));
 }
 
@@ -187,9 +229,12 @@ FA_B200_API int fa_cuda_ssim_cs_backward(const float* x, const float* y, const f
                                          float* aux, float* dx, float* dy, int device,
                                          void* stream) {
   (void)aux;
-  if (!gs || !gcs) return FA_E_ARG;
+  if (!gs || !gcs || !win) return FA_E_ARG;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
   FAB_DEVICE_SCOPE(device);
-  return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, nullptr, nullptr, gs, gcs, dx,
+  float taps[12];
+  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
+  return ssim_bwd_impl(x, y, N, C, H, W, taps, K, shift, C1, C2, nullptr, nullptr, gs, gcs, dx,
                        dy, device, static_cast<cudaStream_t>(stream));
 }
 

@@ -1,0 +1,249 @@
+// Fused SSIM backward on sm_100a: one launch, no frame-sized scratch.
+//
+// Replaces the reference's two-kernel backward (MODE_PREP / MODE_PREP_CS of
+// ssim_fused_kernel, fa_cuda.cu:551-607, writing 3-4 coefficient planes to
+// global memory, then ssim_bwd_scatter_kernel, fa_cuda.cu:655-784, reading
+// them back).  For an output position o with upstream gradient g:
+//   b = g dS/dsxx, c = g dS/dsxy, t_x = g dS/dmx - 2 b ux - c uy
+//   (MS-SSIM: b = -(gS S + gCS cs)/B2, c = 2 (gS A1/B1 + gCS)/B2)
+//   dx(i) = 2 x'(i) (w*b)(i) + y'(i) (w*c)(i) + (w*t_x)(i)     (w* transposed)
+// and symmetrically for dy.  Here one block streams a strip of rows through
+// moments -> coefficients (shared memory) -> transposed blur -> dx/dy, so the
+// coefficients never leave the SM.  A strip of 32*KW moment columns yields
+// 32*KW - (KW-1) gradient columns.
+#include "ssim_common.cuh"
+
+namespace fab {
+
+constexpr int G_MAP = 0;     // dL/dmap per position
+constexpr int G_SCALAR = 1;  // dL/d(batch mean), one device scalar
+constexpr int G_PLANE = 2;   // dL/d(plane-mean S) and dL/d(plane-mean cs)
+
+template <int KW>
+struct BwdGeo {
+  using G = Geo<KW>;
+  static constexpr int SCW = G::NT + KW - 1;  // coefficient row width (zero padded)
+  static constexpr size_t kH = sizeof(float4) * KW * G::NT;
+  static constexpr size_t kC = sizeof(float4) * KW * SCW;
+  static constexpr size_t kX = sizeof(float) * 2 * KW * G::SW;
+  static constexpr size_t kD = sizeof(float) * 2 * KW * G::TD;
+  static constexpr size_t kBytes = kH + kC + kX + kD;
+};
+
+template <int KW, bool DX, bool DY, int GMODE>
+__global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_constant__ SsimArgs p) {
+  using G = Geo<KW>;
+  using B = BwdGeo<KW>;
+  constexpr int NPL = (DX && DY) ? 4 : 3;
+  extern __shared__ float4 smem4[];
+  float4* sH = smem4;                                 // [KW][NT] moments, then scatter rows
+  float4* sC = sH + KW * G::NT;                       // [KW][SCW] coefficients
+  float* sX = reinterpret_cast<float*>(sC + KW * B::SCW);  // [KW][SW] staged inputs
+  float* sY = sX + KW * G::SW;
+  float* dX = sY + KW * G::SW;                        // [KW][TD] x at the gradient rows
+  float* dY = dX + KW * G::TD;
+
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const int plane = blockIdx.z;
+  const long long pbase = (long long)plane * p.H * p.W;
+  const int c0 = blockIdx.x * G::TD;      // first gradient column of the strip
+  const int mc0 = c0 - (KW - 1);          // first moment column
+  const int r0 = blockIdx.y * p.RH;       // first gradient row of the chunk
+  const int rows = min(p.RH, p.H - r0);
+  const int i0 = r0 - (KW - 1);           // first input row
+  const int iters = (rows + 2 * (KW - 1) + KW - 1) / KW;
+  const int q = mc0 + t;                  // this thread's moment column
+  const bool q_ok = q >= 0 && q < p.Wout;
+  const int dcol = c0 + t;                // this thread's gradient column
+  const bool d_ok = t < G::TD && dcol < p.W;
+  const float* X = reinterpret_cast<const float*>(p.x) + pbase;
+  const float* Y = reinterpret_cast<const float*>(p.y) + pbase;
+
+  // zero the coefficient padding columns once
+  for (int i = t; i < KW * (B::SCW - G::NT); i += G::NT) {
+    const int r = i / (B::SCW - G::NT), c = i - r * (B::SCW - G::NT);
+    sC[r * B::SCW + G::NT + c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  float gS = 0.f, gCS = 0.f;
+  if (GMODE == G_SCALAR) gS = __ldg(p.gscalar) * p.grad_norm;
+  if (GMODE == G_PLANE) {
+    gS = __ldg(p.gs + plane) * p.grad_norm;
+    gCS = __ldg(p.gcs + plane) * p.grad_norm;
+  }
+
+  stage_async<float, KW>(p, pbase, i0, mc0, sX, sY);
+
+  float4 ring1[KW], ring2[KW];
+#pragma unroll
+  for (int k = 0; k < KW; ++k) {
+    ring1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    ring2[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  for (int m = 0; m < iters; ++m) {
+    cp_async_wait<0>();
+    stage_convert<float, KW>(p, sX, sY, sX, sY);
+    __syncthreads();
+    // the input values at this iteration's gradient rows (L2-resident)
+    for (int i = t; i < KW * G::TD; i += G::NT) {
+      const int k = i / G::TD, c = i - k * G::TD;
+      const int r = i0 + m * KW + k - (KW - 1);
+      int nb = 0;
+      long long off = 0;
+      if (r >= 0 && r < p.H && c0 + c < p.W) {
+        nb = 4;
+        off = (long long)r * p.W + c0 + c;
+      }
+      cp_async<4>(dX + i, X + off, nb);
+      cp_async<4>(dY + i, Y + off, nb);
+    }
+    cp_async_commit();
+    // horizontal moments: warp k -> staged row k
+    {
+      const float* rx = sX + warp * G::SW + lane * KW;
+      const float* ry = sY + warp * G::SW + lane * KW;
+      float4* out = sH + warp * G::NT + lane * KW;
+      hblur_xy<KW>(p, rx, ry, out);
+      hblur_prod<KW>(p, rx, ry, out);
+    }
+    __syncthreads();
+    const bool more = (m + 1 < iters);
+    if (more) stage_async<float, KW>(p, pbase, i0 + (m + 1) * KW, mc0, sX, sY);
+    // vertical moments -> coefficients
+#pragma unroll
+    for (int k = 0; k < KW; ++k) {
+      ring1[k] = sH[k * G::NT + t];
+      const int L = m * KW + k;
+      const int o = i0 + L - (KW - 1);  // moment row
+      float4 cf = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (L >= KW - 1 && o >= 0 && o < p.Hout && q_ok) {
+        const Moments mo = moments(p, vblur_at<KW, 4>(p, ring1, k));
+        const float iB1 = 1.0f / mo.B1;
+        const float iB2 = 1.0f / mo.B2;
+        const float S = mo.A1 * mo.A2 * iB1 * iB2;
+        const float kk = 2.f * mo.A2 * iB1 * iB2;
+        float g = gS, bb, cc;
+        if (GMODE == G_MAP)
+          g = __ldg(p.dmap + (long long)plane * p.Hout * p.Wout + (long long)o * p.Wout + q);
+        if (GMODE == G_PLANE) {
+          const float CS = mo.A2 * iB2;
+          bb = -(g * S + gCS * CS) * iB2;
+          cc = 2.f * (g * mo.A1 * iB1 + gCS) * iB2;
+        } else {
+          bb = -g * S * iB2;
+          cc = 2.f * g * mo.A1 * iB1 * iB2;
+        }
+        cf.x = bb;
+        cf.y = cc;
+        if (DX) cf.z = g * kk * (mo.my - mo.mx * mo.A1 * iB1) - 2.f * bb * mo.ux - cc * mo.uy;
+        if (DY) {
+          const float ty = g * kk * (mo.mx - mo.my * mo.A1 * iB1) - 2.f * bb * mo.uy - cc * mo.ux;
+          if (DX) cf.w = ty;
+          else cf.z = ty;
+        }
+      }
+      sC[k * B::SCW + t] = cf;
+    }
+    __syncthreads();
+    // horizontal scatter of the coefficient rows
+    {
+      const float4* rc = sC + warp * B::SCW + lane * KW;
+      float4* out = sH + warp * G::NT + lane * KW;
+      hblur_pair<KW, 0, 2>(p, rc, out);
+      hblur_pair<KW, 1, NPL - 2>(p, rc, out);
+    }
+    if (more) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();
+    // vertical scatter -> dx, dy
+#pragma unroll
+    for (int k = 0; k < KW; ++k) {
+      ring2[k] = sH[k * G::NT + t];
+      const int L = m * KW + k;
+      const int r = i0 + L - (KW - 1);  // gradient row
+      if (L >= 2 * (KW - 1) && r < r0 + rows && d_ok) {
+        const float4 s = vblur_at<KW, NPL>(p, ring2, k);
+        const long long off = (long long)r * p.W + dcol;
+        const float xs = dX[k * G::TD + t] - p.shift;
+        const float ys = dY[k * G::TD + t] - p.shift;
+        if (DX) p.dx[pbase + off] = fmaf(2.f * xs, s.x, fmaf(ys, s.y, s.z));
+        if (DY) p.dy[pbase + off] = fmaf(2.f * ys, s.x, fmaf(xs, s.y, (DX && DY) ? s.w : s.z));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+template <int KW, bool DX, bool DY, int GMODE>
+static int launch_bwd(const SsimArgs& p, int device, cudaStream_t st) {
+  auto kern = ssim_bwd_kernel<KW, DX, DY, GMODE>;
+  const size_t sm = BwdGeo<KW>::kBytes;
+  static bool done[64] = {false};
+  FAB_TRY(ensure_smem(kern, sm, device, done));
+  dim3 grid(p.strips, p.chunks, p.P);
+  kern<<<grid, 32 * KW, sm, st>>>(p);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+template <bool DX, bool DY, int GMODE>
+static int bwd_k(const SsimArgs& p, int K, int device, cudaStream_t st) {
+  switch (K) {
+    case 11: return launch_bwd<11, DX, DY, GMODE>(p, device, st);
+    case 9: return launch_bwd<9, DX, DY, GMODE>(p, device, st);
+    case 7: return launch_bwd<7, DX, DY, GMODE>(p, device, st);
+    case 5: return launch_bwd<5, DX, DY, GMODE>(p, device, st);
+    case 3: return launch_bwd<3, DX, DY, GMODE>(p, device, st);
+    default: return FA_E_WINDOW;
+  }
+}
+
+template <int GMODE>
+static int bwd_g(const SsimArgs& p, int K, int device, cudaStream_t st) {
+  if (p.dx && p.dy) return bwd_k<true, true, GMODE>(p, K, device, st);
+  if (p.dx) return bwd_k<true, false, GMODE>(p, K, device, st);
+  return bwd_k<false, true, GMODE>(p, K, device, st);
+}
+
+int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* taps,
+                  int K, double shift, double C1, double C2, const float* dmap,
+                  const float* gscalar, const float* gs, const float* gcs, float* dx, float* dy,
+                  int device, cudaStream_t st) {
+  if (!x || !y || !taps) return FA_E_ARG;
+  if (!dx && !dy) return FA_E_ARG;
+  const int forms = (dmap ? 1 : 0) + (gscalar ? 1 : 0) + ((gs || gcs) ? 1 : 0);
+  if (forms != 1) return FA_E_ARG;
+  if ((gs != nullptr) != (gcs != nullptr)) return FA_E_ARG;
+  if (N <= 0 || C <= 0 || H <= 0 || W <= 0) return FA_E_SHAPE;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  const int Hout = H - K + 1, Wout = W - K + 1;
+  if (Hout <= 0 || Wout <= 0) return FA_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 3u) return FA_E_ARG;
+  SsimArgs p{};
+  p.x = reinterpret_cast<const char*>(x);
+  p.y = reinterpret_cast<const char*>(y);
+  p.N = N; p.C = C; p.H = H; p.W = W;
+  p.Cm = C; p.P = N * C;
+  if (p.P > 65535) return FA_E_SHAPE;
+  p.sn = (long long)C * H * W; p.sc = (long long)H * W; p.sh = W;
+  p.Hout = Hout; p.Wout = Wout;
+  p.shift = (float)shift; p.C1 = (float)C1; p.C2 = (float)C2;
+  for (int j = 0; j < K; ++j) p.w[j] = taps[j];
+  p.dmap = dmap; p.gscalar = gscalar; p.gs = gs; p.gcs = gcs;
+  p.dx = dx; p.dy = dy;
+  const double npix = (double)Hout * Wout;
+  p.grad_norm = gscalar ? (float)(1.0 / (npix * p.P)) : (gs ? (float)(1.0 / npix) : 1.0f);
+  const int td = 32 * K - (K - 1);
+  const SsimPlan pl = plan_rows(H, (W + td - 1) / td, p.P, device, 1, 4);
+  p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
+  if (dmap) return bwd_g<G_MAP>(p, K, device, st);
+  if (gscalar) return bwd_g<G_SCALAR>(p, K, device, st);
+  return bwd_g<G_PLANE>(p, K, device, st);
+}
+
+}  // namespace fab

@@ -1,0 +1,258 @@
+// SSIM forward on sm_100a: per-plane SSIM and cs means, the SSIM map, per
+// image and batch means -- one launch.  Replaces the reference's
+// ssim_fused_kernel REDUCE/MAP/CS modes + finalize (fa_cuda.cu:389-637,
+// 182-234, host 1167-1283).  Layout notes: ssim_common.cuh.
+#include "ssim_common.cuh"
+
+namespace fab {
+
+// Last block: per-plane sums in a fixed order, then per-image and batch means.
+__device__ void ssim_fwd_finalize(const SsimArgs& p, int bpp) {
+  __shared__ double s_red[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const double npix = (double)p.Hout * (double)p.Wout;
+  for (int pl = wid; pl < p.P; pl += nw) {
+    double s = 0.0, c = 0.0;
+    for (int i = lane; i < bpp; i += 32) {
+      s += p.part_s[(long long)pl * bpp + i];
+      if (p.part_cs) c += p.part_cs[(long long)pl * bpp + i];
+    }
+    s = warp_sum(s);
+    c = warp_sum(c);
+    if (lane == 0) {
+      p.part_s[(long long)pl * bpp] = s;
+      if (p.out_plane_s) p.out_plane_s[pl] = s / npix;
+      if (p.out_plane_cs) p.out_plane_cs[pl] = c / npix;
+    }
+  }
+  __syncthreads();
+  __threadfence_block();
+  double t = 0.0;
+  for (int n = threadIdx.x; n < p.N; n += blockDim.x) {
+    double s = 0.0;
+    for (int c = 0; c < p.Cm; ++c) s += p.part_s[(long long)(n * p.Cm + c) * bpp];
+    if (p.out_per_image) p.out_per_image[n] = s / (npix * p.Cm);
+    t += s;
+  }
+  t = block_sum(t, s_red);
+  if (threadIdx.x == 0 && p.out_total) *p.out_total = t / (npix * p.Cm * (double)p.N);
+}
+
+template <typename T, int KW, bool CS, int STAGE>
+__global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_constant__ SsimArgs p) {
+  using G = Geo<KW>;
+  using R = Raw<T, KW>;
+  constexpr bool ASYNC = (STAGE == STAGE_ASYNC);
+  extern __shared__ float4 smem4[];
+  float4* sH = smem4;                                        // [KW][NT]
+  float* sX = reinterpret_cast<float*>(smem4 + KW * G::NT);  // [KW][SW]
+  float* sY = sX + KW * G::SW;
+  T* rawX = R::kInPlace ? reinterpret_cast<T*>(sX) : reinterpret_cast<T*>(sY + KW * G::SW);
+  T* rawY = R::kInPlace ? reinterpret_cast<T*>(sY) : rawX + KW * R::RPE;
+  __shared__ double s_red[32];
+  __shared__ int s_flag;
+
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const int plane = blockIdx.z;
+  const int pn = plane / p.Cm, pc = plane - pn * p.Cm;
+  const long long base = (long long)pn * p.sn + (long long)pc * p.sc;
+  const int c0 = blockIdx.x * G::NT;
+  const int r0 = blockIdx.y * p.RH;
+  const int rows = min(p.RH, p.Hout - r0);
+  const int col = c0 + t;
+  const bool col_ok = col < p.Wout;
+  const int iters = (rows + KW - 1 + KW - 1) / KW;
+  float* map = p.map_out ? p.map_out + (long long)plane * p.Hout * p.Wout : nullptr;
+
+  float vx[ASYNC ? 1 : G::NE], vy[ASYNC ? 1 : G::NE];
+  if constexpr (ASYNC) {
+    stage_async<T, KW>(p, base, r0, c0, rawX, rawY);
+  } else {
+    stage_load<T, STAGE == STAGE_LUMA, KW>(p, base, r0, c0, vx, vy);
+    stage_store<KW>(sX, sY, vx, vy);
+  }
+
+  float4 ring[KW];
+#pragma unroll
+  for (int k = 0; k < KW; ++k) ring[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  double acc_s = 0.0, acc_cs = 0.0;
+
+  for (int m = 0; m < iters; ++m) {
+    if constexpr (ASYNC) {
+      cp_async_wait<0>();
+      stage_convert<T, KW>(p, rawX, rawY, sX, sY);
+    }
+    __syncthreads();
+    // horizontal: warp k -> staged row k, lane -> columns [lane*KW, lane*KW+KW)
+    {
+      const float* rx = sX + warp * G::SW + lane * KW;
+      const float* ry = sY + warp * G::SW + lane * KW;
+      float4* out = sH + warp * G::NT + lane * KW;
+      hblur_xy<KW>(p, rx, ry, out);
+      hblur_prod<KW>(p, rx, ry, out);
+    }
+    __syncthreads();
+    const bool more = (m + 1 < iters);
+    if (more) {
+      if constexpr (ASYNC) stage_async<T, KW>(p, base, r0 + (m + 1) * KW, c0, rawX, rawY);
+      else stage_load<T, STAGE == STAGE_LUMA, KW>(p, base, r0 + (m + 1) * KW, c0, vx, vy);
+    }
+    // vertical + epilogue
+    float fs = 0.f, fcs = 0.f;
+#pragma unroll
+    for (int k = 0; k < KW; ++k) {
+      ring[k] = sH[k * G::NT + t];
+      const int o = m * KW + k - (KW - 1);
+      if (o >= 0 && o < rows && col_ok) {
+        const Moments mo = moments(p, vblur_at<KW, 4>(p, ring, k));
+        float S;
+        if (CS) {
+          // one reciprocal for both: S = A1 A2 / (B1 B2), cs = A2 / B2
+          const float inv = 1.0f / (mo.B1 * mo.B2);
+          S = mo.A1 * mo.A2 * inv;
+          fcs += mo.A2 * mo.B1 * inv;
+        } else {
+          S = (mo.A1 * mo.A2) / (mo.B1 * mo.B2);
+        }
+        fs += S;
+        if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
+      }
+    }
+    acc_s += (double)fs;
+    acc_cs += (double)fcs;
+    if constexpr (!ASYNC) {
+      if (more) stage_store<KW>(sX, sY, vx, vy);
+    }
+  }
+
+  const int bpp = p.strips * p.chunks;
+  const long long pidx = (long long)plane * bpp + blockIdx.y * p.strips + blockIdx.x;
+  acc_s = block_sum(acc_s, s_red);
+  if (t == 0) p.part_s[pidx] = acc_s;
+  if (CS) {
+    acc_cs = block_sum(acc_cs, s_red);
+    if (t == 0) p.part_cs[pidx] = acc_cs;
+  }
+  if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag))
+    ssim_fwd_finalize(p, bpp);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+template <typename T, int KW, int STAGE>
+static constexpr size_t fwd_smem() {
+  return sizeof(float4) * KW * Geo<KW>::NT + sizeof(float) * 2 * KW * Geo<KW>::SW +
+         (STAGE == STAGE_ASYNC ? Raw<T, KW>::kBytes : 0);
+}
+
+static SsimPlan fwd_plan(int Hout, int Wout, int K, int planes, int device) {
+  const int nt = 32 * K;
+  return plan_rows(Hout, (Wout + nt - 1) / nt, planes, device, 2, 4);
+}
+
+size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device) {
+  const SsimPlan pl = fwd_plan(Hout, Wout, K, planes, device);
+  return FAB_COUNTER_BYTES + 2 * sizeof(double) * (size_t)planes * pl.strips * pl.chunks;
+}
+
+template <typename T, int KW, bool CS, int STAGE>
+static int launch_fwd(const SsimArgs& p, int device, cudaStream_t st) {
+  auto kern = ssim_fwd_kernel<T, KW, CS, STAGE>;
+  const size_t sm = fwd_smem<T, KW, STAGE>();
+  static bool done[64] = {false};
+  FAB_TRY(ensure_smem(kern, sm, device, done));
+  dim3 grid(p.strips, p.chunks, p.P);
+  kern<<<grid, 32 * KW, sm, st>>>(p);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+template <typename T, bool CS, int STAGE>
+static int fwd_k(const SsimArgs& p, int K, int device, cudaStream_t st) {
+  switch (K) {
+    case 11: return launch_fwd<T, 11, CS, STAGE>(p, device, st);
+    case 9: return launch_fwd<T, 9, CS, STAGE>(p, device, st);
+    case 7: return launch_fwd<T, 7, CS, STAGE>(p, device, st);
+    case 5: return launch_fwd<T, 5, CS, STAGE>(p, device, st);
+    case 3: return launch_fwd<T, 3, CS, STAGE>(p, device, st);
+    default: return FA_E_WINDOW;
+  }
+}
+
+template <typename T>
+static int fwd_dispatch(const SsimArgs& p, int stage, bool cs, int K, int device,
+                        cudaStream_t st) {
+  if (stage == STAGE_ASYNC)
+    return cs ? fwd_k<T, true, STAGE_ASYNC>(p, K, device, st)
+              : fwd_k<T, false, STAGE_ASYNC>(p, K, device, st);
+  if (stage == STAGE_LUMA)
+    return cs ? fwd_k<T, true, STAGE_LUMA>(p, K, device, st)
+              : fwd_k<T, false, STAGE_LUMA>(p, K, device, st);
+  return cs ? fwd_k<T, true, STAGE_GENERIC>(p, K, device, st)
+            : fwd_k<T, false, STAGE_GENERIC>(p, K, device, st);
+}
+
+// cp.async needs every row start of the staged strips aligned to the copy size.
+static bool async_ok(const View& v, int esize) {
+  const int cb = esize == 8 ? 8 : 4;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(v.data);
+  return (a % cb) == 0 && ((v.sh * esize) % cb) == 0 && ((v.sc * esize) % cb) == 0 &&
+         ((v.sn * esize) % cb) == 0;
+}
+
+int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, const float* taps,
+                  int K, double shift, double C1, double C2, float* map_out, void* ws,
+                  size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
+                  double* out_per_image, double* out_total, int device, cudaStream_t st) {
+  if (!x.data || !y.data || !taps || !ws) return FA_E_ARG;
+  if (x.n <= 0 || x.c <= 0 || x.h <= 0 || x.w <= 0) return FA_E_SHAPE;
+  if (x.n != y.n || x.c != y.c || x.h != y.h || x.w != y.w) return FA_E_SHAPE;
+  if (x.sn != y.sn || x.sc != y.sc || x.sh != y.sh) return FA_E_SHAPE;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  if (luma && x.c != 3) return FA_E_SHAPE;
+  const int Hout = x.h - K + 1, Wout = x.w - K + 1;
+  if (Hout <= 0 || Wout <= 0) return FA_E_SHAPE;
+  SsimArgs p{};
+  p.x = static_cast<const char*>(x.data);
+  p.y = static_cast<const char*>(y.data);
+  p.sn = x.sn; p.sc = x.sc; p.sh = x.sh;
+  p.N = x.n; p.C = x.c; p.H = x.h; p.W = x.w;
+  p.Cm = luma ? 1 : x.c;
+  p.P = p.N * p.Cm;
+  if (p.P > 65535) return FA_E_SHAPE;
+  p.Hout = Hout; p.Wout = Wout;
+  p.shift = (float)shift; p.C1 = (float)C1; p.C2 = (float)C2;
+  if (luma) {
+    p.lk0 = (float)luma[0]; p.lk1 = (float)luma[1]; p.lk2 = (float)luma[2]; p.lk3 = (float)luma[3];
+  }
+  for (int j = 0; j < K; ++j) p.w[j] = taps[j];
+  const SsimPlan pl = fwd_plan(Hout, Wout, K, p.P, device);
+  p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
+  const size_t nb = (size_t)p.P * pl.strips * pl.chunks;
+  if (ws_bytes < FAB_COUNTER_BYTES + 2 * sizeof(double) * nb) return FA_E_ARG;
+  p.counter = static_cast<unsigned int*>(ws);
+  p.part_s = reinterpret_cast<double*>(static_cast<char*>(ws) + FAB_COUNTER_BYTES);
+  p.part_cs = out_plane_cs ? p.part_s + nb : nullptr;
+  p.map_out = map_out;
+  p.out_plane_s = out_plane_s; p.out_plane_cs = out_plane_cs;
+  p.out_per_image = out_per_image; p.out_total = out_total;
+  const bool cs = out_plane_cs != nullptr;
+  static const int esz[5] = {1, 2, 2, 4, 8};
+  if (dtype < 0 || dtype > 4) return FA_E_DTYPE;
+  const int stage = luma ? STAGE_LUMA
+                         : ((async_ok(x, esz[dtype]) && async_ok(y, esz[dtype])) ? STAGE_ASYNC
+                                                                                 : STAGE_GENERIC);
+  switch (dtype) {
+    case FA_U8: return fwd_dispatch<unsigned char>(p, stage, cs, K, device, st);
+    case FA_F16: return fwd_dispatch<f16_t>(p, stage, cs, K, device, st);
+    case FA_BF16: return fwd_dispatch<bf16_t>(p, stage, cs, K, device, st);
+    case FA_F32: return fwd_dispatch<float>(p, stage, cs, K, device, st);
+    default: return fwd_dispatch<double>(p, stage, cs, K, device, st);
+  }
+}
+
+}  // namespace fab

@@ -290,10 +290,10 @@ def _reject_double_backward() -> None:
             "Hessian-vector products, torch.func.hessian) cannot use them.")
 
 
-def _kernel_window(win_size: int, sigma: float, device) -> torch.Tensor:
+def _kernel_window(win_size: int, sigma: float, device) -> "backend.Taps":
     if win_size not in backend.KERNEL_WINDOWS:
         raise ValueError(f"win_size must be one of {backend.KERNEL_WINDOWS}, got {win_size}")
-    return gaussian_window_1d(win_size, sigma, device=device, dtype=torch.float32)
+    return backend.host_taps(win_size, sigma)
 
 
 class _FusedSSIM(torch.autograd.Function):
@@ -309,7 +309,8 @@ class _FusedSSIM(torch.autograd.Function):
                                    want_map=(mode == "map"),
                                    want_per_image=(mode == "none"),
                                    want_total=(mode == "mean"))
-        ctx.save_for_backward(x, y, win)
+        ctx.save_for_backward(x, y)
+        ctx.win = win
         ctx.consts = (shift, C1, C2)
         ctx.mode = mode
         if mode == "map":
@@ -319,7 +320,8 @@ class _FusedSSIM(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         _reject_double_backward()
-        x, y, win = ctx.saved_tensors
+        x, y = ctx.saved_tensors
+        win = ctx.win
         shift, C1, C2 = ctx.consts
         nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if not (nx or ny):
@@ -416,14 +418,16 @@ class _FusedSSIMCS(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, y, win, shift, C1, C2):
         res = backend.ssim_forward(x, y, win, shift=shift, C1=C1, C2=C2, want_cs=True)
-        ctx.save_for_backward(x, y, win)
+        ctx.save_for_backward(x, y)
+        ctx.win = win
         ctx.consts = (shift, C1, C2)
         return res["plane_s"], res["plane_cs"]
 
     @staticmethod
     def backward(ctx, g_s, g_cs):
         _reject_double_backward()
-        x, y, win = ctx.saved_tensors
+        x, y = ctx.saved_tensors
+        win = ctx.win
         shift, C1, C2 = ctx.consts
         nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if not (nx or ny):

@@ -113,7 +113,11 @@ FA_B200_API int fa_cuda_pixel_reduce(const void* a, const void* b, int dtype,
 /* replaces fa_cuda_ssim_workspace, fa_abi.h:136 */
 FA_B200_API int fa_cuda_ssim_workspace(int H, int W, int K, int* out_bpp);
 
-/* replaces fa_cuda_ssim, fa_abi.h:139-146.  partial: [N*C, bpp] float64. */
+/* replaces fa_cuda_ssim, fa_abi.h:139-146.  partial: [N*C, bpp] float64.
+ * `win` is the device window, as in the reference; the SSIM entry points of
+ * this block copy it to the host once per (device, pointer, K) and cache it,
+ * so the first call with a given window synchronises (make it outside any
+ * stream capture). */
 FA_B200_API int fa_cuda_ssim(const void* x, const void* y, int dtype, int N,
                              int C, int H, int W, const float* win, int K,
                              double shift, double C1, double C2,
@@ -210,9 +214,11 @@ FA_B200_API int fa_b200_ssim_workspace_bytes(int n, int c, int h, int w, int K,
  *   map_out          [N, C', Hout, Wout] float32 SSIM map
  *   out_plane_s/cs   [N*C'] per-plane means of SSIM and of its cs factor
  *   out_per_image    [N] mean over C' planes; out_total: batch mean
- * (C' = 1 with luma, else C). */
+ * (C' = 1 with luma, else C).
+ * taps_host: the K float32 taps of the 1-D window, in HOST memory, read
+ * during the call (they travel in the kernel parameters). */
 FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y,
-                             const double* luma, const float* win, int K,
+                             const double* luma, const float* taps_host, int K,
                              double shift, double C1, double C2,
                              float* map_out, void* workspace,
                              size_t workspace_bytes, double* out_plane_s,
@@ -227,9 +233,10 @@ FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y,
  *                                   1/(N*C*Hout*Wout) inside
  *   gs, gcs   [N*C] (device)      : d loss / d (plane-mean SSIM) and
  *                                   d loss / d (plane-mean cs) (MS-SSIM)
- * x, y: float32 contiguous [N, C, H, W].  dx / dy nullable (not both). */
+ * x, y: float32 contiguous [N, C, H, W].  dx / dy nullable (not both).
+ * taps_host: as for fa_b200_ssim (host memory). */
 FA_B200_API int fa_b200_ssim_backward(const float* x, const float* y, int N,
-                                      int C, int H, int W, const float* win,
+                                      int C, int H, int W, const float* taps_host,
                                       int K, double shift, double C1,
                                       double C2, const float* dL_dmap,
                                       const float* g_scalar, const float* gs,
