@@ -99,6 +99,8 @@ PROTOTYPES = {
     "fa_b200_gmsd_workspace_bytes": [_i, _i, _i, _i, _i, _i, _vp],
     "fa_b200_gmsd": [_pview, _pview, _vp, _d, _d, _i, _vp, _sz, _vp, _vp, _vp,
                      _i, _vp],
+    "fa_b200_pixel_reduce_noalloc": [_pview, _pview, _vp, _i, _d, _d, _vp, _vp, _vp, _vp,
+                                     _vp, _i, _vp],
     "fa_b200_pixel_backward": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _vp, _i,
                                _vp, _vp, _i, _vp],
 }

@@ -519,3 +519,79 @@ int pixel_backward_impl(const float* x, const float* y, int N, int C, int H, int
 }
 
 }  // namespace fab
+
+// ---------------------------------------------------------------------------
+// Pixel reduction without caller-provided scratch.
+//
+// Some callers cannot allocate device memory at all: a plugin that only ever
+// sees the host application's frame buffers, code running where cudaMalloc is
+// forbidden or unavailable, or a caller whose allocator is owned by someone
+// else.  They still need the reduction's scratch (grid-completion counters and
+// per-block partial sums).  This variant keeps that scratch in one fixed
+// array in device global memory that is part of the library image: every GPU
+// that loads the library holds these bytes until the process exits, and no
+// call allocates anything.
+//
+//   * Limit: FA_B200_NOALLOC_SCRATCH_BYTES of scratch, which covers batches of
+//     up to FA_B200_NOALLOC_MAX_IMAGES images; larger batches are rejected
+//     with FA_E_SHAPE before anything is launched.
+//   * The array is shared by every call on a device and keeps the last call's
+//     contents.  Each call clears the counters it needs on its own stream
+//     first.  Calls that may run at the same time on the GPU (different
+//     streams, several host threads) race on the array and give wrong results;
+//     serialise them.
+//   * The first call on each device looks the array's device address up
+//     (cudaGetSymbolAddress, with that device current) and caches it; make
+//     that first call before any stream capture.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace fab {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FA_B200_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on `device`, looked up once per device.
+// In host code the symbol itself is only a host-side stand-in, never a
+// device pointer, so the address must come from the runtime.
+static int noalloc_scratch(int device, void** out) {
+  constexpr int MAXD = 64;
+  static std::mutex mu;
+  static void* addr[MAXD] = {nullptr};
+  if (device < 0 || device >= MAXD) return FA_E_ARG;
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[device]) {
+    void* p = nullptr;
+    FAB_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));  // the device is current here
+    addr[device] = p;
+  }
+  *out = addr[device];
+  return FA_OK;
+}
+
+}  // namespace fab
+
+extern "C" FA_B200_API int fa_b200_pixel_reduce_noalloc(
+    const fa_view* a, const fa_view* b, const double* luma, int op, double param,
+    double psnr_bias, double* out_per_image, double* out_total, double* out_psnr_per_image,
+    double* out_psnr_total, uint64_t* out_isum_per_image, int device, void* stream) {
+  using namespace fab;
+  if (!a || !b || !a->data || !b->data) return FA_E_ARG;
+  if (a->dtype != b->dtype) return FA_E_DTYPE;
+  if (a->n <= 0 || a->c <= 0 || a->h <= 0 || a->w <= 0) return FA_E_SHAPE;
+  if (a->n > FA_B200_NOALLOC_MAX_IMAGES) return FA_E_SHAPE;
+  FAB_DEVICE_SCOPE(device);
+  int dev = device;
+  if (dev < 0) FAB_TRY(cudaGetDevice(&dev));
+  const size_t need = pixel_ws_bytes(a->n, dev);
+  if (need > FA_B200_NOALLOC_SCRATCH_BYTES) return FA_E_SHAPE;
+  void* ws = nullptr;
+  const int rc = noalloc_scratch(dev, &ws);
+  if (rc != FA_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // counters must start at zero; a previous call may have been interrupted
+  FAB_TRY(cudaMemsetAsync(ws, 0, FAB_COUNTER_BYTES, st));
+  return pixel_reduce_impl(to_view(*a), to_view(*b), a->dtype, luma, op, param, psnr_bias, ws,
+                           FA_B200_NOALLOC_SCRATCH_BYTES, out_per_image, out_total,
+                           out_psnr_per_image, out_psnr_total,
+                           reinterpret_cast<unsigned long long*>(out_isum_per_image), dev, st);
+}

@@ -272,6 +272,26 @@ FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N,
                                        int per_image, float* dx, float* dy,
                                        int device, void* stream);
 
+/* Pixel reduction for callers that cannot allocate device memory.  No
+ * counterpart in the reference: its reductions always take caller-allocated
+ * scratch.  Callers such as host-application plugins that only receive frame
+ * buffers, or code running where cudaMalloc is unavailable, can use this
+ * variant: its scratch is a fixed array of FA_B200_NOALLOC_SCRATCH_BYTES
+ * that lives in the library (held on every GPU that loads it until exit), so
+ * the call allocates nothing.  Same arguments and outputs as
+ * fa_b200_pixel_reduce minus the workspace.  Batches of more than
+ * FA_B200_NOALLOC_MAX_IMAGES images return FA_E_SHAPE.  All calls on a
+ * device share the array: calls that may overlap on the GPU race, so
+ * serialise them.  The first call on a device looks up the array's address;
+ * make it before any stream capture. */
+#define FA_B200_NOALLOC_SCRATCH_BYTES (64 * 1024)
+#define FA_B200_NOALLOC_MAX_IMAGES 4096
+FA_B200_API int fa_b200_pixel_reduce_noalloc(
+    const fa_view* a, const fa_view* b, const double* luma, int op,
+    double param, double psnr_bias, double* out_per_image, double* out_total,
+    double* out_psnr_per_image, double* out_psnr_total,
+    uint64_t* out_isum_per_image, int device, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif
