@@ -175,7 +175,19 @@ __device__ __forceinline__ void reduce_run(const T* pa, const T* pb, long long l
 #pragma unroll
     for (int u = 0; u < PIX_UNROLL; ++u) accum_vec<T, OP>(xa[u], xb[u], acc, lut, pf, pd);
   }
-  for (; v < nv; v += nl) accum_vec<T, OP>(__ldg(va + v), __ldg(vb + v), acc, lut, pf, pd);
+  if (v < nv) {
+    // the remainder: every load issued before any is used
+    uint4 xa[PIX_UNROLL], xb[PIX_UNROLL];
+#pragma unroll
+    for (int u = 0; u < PIX_UNROLL; ++u) {
+      const bool ok = v + u * nl < nv;
+      xa[u] = ok ? __ldg(va + v + u * nl) : make_uint4(0, 0, 0, 0);
+      xb[u] = ok ? __ldg(vb + v + u * nl) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < PIX_UNROLL; ++u)
+      if (v + u * nl < nv) accum_vec<T, OP>(xa[u], xb[u], acc, lut, pf, pd);
+  }
 }
 
 // Luma rows: dY = k0*dR + k1*dG + k2*dB in float64 (the luma offset cancels).
@@ -364,13 +376,39 @@ static int pix_bpi(int n_images, int device) {
   return (int)bpi;
 }
 
+// Blocks per image so that the whole grid is one wave of resident blocks
+// (never more than the workspace was sized for).
+template <auto KERN>
+static int wave_bpi(const PixArgs& p, int device) {
+  static int occ[64] = {0};  // one cache per kernel instantiation
+  auto* kern = KERN;
+  int nb = 0;
+  if (device >= 0 && device < 64 && occ[device] > 0) {
+    nb = occ[device];
+  } else {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, PIX_THREADS, 0) != cudaSuccess ||
+        nb <= 0)
+      nb = 4;
+    if (device >= 0 && device < 64) occ[device] = nb;
+  }
+  long long bpi = (long long)nb * sm_count(device) / p.n;
+  if (bpi < 1) bpi = 1;
+  return bpi < p.bpi ? (int)bpi : p.bpi;
+}
+
 template <typename T>
-static int launch_pixel_t(PixArgs& p, int op, cudaStream_t st) {
-  dim3 grid(p.bpi, p.n);
-#define FAB_PIX_OP(OPV)                                                        \
-  if (p.luma) pixel_rows_kernel<T, OPV, true><<<grid, PIX_THREADS, 0, st>>>(p); \
-  else if (p.flat) pixel_flat_kernel<T, OPV><<<grid, PIX_THREADS, 0, st>>>(p); \
-  else pixel_rows_kernel<T, OPV, false><<<grid, PIX_THREADS, 0, st>>>(p);
+static int launch_pixel_t(PixArgs& p, int op, int device, cudaStream_t st) {
+#define FAB_PIX_OP(OPV)                                                                  \
+  if (p.luma) {                                                                          \
+    p.bpi = wave_bpi<pixel_rows_kernel<T, OPV, true>>(p, device);                        \
+    pixel_rows_kernel<T, OPV, true><<<dim3(p.bpi, p.n), PIX_THREADS, 0, st>>>(p);        \
+  } else if (p.flat) {                                                                   \
+    p.bpi = wave_bpi<pixel_flat_kernel<T, OPV>>(p, device);                              \
+    pixel_flat_kernel<T, OPV><<<dim3(p.bpi, p.n), PIX_THREADS, 0, st>>>(p);              \
+  } else {                                                                               \
+    p.bpi = wave_bpi<pixel_rows_kernel<T, OPV, false>>(p, device);                       \
+    pixel_rows_kernel<T, OPV, false><<<dim3(p.bpi, p.n), PIX_THREADS, 0, st>>>(p);       \
+  }
   switch (op) {
     case FA_OP_MSE: FAB_PIX_OP(FA_OP_MSE); break;
     case FA_OP_L1: FAB_PIX_OP(FA_OP_L1); break;
@@ -413,11 +451,11 @@ int pixel_reduce_impl(const View& a, const View& b, int dtype, const double* lum
   p.out_psnr_per_image = out_ppi; p.out_psnr_total = out_ptot;
   p.out_isum = out_isum;
   switch (dtype) {
-    case FA_U8: return launch_pixel_t<unsigned char>(p, op, st);
-    case FA_F16: return launch_pixel_t<f16_t>(p, op, st);
-    case FA_BF16: return launch_pixel_t<bf16_t>(p, op, st);
-    case FA_F32: return launch_pixel_t<float>(p, op, st);
-    case FA_F64: return launch_pixel_t<double>(p, op, st);
+    case FA_U8: return launch_pixel_t<unsigned char>(p, op, device, st);
+    case FA_F16: return launch_pixel_t<f16_t>(p, op, device, st);
+    case FA_BF16: return launch_pixel_t<bf16_t>(p, op, device, st);
+    case FA_F32: return launch_pixel_t<float>(p, op, device, st);
+    case FA_F64: return launch_pixel_t<double>(p, op, device, st);
     default: return FA_E_DTYPE;
   }
 }
