@@ -273,14 +273,15 @@ def timed_call(fn, ev):
     return s0.elapsed_time(s1)
 
 
-def run_psnr_only(args):
-    """Profiling mode: only the config-1 uint8 PSNR kernel, `steps` calls."""
+def run_only(args):
+    """Profiling mode: only one uint8 config-1 metric kernel, warmup + steps calls."""
     import frame_analytics_b200 as fa
 
-    ua, ub = u8_pair(PIX_SHAPE, 5.0, 0)
+    ua, ub = u8_pair((args.images,) + PIX_SHAPE[1:], 5.0, 0)
     xu, yu = torch.from_numpy(ua).cuda(), torch.from_numpy(ub).cuda()
+    fn = {"psnr": fa.psnr, "ssim_u8": fa.ssim, "gmsd_u8": fa.gmsd}[args.only]
     for _ in range(args.warmup + args.steps):
-        fa.psnr(xu, yu)
+        fn(xu, yu)
     torch.cuda.synchronize()
 
 
@@ -465,8 +466,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--psnr-only", action="store_true",
-                    help="profiling mode: only the uint8 PSNR kernel")
+    ap.add_argument("--only", choices=["psnr", "ssim_u8", "gmsd_u8"], default=None,
+                    help="profiling mode: only this uint8 kernel (config-1 frames)")
     ap.add_argument("--no-extra", action="store_true",
                     help="time only the headline step (profiling runs)")
     ap.add_argument("--images", type=int, default=8,
@@ -476,8 +477,8 @@ def main():
     SHAPE = (args.images,) + SHAPE[1:]
     if args.warmup < 3:
         args.warmup = 3
-    if args.psnr_only:
-        run_psnr_only(args)
+    if args.only:
+        run_only(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

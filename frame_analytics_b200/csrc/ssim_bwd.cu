@@ -22,30 +22,44 @@ constexpr int G_PLANE = 2;   // dL/d(plane-mean S) and dL/d(plane-mean cs)
 template <int KW>
 struct BwdGeo {
   using G = Geo<KW>;
-  static constexpr int SCW = G::NT + KW - 1;  // coefficient row width (zero padded)
+  using R = Raw<float, KW>;
+  static constexpr int SCW = (G::NT + KW - 1 + 7) / 8 * 8;  // coefficient row width, zero padded
   static constexpr size_t kH = sizeof(float4) * KW * G::NT;
   static constexpr size_t kC = sizeof(float4) * KW * SCW;
-  static constexpr size_t kX = sizeof(float) * 2 * KW * G::SW;
-  static constexpr size_t kD = sizeof(float) * 2 * KW * G::TD;
+  static constexpr size_t kX = R::kFloatBytes;  // staged moment rows, x and y
+  static constexpr size_t kD = R::kFloatBytes;  // x and y at the gradient rows
   static constexpr size_t kBytes = kH + kC + kX + kD;
+  static_assert(kH % 128 == 0 && kC % 128 == 0, "TMA destinations must stay aligned");
 };
 
-template <int KW, bool DX, bool DY, int GMODE>
+// floor division for the (possibly negative) strip origin
+__device__ __forceinline__ int floor_to(int v, int a) {
+  return (v >= 0 ? v / a : -((-v + a - 1) / a)) * a;
+}
+
+// STAGE_TMA: TMA staging (row pitch a multiple of 16 bytes); STAGE_GENERIC:
+// register staging and direct loads for any float32 rows (built with both
+// gradients only; a null dx or dy is simply not written).
+template <int KW, bool DX, bool DY, int GMODE, int STAGE>
 __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_constant__ SsimArgs p) {
+  constexpr bool TMA = (STAGE == STAGE_TMA);
   using G = Geo<KW>;
   using B = BwdGeo<KW>;
   constexpr int NPL = (DX && DY) ? 4 : 3;
-  extern __shared__ float4 smem4[];
+  using R = Raw<float, KW>;
+  extern __shared__ __align__(128) float4 smem4[];
   float4* sH = smem4;                                 // [KW][NT] moments, then scatter rows
   float4* sC = sH + KW * G::NT;                       // [KW][SCW] coefficients
-  float* sX = reinterpret_cast<float*>(sC + KW * B::SCW);  // [KW][SW] staged inputs
-  float* sY = sX + KW * G::SW;
-  float* dX = sY + KW * G::SW;                        // [KW][TD] x at the gradient rows
-  float* dY = dX + KW * G::TD;
+  float* sX = reinterpret_cast<float*>(sC + KW * B::SCW);  // [KW][RP] staged inputs
+  float* sY = sX + KW * R::RP;
+  float* dX = sY + KW * R::RP;                        // [KW][RP] x at the gradient rows
+  float* dY = dX + KW * R::RP;
+  __shared__ __align__(8) unsigned long long s_bar[2];  // staging, gradient rows
 
   const int t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5;
   const int plane = blockIdx.z;
+  const int pn = plane / p.C, pc = plane - pn * p.C;
   const long long pbase = (long long)plane * p.H * p.W;
   const int c0 = blockIdx.x * G::TD;      // first gradient column of the strip
   const int mc0 = c0 - (KW - 1);          // first moment column
@@ -57,8 +71,9 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
   const bool q_ok = q >= 0 && q < p.Wout;
   const int dcol = c0 + t;                // this thread's gradient column
   const bool d_ok = t < G::TD && dcol < p.W;
-  const float* X = reinterpret_cast<const float*>(p.x) + pbase;
-  const float* Y = reinterpret_cast<const float*>(p.y) + pbase;
+  // TMA x coordinates rounded down to 16 bytes, and the offsets into the rows
+  const int xs0 = floor_to(mc0 + p.tma_d, R::XA), sofs = mc0 + p.tma_d - xs0;
+  const int xd0 = floor_to(c0 + p.tma_d, R::XA), dofs = c0 + p.tma_d - xd0;
 
   // zero the coefficient padding columns once
   for (int i = t; i < KW * (B::SCW - G::NT); i += G::NT) {
@@ -73,7 +88,20 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
     gCS = __ldg(p.gcs + plane) * p.grad_norm;
   }
 
-  stage_async<float, KW>(p, pbase, i0, mc0, sX, sY);
+  float vx[TMA ? 1 : G::NE], vy[TMA ? 1 : G::NE];
+  if constexpr (TMA) {
+    if (t == 0) {
+      mbar_init(&s_bar[0], 1);
+      mbar_init(&s_bar[1], 1);
+    }
+    fence_async_smem();
+    __syncthreads();
+    stage_tma<float, KW>(p, pn, pc, i0, xs0, sX, sY, &s_bar[0]);
+  } else {
+    stage_load<float, false, KW>(p, pbase, i0, mc0, vx, vy);
+    stage_store<KW, R::RP>(sX, sY, vx, vy);
+  }
+  const int so = TMA ? sofs : 0;
 
   float4 ring1[KW], ring2[KW];
 #pragma unroll
@@ -83,34 +111,28 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
   }
 
   for (int m = 0; m < iters; ++m) {
-    cp_async_wait<0>();
-    stage_convert<float, KW>(p, sX, sY, sX, sY);
+    if constexpr (TMA) {
+      mbar_wait(&s_bar[0], m & 1);
+      stage_convert<float, KW>(p, sX, sY, sX, sY);
+    }
     __syncthreads();
     // the input values at this iteration's gradient rows (L2-resident)
-    for (int i = t; i < KW * G::TD; i += G::NT) {
-      const int k = i / G::TD, c = i - k * G::TD;
-      const int r = i0 + m * KW + k - (KW - 1);
-      int nb = 0;
-      long long off = 0;
-      if (r >= 0 && r < p.H && c0 + c < p.W) {
-        nb = 4;
-        off = (long long)r * p.W + c0 + c;
-      }
-      cp_async<4>(dX + i, X + off, nb);
-      cp_async<4>(dY + i, Y + off, nb);
-    }
-    cp_async_commit();
+    if constexpr (TMA)
+      stage_tma<float, KW>(p, pn, pc, i0 + m * KW - (KW - 1), xd0, dX, dY, &s_bar[1]);
     // horizontal moments: warp k -> staged row k
     {
-      const float* rx = sX + warp * G::SW + lane * KW;
-      const float* ry = sY + warp * G::SW + lane * KW;
+      const float* rx = sX + warp * R::RP + so + lane * KW;
+      const float* ry = sY + warp * R::RP + so + lane * KW;
       float4* out = sH + warp * G::NT + lane * KW;
       hblur_xy<KW>(p, rx, ry, out);
       hblur_prod<KW>(p, rx, ry, out);
     }
     __syncthreads();
     const bool more = (m + 1 < iters);
-    if (more) stage_async<float, KW>(p, pbase, i0 + (m + 1) * KW, mc0, sX, sY);
+    if (more) {
+      if constexpr (TMA) stage_tma<float, KW>(p, pn, pc, i0 + (m + 1) * KW, xs0, sX, sY, &s_bar[0]);
+      else stage_load<float, false, KW>(p, pbase, i0 + (m + 1) * KW, mc0, vx, vy);
+    }
     // vertical moments -> coefficients
 #pragma unroll
     for (int k = 0; k < KW; ++k) {
@@ -154,8 +176,7 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
       hblur_pair<KW, 0, 2>(p, rc, out);
       hblur_pair<KW, 1, NPL - 2>(p, rc, out);
     }
-    if (more) cp_async_wait<1>();
-    else cp_async_wait<0>();
+    if constexpr (TMA) mbar_wait(&s_bar[1], m & 1);
     __syncthreads();
     // vertical scatter -> dx, dy
 #pragma unroll
@@ -166,10 +187,22 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
       if (L >= 2 * (KW - 1) && r < r0 + rows && d_ok) {
         const float4 s = vblur_at<KW, NPL>(p, ring2, k);
         const long long off = (long long)r * p.W + dcol;
-        const float xs = dX[k * G::TD + t] - p.shift;
-        const float ys = dY[k * G::TD + t] - p.shift;
-        if (DX) p.dx[pbase + off] = fmaf(2.f * xs, s.x, fmaf(ys, s.y, s.z));
-        if (DY) p.dy[pbase + off] = fmaf(2.f * ys, s.x, fmaf(xs, s.y, (DX && DY) ? s.w : s.z));
+        float xs, ys;
+        if constexpr (TMA) {
+          xs = dX[k * R::RP + dofs + t] - p.shift;
+          ys = dY[k * R::RP + dofs + t] - p.shift;
+        } else {
+          xs = __ldg(reinterpret_cast<const float*>(p.x) + pbase + off) - p.shift;
+          ys = __ldg(reinterpret_cast<const float*>(p.y) + pbase + off) - p.shift;
+        }
+        if (DX && p.dx) p.dx[pbase + off] = fmaf(2.f * xs, s.x, fmaf(ys, s.y, s.z));
+        if (DY && p.dy) p.dy[pbase + off] = fmaf(2.f * ys, s.x, fmaf(xs, s.y, (DX && DY) ? s.w : s.z));
+      }
+    }
+    if constexpr (!TMA) {
+      if (more) {
+        __syncthreads();  // every h1 read of this iteration's rows is long done; keep it simple
+        stage_store<KW, R::RP>(sX, sY, vx, vy);
       }
     }
   }
@@ -179,9 +212,9 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
 // host side
 // ---------------------------------------------------------------------------
 
-template <int KW, bool DX, bool DY, int GMODE>
+template <int KW, bool DX, bool DY, int GMODE, int STAGE>
 static int launch_bwd(const SsimArgs& p, int device, cudaStream_t st) {
-  auto kern = ssim_bwd_kernel<KW, DX, DY, GMODE>;
+  auto kern = ssim_bwd_kernel<KW, DX, DY, GMODE, STAGE>;
   const size_t sm = BwdGeo<KW>::kBytes;
   static bool done[64] = {false};
   FAB_TRY(ensure_smem(kern, sm, device, done));
@@ -191,23 +224,34 @@ static int launch_bwd(const SsimArgs& p, int device, cudaStream_t st) {
   return FA_OK;
 }
 
-template <bool DX, bool DY, int GMODE>
+template <bool DX, bool DY, int GMODE, int STAGE>
 static int bwd_k(const SsimArgs& p, int K, int device, cudaStream_t st) {
   switch (K) {
-    case 11: return launch_bwd<11, DX, DY, GMODE>(p, device, st);
-    case 9: return launch_bwd<9, DX, DY, GMODE>(p, device, st);
-    case 7: return launch_bwd<7, DX, DY, GMODE>(p, device, st);
-    case 5: return launch_bwd<5, DX, DY, GMODE>(p, device, st);
-    case 3: return launch_bwd<3, DX, DY, GMODE>(p, device, st);
+    case 11: return launch_bwd<11, DX, DY, GMODE, STAGE>(p, device, st);
+    case 9: return launch_bwd<9, DX, DY, GMODE, STAGE>(p, device, st);
+    case 7: return launch_bwd<7, DX, DY, GMODE, STAGE>(p, device, st);
+    case 5: return launch_bwd<5, DX, DY, GMODE, STAGE>(p, device, st);
+    case 3: return launch_bwd<3, DX, DY, GMODE, STAGE>(p, device, st);
     default: return FA_E_WINDOW;
   }
 }
 
 template <int GMODE>
-static int bwd_g(const SsimArgs& p, int K, int device, cudaStream_t st) {
-  if (p.dx && p.dy) return bwd_k<true, true, GMODE>(p, K, device, st);
-  if (p.dx) return bwd_k<true, false, GMODE>(p, K, device, st);
-  return bwd_k<false, true, GMODE>(p, K, device, st);
+static int bwd_g(const SsimArgs& p, bool tma, int K, int device, cudaStream_t st) {
+  if (!tma) return bwd_k<true, true, GMODE, STAGE_GENERIC>(p, K, device, st);
+  if (p.dx && p.dy) return bwd_k<true, true, GMODE, STAGE_TMA>(p, K, device, st);
+  if (p.dx) return bwd_k<true, false, GMODE, STAGE_TMA>(p, K, device, st);
+  return bwd_k<false, true, GMODE, STAGE_TMA>(p, K, device, st);
+}
+
+static int bwd_box_width(int K) {
+  switch (K) {
+    case 11: return Raw<float, 11>::BW;
+    case 9: return Raw<float, 9>::BW;
+    case 7: return Raw<float, 7>::BW;
+    case 5: return Raw<float, 5>::BW;
+    default: return Raw<float, 3>::BW;
+  }
 }
 
 int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* taps,
@@ -233,17 +277,29 @@ int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, co
   p.sn = (long long)C * H * W; p.sc = (long long)H * W; p.sh = W;
   p.Hout = Hout; p.Wout = Wout;
   p.shift = (float)shift; p.C1 = (float)C1; p.C2 = (float)C2;
-  for (int j = 0; j < K; ++j) p.w[j] = taps[j];
+  for (int j = 0; j < K; ++j) {
+    p.w[j] = taps[j];
+    p.w2[j] = make_float2(taps[j], taps[j]);
+  }
   p.dmap = dmap; p.gscalar = gscalar; p.gs = gs; p.gcs = gcs;
   p.dx = dx; p.dy = dy;
   const double npix = (double)Hout * Wout;
   p.grad_norm = gscalar ? (float)(1.0 / (npix * p.P)) : (gs ? (float)(1.0 / npix) : 1.0f);
+  bool tma = false;
+  {
+    const View vx{x, N, C, H, W, p.sn, p.sc, p.sh}, vy{y, N, C, H, W, p.sn, p.sc, p.sh};
+    int dx_ = 0, dy_ = 0;
+    const int bw = bwd_box_width(K);
+    tma = make_row_map(&p.tmx, vx, FA_F32, bw, &dx_) && make_row_map(&p.tmy, vy, FA_F32, bw, &dy_) &&
+          dx_ == dy_;
+    p.tma_d = tma ? dx_ : 0;
+  }
   const int td = 32 * K - (K - 1);
   const SsimPlan pl = plan_rows(H, (W + td - 1) / td, p.P, device, 1, 4);
   p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
-  if (dmap) return bwd_g<G_MAP>(p, K, device, st);
-  if (gscalar) return bwd_g<G_SCALAR>(p, K, device, st);
-  return bwd_g<G_PLANE>(p, K, device, st);
+  if (dmap) return bwd_g<G_MAP>(p, tma, K, device, st);
+  if (gscalar) return bwd_g<G_SCALAR>(p, tma, K, device, st);
+  return bwd_g<G_PLANE>(p, tma, K, device, st);
 }
 
 }  // namespace fab

@@ -26,11 +26,16 @@
 //     its tap from the constant bank instead of a register.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace fab {
 
 struct SsimArgs {
+  CUtensorMap tmx, tmy;  // TMA row maps of x and y (STAGE_TMA)
+  int sofs;              // staged-row offset of the strip's first column
+  int tma_d;             // leading elements the aligned map base adds
   const char* x;
   const char* y;
   long long sn, sc, sh;
@@ -40,6 +45,7 @@ struct SsimArgs {
   float shift, C1, C2;
   float lk0, lk1, lk2, lk3;
   float w[12];        // Gaussian taps
+  float2 w2[12];      // the same taps as {w, w} pairs for packed f32x2 FMAs
   int strips, chunks, RH;
   // forward
   float* map_out;
@@ -68,85 +74,136 @@ struct Geo {
   static constexpr int TD = NT - (KW - 1);             // backward: dx columns per strip
 };
 
-// Staging modes: cp.async of raw elements (aligned views, no luma), register
-// loads of any strided view, and register loads with the luma projection.
-constexpr int STAGE_ASYNC = 0;
+// Staging modes: TMA row copies of raw elements (16-byte-compatible views, no
+// luma), register loads of any strided view, and register loads with the
+// luma projection.
+constexpr int STAGE_TMA = 0;
 constexpr int STAGE_GENERIC = 1;
 constexpr int STAGE_LUMA = 2;
 
-// raw-staging geometry for cp.async: 4-byte chunks (8 for float64)
+// TMA staging geometry.  Each staged row is two boxes of BW elements landing
+// back to back, so a row is contiguous in shared memory.  The first column is
+// rounded down to a 16-byte boundary (the TMA x coordinate must be), which
+// leaves up to 16/sizeof(T)-1 leading elements: RP = 2*BW covers them.  BW is
+// a multiple of 128 bytes so every row half starts 128-byte aligned.
 template <typename T, int KW>
 struct Raw {
-  static constexpr int CB = sizeof(T) == 8 ? 8 : 4;     // bytes per copy
-  static constexpr int EPC = CB / (int)sizeof(T);        // elements per copy
-  static constexpr int RC = (Geo<KW>::SW + EPC - 1) / EPC;  // copies per row
-  static constexpr int RPE = RC * EPC;                   // raw row pitch, elements
+  static constexpr int E = (int)sizeof(T);
+  static constexpr int XA = 16 / E;                               // x alignment, elements
+  static constexpr int Q = 128 / E;                               // BW granule, elements
+  static constexpr int BW = ((Geo<KW>::SW + XA - 1 + 1) / 2 + Q - 1) / Q * Q;
+  static constexpr int RP = 2 * BW;                               // raw row pitch, elements
   static constexpr bool kInPlace = std::is_same<T, float>::value;
-  static constexpr size_t kBytes = kInPlace ? 0 : sizeof(T) * 2 * KW * RPE;
+  // converted-row pitch: float32 converts in place; other types pack tighter
+  static constexpr int FP = kInPlace ? RP : (Geo<KW>::SW + XA - 1 + 3) / 4 * 4;
+  static constexpr size_t kFloatBytes = (sizeof(float) * 2 * KW * FP + 127) / 128 * 128;  // x, y
+  static constexpr size_t kRawBytes = kInPlace ? 0 : (size_t)E * 2 * KW * RP;
+  static constexpr unsigned kTxBytes = (unsigned)E * 2u * KW * RP;    // per iteration
+  static_assert(BW <= 256, "TMA box too wide");
 };
 
 // ---------------------------------------------------------------------------
-// cp.async
+// TMA + mbarrier
 // ---------------------------------------------------------------------------
-template <int CB>
-__device__ __forceinline__ void cp_async(void* smem, const void* gmem, int src_bytes) {
-  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-  if constexpr (CB == 8) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gmem),
-                 "r"(src_bytes));
-  } else {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem),
-                 "r"(src_bytes));
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Bounded wait on a phase: gives up after ~2^24 polls instead of hanging.
+__device__ __forceinline__ void mbar_wait(unsigned long long* bar, unsigned parity) {
+  const unsigned a = smem_u32(bar);
+  for (int i = 0; i < (1 << 24); ++i) {
+    unsigned done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return;
   }
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+// One box {BW, 1, 1, 1} of a 4-D map (x, row, channel, image) into smem.
+__device__ __forceinline__ void tma_row(void* dst, const CUtensorMap* map, int x, int y, int c,
+                                        int n, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<unsigned long long>(map)), "r"(x), "r"(y), "r"(c), "r"(n),
+      "r"(smem_u32(bar))
+      : "memory");
 }
 
-// Issue the copies of KW rows (SW columns from col0) of one plane.  Rows and
-// columns outside the image are zero-filled (their values feed only outputs
-// that are never used).
+// Warp 0 issues the copies of KW rows of x and y starting at row0: lane r
+// copies row r of x, lane 16 + r row r of y (two boxes each), after lane 0 has
+// armed the barrier with the byte count.  Rows and columns outside the image
+// arrive as zeros.  x0 is the 16-byte-aligned map x coordinate of the strip.
 template <typename T, int KW>
-__device__ __forceinline__ void stage_async(const SsimArgs& p, long long base, int row0,
-                                            int col0, T* rawx, T* rawy) {
+__device__ __forceinline__ void stage_tma(const SsimArgs& p, int pn, int pc, int row0, int x0,
+                                          T* rawx, T* rawy, unsigned long long* bar) {
   using R = Raw<T, KW>;
-  const T* X = reinterpret_cast<const T*>(p.x) + base;
-  const T* Y = reinterpret_cast<const T*>(p.y) + base;
-  for (int i = threadIdx.x; i < KW * R::RC; i += Geo<KW>::NT) {
-    const int r = i / R::RC;
-    const int ch = i - r * R::RC;
-    const int gr = row0 + r, gc = col0 + ch * R::EPC;
-    int nb = 0;
-    long long off = 0;
-    if (gr >= 0 && gr < p.H && gc >= 0 && gc < p.W) {
-      nb = min(R::CB, (p.W - gc) * (int)sizeof(T));
-      off = (long long)gr * p.sh + gc;
+  static_assert(KW <= 16, "one lane per row");
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int r = lane & 15;
+    if (lane == 0) {
+      fence_async_smem();  // earlier generic accesses of the buffers come first
+      mbar_expect_tx(bar, R::kTxBytes);
     }
-    cp_async<R::CB>(rawx + r * R::RPE + ch * R::EPC, X + off, nb);
-    cp_async<R::CB>(rawy + r * R::RPE + ch * R::EPC, Y + off, nb);
+    __syncwarp();
+    if (r < KW) {
+      if (lane != 0) fence_async_smem();
+      const CUtensorMap* map = lane < 16 ? &p.tmx : &p.tmy;
+      T* dst = (lane < 16 ? rawx : rawy) + r * R::RP;
+      tma_row(dst, map, x0, row0 + r, pc, pn, bar);
+      tma_row(dst + R::BW, map, x0 + R::BW, row0 + r, pc, pn, bar);
+    }
   }
-  cp_async_commit();
 }
 
-// After the copies landed: this thread's own chunks -> shifted floats.
+// After the copies landed: raw (pitch RP) -> shifted floats (pitch FP), 4
+// elements per step.
 template <typename T, int KW>
 __device__ __forceinline__ void stage_convert(const SsimArgs& p, const T* rawx, const T* rawy,
                                               float* sx, float* sy) {
   using R = Raw<T, KW>;
-  using G = Geo<KW>;
-  for (int i = threadIdx.x; i < KW * R::RC; i += G::NT) {
-    const int r = i / R::RC;
-    const int ch = i - r * R::RC;
-#pragma unroll
-    for (int e = 0; e < R::EPC; ++e) {
-      const int c = ch * R::EPC + e;
-      if (c < G::SW) {
-        sx[r * G::SW + c] = Ld<T>::f(rawx[r * R::RPE + c]) - p.shift;
-        sy[r * G::SW + c] = Ld<T>::f(rawy[r * R::RPE + c]) - p.shift;
-      }
+  constexpr int N4 = KW * R::RP / 4;
+  constexpr int R4 = R::RP / 4;
+  for (int i = threadIdx.x; i < N4; i += Geo<KW>::NT) {
+    const int r = i / R4, c4 = i - r * R4;
+    if (4 * c4 >= R::FP) continue;
+    const int o4 = (r * R::FP) / 4 + c4;
+    float4 a, b;
+    if constexpr (std::is_same<T, float>::value) {
+      a = reinterpret_cast<const float4*>(rawx)[i];
+      b = reinterpret_cast<const float4*>(rawy)[i];
+    } else if constexpr (std::is_same<T, unsigned char>::value) {
+      const unsigned u = reinterpret_cast<const unsigned*>(rawx)[i];
+      const unsigned v = reinterpret_cast<const unsigned*>(rawy)[i];
+      a = make_float4((float)(u & 0xff), (float)((u >> 8) & 0xff), (float)((u >> 16) & 0xff),
+                      (float)(u >> 24));
+      b = make_float4((float)(v & 0xff), (float)((v >> 8) & 0xff), (float)((v >> 16) & 0xff),
+                      (float)(v >> 24));
+    } else {
+      const T* ex = rawx + 4 * i;
+      const T* ey = rawy + 4 * i;
+      a = make_float4(Ld<T>::f(ex[0]), Ld<T>::f(ex[1]), Ld<T>::f(ex[2]), Ld<T>::f(ex[3]));
+      b = make_float4(Ld<T>::f(ey[0]), Ld<T>::f(ey[1]), Ld<T>::f(ey[2]), Ld<T>::f(ey[3]));
     }
+    a.x -= p.shift; a.y -= p.shift; a.z -= p.shift; a.w -= p.shift;
+    b.x -= p.shift; b.y -= p.shift; b.z -= p.shift; b.w -= p.shift;
+    reinterpret_cast<float4*>(sx)[o4] = a;
+    reinterpret_cast<float4*>(sy)[o4] = b;
   }
 }
 
@@ -187,7 +244,7 @@ __device__ __forceinline__ void stage_load(const SsimArgs& p, long long base, in
 }
 
 // ... and store them once the buffer is free.
-template <int KW>
+template <int KW, int P>
 __device__ __forceinline__ void stage_store(float* sx, float* sy, const float (&vx)[Geo<KW>::NE],
                                             const float (&vy)[Geo<KW>::NE]) {
   using G = Geo<KW>;
@@ -195,8 +252,9 @@ __device__ __forceinline__ void stage_store(float* sx, float* sy, const float (&
   for (int e = 0; e < G::NE; ++e) {
     const int idx = threadIdx.x + e * G::NT;
     if (idx < KW * G::SW) {
-      sx[idx] = vx[e];
-      sy[idx] = vy[e];
+      const int r = idx / G::SW, c = idx - r * G::SW;
+      sx[r * P + c] = vx[e];
+      sy[r * P + c] = vy[e];
     }
   }
 }
@@ -215,14 +273,11 @@ __device__ __forceinline__ void hblur_xy(const SsimArgs& p, const float* __restr
   for (int o = 0; o < KW; ++o) acc[o] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int q = 0; q < 2 * KW - 1; ++q) {
-    const float xv = sx[q], yv = sy[q];
+    const float2 v = make_float2(sx[q], sy[q]);
 #pragma unroll
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
-      if (j >= 0 && j < KW) {
-        acc[o].x = fmaf(p.w[j], xv, acc[o].x);
-        acc[o].y = fmaf(p.w[j], yv, acc[o].y);
-      }
+      if (j >= 0 && j < KW) acc[o] = __ffma2_rn(p.w2[j], v, acc[o]);
     }
   }
 #pragma unroll
@@ -240,16 +295,12 @@ __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __res
 #pragma unroll
   for (int q = 0; q < 2 * KW - 1; ++q) {
     const float xv = sx[q], yv = sy[q];
-    const float xy = xv * yv;
     const float dv = xv - yv;
-    const float dd = dv * dv;
+    const float2 v = make_float2(xv * yv, dv * dv);
 #pragma unroll
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
-      if (j >= 0 && j < KW) {
-        acc[o].x = fmaf(p.w[j], xy, acc[o].x);
-        acc[o].y = fmaf(p.w[j], dd, acc[o].y);
-      }
+      if (j >= 0 && j < KW) acc[o] = __ffma2_rn(p.w2[j], v, acc[o]);
     }
   }
 #pragma unroll
@@ -271,8 +322,8 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
       if (j >= 0 && j < KW) {
-        acc[o].x = fmaf(p.w[j], v.x, acc[o].x);
-        if (NC == 2) acc[o].y = fmaf(p.w[j], v.y, acc[o].y);
+        if (NC == 2) acc[o] = __ffma2_rn(p.w2[j], v, acc[o]);
+        else acc[o].x = fmaf(p.w[j], v.x, acc[o].x);
       }
     }
   }
@@ -284,16 +335,15 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
 // output row needs slots K+1 .. K+KW (mod KW), oldest first.
 template <int KW, int K, int NPL>
 __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[KW]) {
-  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < KW; ++j) {
     const float4 h = ring[(K + 1 + j) % KW];
-    s.x = fmaf(p.w[j], h.x, s.x);
-    s.y = fmaf(p.w[j], h.y, s.y);
-    s.z = fmaf(p.w[j], h.z, s.z);
-    if (NPL == 4) s.w = fmaf(p.w[j], h.w, s.w);
+    a = __ffma2_rn(p.w2[j], make_float2(h.x, h.y), a);
+    if (NPL == 4) b = __ffma2_rn(p.w2[j], make_float2(h.z, h.w), b);
+    else b.x = fmaf(p.w[j], h.z, b.x);
   }
-  return s;
+  return make_float4(a.x, a.y, b.x, b.y);
 }
 
 // Static-slot dispatch of vblur for a loop index k that the unroller resolves.
@@ -340,6 +390,13 @@ static cudaError_t ensure_smem(K* kern, size_t bytes, int device, bool (&done)[6
   if (e == cudaSuccess && device >= 0 && device < 64) done[device] = true;
   return e;
 }
+
+// Host: a 4-D TMA map (x, row, channel, image) of a strided view, with the
+// base rounded down to 16 bytes (the leading elements that adds are returned
+// in *d).  Returns false when the view cannot be described (strides not
+// multiples of 16 bytes, or no driver entry point); callers then stage with
+// register loads.
+bool make_row_map(CUtensorMap* map, const View& v, int dtype, int box_w, int* d);
 
 struct SsimPlan {
   int strips, chunks, RH;

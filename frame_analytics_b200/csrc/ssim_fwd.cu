@@ -43,15 +43,17 @@ template <typename T, int KW, bool CS, int STAGE>
 __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_constant__ SsimArgs p) {
   using G = Geo<KW>;
   using R = Raw<T, KW>;
-  constexpr bool ASYNC = (STAGE == STAGE_ASYNC);
-  extern __shared__ float4 smem4[];
+  constexpr bool TMA = (STAGE == STAGE_TMA);
+  extern __shared__ __align__(128) float4 smem4[];
   float4* sH = smem4;                                        // [KW][NT]
-  float* sX = reinterpret_cast<float*>(smem4 + KW * G::NT);  // [KW][SW]
-  float* sY = sX + KW * G::SW;
-  T* rawX = R::kInPlace ? reinterpret_cast<T*>(sX) : reinterpret_cast<T*>(sY + KW * G::SW);
-  T* rawY = R::kInPlace ? reinterpret_cast<T*>(sY) : rawX + KW * R::RPE;
+  float* sX = reinterpret_cast<float*>(smem4 + KW * G::NT);  // [KW][FP]
+  float* sY = sX + KW * R::FP;
+  T* rawX = R::kInPlace ? reinterpret_cast<T*>(sX)
+                        : reinterpret_cast<T*>(reinterpret_cast<char*>(sX) + R::kFloatBytes);
+  T* rawY = R::kInPlace ? reinterpret_cast<T*>(sY) : rawX + KW * R::RP;
   __shared__ double s_red[32];
   __shared__ int s_flag;
+  __shared__ __align__(8) unsigned long long s_bar;
 
   const int t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5;
@@ -65,13 +67,21 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
   const bool col_ok = col < p.Wout;
   const int iters = (rows + KW - 1 + KW - 1) / KW;
   float* map = p.map_out ? p.map_out + (long long)plane * p.Hout * p.Wout : nullptr;
+  // TMA x coordinate of the strip, rounded down to 16 bytes, and the offset of
+  // column c0 inside the staged rows
+  const int xm = c0 + p.tma_d;
+  const int x0 = TMA ? (xm / R::XA) * R::XA : 0;
+  const int sofs = TMA ? xm - x0 : 0;
 
-  float vx[ASYNC ? 1 : G::NE], vy[ASYNC ? 1 : G::NE];
-  if constexpr (ASYNC) {
-    stage_async<T, KW>(p, base, r0, c0, rawX, rawY);
+  float vx[TMA ? 1 : G::NE], vy[TMA ? 1 : G::NE];
+  if constexpr (TMA) {
+    if (t == 0) mbar_init(&s_bar, 1);
+    fence_async_smem();
+    __syncthreads();
+    stage_tma<T, KW>(p, pn, pc, r0, x0, rawX, rawY, &s_bar);
   } else {
     stage_load<T, STAGE == STAGE_LUMA, KW>(p, base, r0, c0, vx, vy);
-    stage_store<KW>(sX, sY, vx, vy);
+    stage_store<KW, R::FP>(sX, sY, vx, vy);
   }
 
   float4 ring[KW];
@@ -80,15 +90,15 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
   double acc_s = 0.0, acc_cs = 0.0;
 
   for (int m = 0; m < iters; ++m) {
-    if constexpr (ASYNC) {
-      cp_async_wait<0>();
+    if constexpr (TMA) {
+      mbar_wait(&s_bar, m & 1);
       stage_convert<T, KW>(p, rawX, rawY, sX, sY);
     }
     __syncthreads();
     // horizontal: warp k -> staged row k, lane -> columns [lane*KW, lane*KW+KW)
     {
-      const float* rx = sX + warp * G::SW + lane * KW;
-      const float* ry = sY + warp * G::SW + lane * KW;
+      const float* rx = sX + warp * R::FP + sofs + lane * KW;
+      const float* ry = sY + warp * R::FP + sofs + lane * KW;
       float4* out = sH + warp * G::NT + lane * KW;
       hblur_xy<KW>(p, rx, ry, out);
       hblur_prod<KW>(p, rx, ry, out);
@@ -96,7 +106,7 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
     __syncthreads();
     const bool more = (m + 1 < iters);
     if (more) {
-      if constexpr (ASYNC) stage_async<T, KW>(p, base, r0 + (m + 1) * KW, c0, rawX, rawY);
+      if constexpr (TMA) stage_tma<T, KW>(p, pn, pc, r0 + (m + 1) * KW, x0, rawX, rawY, &s_bar);
       else stage_load<T, STAGE == STAGE_LUMA, KW>(p, base, r0 + (m + 1) * KW, c0, vx, vy);
     }
     // vertical + epilogue
@@ -122,8 +132,8 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
     }
     acc_s += (double)fs;
     acc_cs += (double)fcs;
-    if constexpr (!ASYNC) {
-      if (more) stage_store<KW>(sX, sY, vx, vy);
+    if constexpr (!TMA) {
+      if (more) stage_store<KW, R::FP>(sX, sY, vx, vy);
     }
   }
 
@@ -145,8 +155,8 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
 
 template <typename T, int KW, int STAGE>
 static constexpr size_t fwd_smem() {
-  return sizeof(float4) * KW * Geo<KW>::NT + sizeof(float) * 2 * KW * Geo<KW>::SW +
-         (STAGE == STAGE_ASYNC ? Raw<T, KW>::kBytes : 0);
+  return sizeof(float4) * KW * Geo<KW>::NT + Raw<T, KW>::kFloatBytes +
+         (STAGE == STAGE_TMA ? Raw<T, KW>::kRawBytes : 0);
 }
 
 static SsimPlan fwd_plan(int Hout, int Wout, int K, int planes, int device) {
@@ -186,9 +196,9 @@ static int fwd_k(const SsimArgs& p, int K, int device, cudaStream_t st) {
 template <typename T>
 static int fwd_dispatch(const SsimArgs& p, int stage, bool cs, int K, int device,
                         cudaStream_t st) {
-  if (stage == STAGE_ASYNC)
-    return cs ? fwd_k<T, true, STAGE_ASYNC>(p, K, device, st)
-              : fwd_k<T, false, STAGE_ASYNC>(p, K, device, st);
+  if (stage == STAGE_TMA)
+    return cs ? fwd_k<T, true, STAGE_TMA>(p, K, device, st)
+              : fwd_k<T, false, STAGE_TMA>(p, K, device, st);
   if (stage == STAGE_LUMA)
     return cs ? fwd_k<T, true, STAGE_LUMA>(p, K, device, st)
               : fwd_k<T, false, STAGE_LUMA>(p, K, device, st);
@@ -196,12 +206,82 @@ static int fwd_dispatch(const SsimArgs& p, int stage, bool cs, int K, int device
             : fwd_k<T, false, STAGE_GENERIC>(p, K, device, st);
 }
 
-// cp.async needs every row start of the staged strips aligned to the copy size.
-static bool async_ok(const View& v, int esize) {
-  const int cb = esize == 8 ? 8 : 4;
+// ---------------------------------------------------------------------------
+// TMA maps
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+bool make_row_map(CUtensorMap* map, const View& v, int dtype, int box_w, int* d) {
+  static const int esz[5] = {1, 2, 2, 4, 8};
+  static const CUtensorMapDataType dts[5] = {
+      CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+      CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+      CU_TENSOR_MAP_DATA_TYPE_FLOAT64};
+  if (dtype < 0 || dtype > 4) return false;
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const long long E = esz[dtype];
   const uintptr_t a = reinterpret_cast<uintptr_t>(v.data);
-  return (a % cb) == 0 && ((v.sh * esize) % cb) == 0 && ((v.sc * esize) % cb) == 0 &&
-         ((v.sn * esize) % cb) == 0;
+  const uintptr_t b = a & ~(uintptr_t)15;
+  if ((a - b) % E) return false;
+  *d = (int)((a - b) / E);
+  // strides of singleton dimensions are never used: give them a legal value
+  long long sh = v.sh * E, sc = v.sc * E, sn = v.sn * E;
+  if (v.c == 1) sc = ((sh * v.h + 15) / 16) * 16;
+  if (v.n == 1) sn = ((sc * v.c + 15) / 16) * 16;
+  const long long lim = 1LL << 40;
+  if (sh % 16 || sc % 16 || sn % 16 || sh <= 0 || sc <= 0 || sn <= 0 || sh >= lim ||
+      sc >= lim || sn >= lim)
+    return false;
+  if ((box_w * E) % 16 || box_w > 256) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)(v.w + *d), (cuuint64_t)v.h, (cuuint64_t)v.c,
+                              (cuuint64_t)v.n};
+  const cuuint64_t strides[3] = {(cuuint64_t)sh, (cuuint64_t)sc, (cuuint64_t)sn};
+  const cuuint32_t box[4] = {(cuuint32_t)box_w, 1, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, dts[dtype], 4, reinterpret_cast<void*>(b), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int KW>
+static int box_width(int dtype) {
+  switch (dtype) {
+    case FA_U8: return Raw<unsigned char, KW>::BW;
+    case FA_F16: return Raw<f16_t, KW>::BW;
+    case FA_BF16: return Raw<bf16_t, KW>::BW;
+    case FA_F32: return Raw<float, KW>::BW;
+    default: return Raw<double, KW>::BW;
+  }
+}
+
+static int box_width_k(int K, int dtype) {
+  switch (K) {
+    case 11: return box_width<11>(dtype);
+    case 9: return box_width<9>(dtype);
+    case 7: return box_width<7>(dtype);
+    case 5: return box_width<5>(dtype);
+    default: return box_width<3>(dtype);
+  }
 }
 
 int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, const float* taps,
@@ -229,7 +309,10 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
   if (luma) {
     p.lk0 = (float)luma[0]; p.lk1 = (float)luma[1]; p.lk2 = (float)luma[2]; p.lk3 = (float)luma[3];
   }
-  for (int j = 0; j < K; ++j) p.w[j] = taps[j];
+  for (int j = 0; j < K; ++j) {
+    p.w[j] = taps[j];
+    p.w2[j] = make_float2(taps[j], taps[j]);
+  }
   const SsimPlan pl = fwd_plan(Hout, Wout, K, p.P, device);
   p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
   const size_t nb = (size_t)p.P * pl.strips * pl.chunks;
@@ -241,11 +324,17 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
   p.out_plane_s = out_plane_s; p.out_plane_cs = out_plane_cs;
   p.out_per_image = out_per_image; p.out_total = out_total;
   const bool cs = out_plane_cs != nullptr;
-  static const int esz[5] = {1, 2, 2, 4, 8};
   if (dtype < 0 || dtype > 4) return FA_E_DTYPE;
-  const int stage = luma ? STAGE_LUMA
-                         : ((async_ok(x, esz[dtype]) && async_ok(y, esz[dtype])) ? STAGE_ASYNC
-                                                                                 : STAGE_GENERIC);
+  int stage = luma ? STAGE_LUMA : STAGE_GENERIC;
+  if (!luma) {
+    const int bw = box_width_k(K, dtype);
+    int dx = 0, dy = 0;
+    if (make_row_map(&p.tmx, x, dtype, bw, &dx) && make_row_map(&p.tmy, y, dtype, bw, &dy) &&
+        dx == dy) {
+      stage = STAGE_TMA;
+      p.tma_d = dx;
+    }
+  }
   switch (dtype) {
     case FA_U8: return fwd_dispatch<unsigned char>(p, stage, cs, K, device, st);
     case FA_F16: return fwd_dispatch<f16_t>(p, stage, cs, K, device, st);
