@@ -303,7 +303,7 @@ __device__ void pix_finalize(const PixArgs& p, double n_per_image) {
 
 // Contiguous images: block (bx, img) strides over image img's c*h*w elements.
 template <typename T, int OP>
-__global__ void __launch_bounds__(PIX_THREADS) pixel_flat_kernel(PixArgs p) {
+__global__ void __launch_bounds__(PIX_THREADS, 6) pixel_flat_kernel(PixArgs p) {
   using Tr = PixTraits<T, OP>;
   using Acc = typename Tr::Acc;
   __shared__ float s_lut[Tr::kLut ? 256 : 1];
