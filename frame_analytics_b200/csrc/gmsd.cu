@@ -15,18 +15,21 @@
 // -(g1 - g2)^2 / (g1^2 + g2^2 + T), which is exact to rounding where q is
 // close to 1, so sum(d) and sum(d^2) give the variance without cancellation.
 // Last-block finalisation keeps the whole metric to one launch.
-#include "common.cuh"
+#include "ssim_common.cuh"  // TMA/mbarrier helpers and make_row_map
 
 namespace fab {
 
-constexpr int GM_T = 128;             // threads
-constexpr int GM_CPT = 4;             // pooled columns per thread
+constexpr int GM_T = 256;             // threads
+constexpr int GM_CPT = 2;             // pooled columns per thread
 constexpr int GM_DW = GM_T * GM_CPT;  // pooled columns staged per strip
-constexpr int GM_OW = GM_DW - 2;      // output columns per strip
+constexpr int GM_OW = GM_DW - 4;      // output columns per strip (a multiple of 4 keeps
+                                      // every strip's 8-byte uint8 loads aligned)
 constexpr int GM_R = 8;               // output rows per iteration
 constexpr int GM_RING = GM_R + 2;
 
 struct GmsdArgs {
+  CUtensorMap tmx, tmy;  // TMA row maps (uint8 TMA kernel)
+  int tma_d;             // leading elements the aligned map base adds
   const char* x;
   const char* y;
   long long sn, sc, sh;
@@ -63,15 +66,12 @@ __device__ __forceinline__ void gm_load4(const GmsdArgs& p, const T* X, long lon
     const long long o0 = base + (long long)(2 * dr) * p.sh + 2 * dc;
     const unsigned char* b0 = reinterpret_cast<const unsigned char*>(X) + o0;
     const unsigned char* b1 = b0 + p.sh;
-    if (dc + GM_CPT <= p.Wd && ((reinterpret_cast<uintptr_t>(b0) | reinterpret_cast<uintptr_t>(b1)) & 7u) == 0) {
-      const uint2 u0 = __ldg(reinterpret_cast<const uint2*>(b0));
-      const uint2 u1 = __ldg(reinterpret_cast<const uint2*>(b1));
-      const unsigned a[2] = {u0.x, u0.y};
-      const unsigned b[2] = {u1.x, u1.y};
+    if (dc + GM_CPT <= p.Wd && ((reinterpret_cast<uintptr_t>(b0) | reinterpret_cast<uintptr_t>(b1)) & 3u) == 0) {
+      const unsigned u0 = __ldg(reinterpret_cast<const unsigned*>(b0));
+      const unsigned u1 = __ldg(reinterpret_cast<const unsigned*>(b1));
 #pragma unroll
       for (int i = 0; i < GM_CPT; ++i) {
-        const unsigned wa = a[i >> 1] >> ((i & 1) * 16);
-        const unsigned wb = b[i >> 1] >> ((i & 1) * 16);
+        const unsigned wa = u0 >> (i * 16), wb = u1 >> (i * 16);
         const int s = (int)(wa & 0xff) + (int)((wa >> 8) & 0xff) + (int)(wb & 0xff) +
                       (int)((wb >> 8) & 0xff);
         v[i] = 0.25f * (float)s;
@@ -94,6 +94,65 @@ __device__ __forceinline__ void gm_load4(const GmsdArgs& p, const T* X, long lon
     }
     v[i] = r;
   }
+}
+
+// One staged pooled row at this thread's columns c .. c+3: column differences
+// D[j] = s[j] - s[j+2] and 3-sums R[j] = s[j] + s[j+1] + s[j+2].
+__device__ __forceinline__ void gm_row_terms(const float* s, float (&D)[GM_CPT],
+                                             float (&R)[GM_CPT]) {
+  static_assert(GM_CPT == 2, "4 staged floats cover 2 output columns");
+  const float2 a = *reinterpret_cast<const float2*>(s);  // 8-byte aligned: s = row + 2t
+  const float2 b = *reinterpret_cast<const float2*>(s + 2);
+  const float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+  for (int j = 0; j < GM_CPT; ++j) {
+    D[j] = v[j] - v[j + 2];
+    R[j] = v[j] + v[j + 1] + v[j + 2];
+  }
+}
+
+// Output rows 0..nr-1 of one iteration from pooled rows 0..nr+1 of a ring
+// (row pitch `pitch` floats): this thread's GM_CPT columns, summed into
+// fs (d = q - 1) and fs2 (d^2); the map is written when requested.
+__device__ __forceinline__ void gm_rows(const GmsdArgs& p, const float* sxr, const float* syr,
+                                        int pitch, int nr, int t, int dc0, int plane, int orow0,
+                                        float& fs, float& fs2) {
+    const int c0t = t * GM_CPT;
+    constexpr float NINTH = 1.0f / 9.0f;
+    // Sliding 3-row window of column differences D (for gx) and row sums R
+    // (for gy) of this thread's 4 output columns, per image; the ring slot
+    // of pooled row r is r % 3, static because the loop is unrolled.
+    float Dx[3][GM_CPT], Rx[3][GM_CPT], Dy[3][GM_CPT], Ry[3][GM_CPT];
+#pragma unroll
+    for (int r = 0; r < GM_R + 2; ++r) {
+      if (r < nr + 2) {
+        gm_row_terms(sxr + r * pitch + c0t, Dx[r % 3], Rx[r % 3]);
+        gm_row_terms(syr + r * pitch + c0t, Dy[r % 3], Ry[r % 3]);
+        if (r >= 2) {
+          const int k = r - 2, s0 = (r - 2) % 3, s1 = (r - 1) % 3, s2 = r % 3;
+#pragma unroll
+          for (int i = 0; i < GM_CPT; ++i) {
+            const int c = c0t + i;
+            if (c < GM_OW && dc0 + c < p.Wout) {
+              // 3x the Prewitt/3 responses
+              const float gx1 = Dx[s0][i] + Dx[s1][i] + Dx[s2][i], gy1 = Rx[s0][i] - Rx[s2][i];
+              const float gx2 = Dy[s0][i] + Dy[s1][i] + Dy[s2][i], gy2 = Ry[s0][i] - Ry[s2][i];
+              const float G1 = fmaf(fmaf(gx1, gx1, gy1 * gy1), NINTH, p.eps);  // g1^2
+              const float G2 = fmaf(fmaf(gx2, gx2, gy2 * gy2), NINTH, p.eps);  // g2^2
+              // G1 - G2 from differences and sums of the gradients: no cancellation
+              const float dG = fmaf(gx1 - gx2, gx1 + gx2, (gy1 - gy2) * (gy1 + gy2)) * NINTH;
+              const float S = G1 + G2;
+              // q - 1 = -(g1 - g2)^2 / (g1^2 + g2^2 + T),  (g1 - g2)^2 = dG^2 / (g1 + g2)^2
+              const float d = -(dG * dG) / ((S + 2.f * sqrtf(G1 * G2)) * (S + p.T));
+              fs += d;
+              fs2 = fmaf(d, d, fs2);
+              if (p.map)
+                p.map[((long long)plane * p.Hout + (orow0 + k)) * p.Wout + dc0 + c] = 1.0f + d;
+            }
+          }
+        }
+      }
+    }
 }
 
 __device__ void gmsd_finalize(const GmsdArgs& p, int bpp) {
@@ -121,9 +180,9 @@ __device__ void gmsd_finalize(const GmsdArgs& p, int bpp) {
 }
 
 template <typename T, bool DOWN, bool LUMA>
-__global__ void __launch_bounds__(GM_T) gmsd_kernel(GmsdArgs p) {
-  __shared__ float sx[GM_RING][GM_DW + 4];
-  __shared__ float sy[GM_RING][GM_DW + 4];
+__global__ void __launch_bounds__(GM_T, 2) gmsd_kernel(GmsdArgs p) {
+  __shared__ __align__(16) float sx[GM_RING][GM_DW + 4];
+  __shared__ __align__(16) float sy[GM_RING][GM_DW + 4];
   __shared__ double s_red[32];
   __shared__ int s_flag;
 
@@ -154,45 +213,33 @@ __global__ void __launch_bounds__(GM_T) gmsd_kernel(GmsdArgs p) {
   double acc = 0.0, acc2 = 0.0;
   for (int rb = 0; rb < rows; rb += GM_R) {
     const int nr = min(GM_R, rows - rb);
-    // pooled rows rb+2 .. rb+nr+1 into ring rows 2 .. nr+1
-    for (int k = 0; k < nr; ++k) {
-      float a[GM_CPT], b[GM_CPT];
-      const int dr = r0 + rb + 2 + k;
-      gm_load4<T, DOWN, LUMA>(p, X, base, dr, dc, a);
-      gm_load4<T, DOWN, LUMA>(p, Y, base, dr, dc, b);
+    // pooled rows rb+2 .. rb+nr+1 into ring rows 2 .. nr+1: every row's loads
+    // are issued before the first store, so the iteration pays one memory
+    // latency, not GM_R of them
+    {
+      float a[GM_R][GM_CPT], b[GM_R][GM_CPT];
 #pragma unroll
-      for (int i = 0; i < GM_CPT; ++i) {
-        sx[2 + k][t * GM_CPT + i] = a[i];
-        sy[2 + k][t * GM_CPT + i] = b[i];
+      for (int k = 0; k < GM_R; ++k) {
+        if (k < nr) {
+          const int dr = r0 + rb + 2 + k;
+          gm_load4<T, DOWN, LUMA>(p, X, base, dr, dc, a[k]);
+          gm_load4<T, DOWN, LUMA>(p, Y, base, dr, dc, b[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < GM_R; ++k) {
+        if (k < nr) {
+#pragma unroll
+          for (int i = 0; i < GM_CPT; ++i) {
+            sx[2 + k][t * GM_CPT + i] = a[k][i];
+            sy[2 + k][t * GM_CPT + i] = b[k][i];
+          }
+        }
       }
     }
     __syncthreads();
     float fs = 0.f, fs2 = 0.f;
-    constexpr float THIRD = 1.0f / 3.0f;
-    for (int k = 0; k < nr; ++k) {
-#pragma unroll
-      for (int i = 0; i < GM_CPT; ++i) {
-        const int c = t * GM_CPT + i;
-        if (c < GM_OW && dc0 + c < p.Wout) {
-          float g[2];
-#pragma unroll
-          for (int which = 0; which < 2; ++which) {
-            const float(*s)[GM_DW + 4] = which ? sy : sx;
-            const float gx = ((s[k][c] - s[k][c + 2]) + (s[k + 1][c] - s[k + 1][c + 2]) +
-                              (s[k + 2][c] - s[k + 2][c + 2])) * THIRD;
-            const float gy = ((s[k][c] - s[k + 2][c]) + (s[k][c + 1] - s[k + 2][c + 1]) +
-                              (s[k][c + 2] - s[k + 2][c + 2])) * THIRD;
-            g[which] = sqrtf(fmaf(gx, gx, fmaf(gy, gy, p.eps)));
-          }
-          const float dg = g[0] - g[1];
-          const float d = -(dg * dg) / fmaf(g[0], g[0], fmaf(g[1], g[1], p.T));
-          fs += d;
-          fs2 = fmaf(d, d, fs2);
-          if (p.map)
-            p.map[((long long)plane * p.Hout + (r0 + rb + k)) * p.Wout + dc0 + c] = 1.0f + d;
-        }
-      }
-    }
+    gm_rows(p, &sx[0][0], &sy[0][0], GM_DW + 4, nr, t, dc0, plane, r0 + rb, fs, fs2);
     acc += (double)fs;
     acc2 += (double)fs2;
     __syncthreads();
@@ -215,6 +262,119 @@ __global__ void __launch_bounds__(GM_T) gmsd_kernel(GmsdArgs p) {
     gmsd_finalize(p, bpp);
 }
 
+
+// ---------------------------------------------------------------------------
+// uint8 kernel with TMA staging.  Each iteration of GM_R output rows needs
+// GM_R + 2 pooled rows, i.e. 2 * (GM_R + 2) input rows with the 2x2 pool.  They
+// arrive as one-row TMA boxes (GMT_BOX bytes, x rounded down to 16 bytes),
+// issued by all threads; the block pools them from shared memory into the
+// float ring, issues the next iteration's copies, then computes.  No thread
+// waits on a global load.
+// ---------------------------------------------------------------------------
+constexpr int GMT_BOX = 256;
+
+template <bool DOWN>
+struct GmTma {
+  static constexpr int RIN = DOWN ? 2 * (GM_R + 2) : (GM_R + 2);  // input rows / iteration
+  static constexpr int NB = DOWN ? 5 : 3;                         // boxes per input row
+  static constexpr int IW = NB * GMT_BOX;                         // staged bytes per row
+  static constexpr unsigned TX = 2u * RIN * IW;                   // bytes per iteration
+  static constexpr int RP = GM_DW + 4;                            // ring pitch, floats
+  static constexpr size_t RAW = (size_t)2 * RIN * IW;
+  static constexpr size_t SMEM = RAW + sizeof(float) * 2 * (GM_R + 2) * RP;
+  static_assert(RAW % 128 == 0, "ring must stay 16-byte aligned");
+};
+
+// 4 (or 8) consecutive bytes at byte offset o of a staged row, any alignment.
+__device__ __forceinline__ unsigned gm_bytes4(const unsigned char* row, int o) {
+  const unsigned* w = reinterpret_cast<const unsigned*>(row) + (o >> 2);
+  return __funnelshift_r(w[0], w[1], (o & 3) * 8);
+}
+
+template <bool DOWN>
+__global__ void __launch_bounds__(GM_T, 2) gmsd_tma_kernel(const __grid_constant__ GmsdArgs p) {
+  using G = GmTma<DOWN>;
+  extern __shared__ __align__(128) unsigned char s_gm[];
+  unsigned char* rawx = s_gm;
+  unsigned char* rawy = s_gm + G::RIN * G::IW;
+  float* ringx = reinterpret_cast<float*>(s_gm + G::RAW);
+  float* ringy = ringx + (GM_R + 2) * G::RP;
+  __shared__ __align__(8) unsigned long long s_bar;
+  __shared__ double s_red[32];
+  __shared__ int s_flag;
+
+  const int t = threadIdx.x;
+  const int plane = blockIdx.z;
+  const int pn = plane / p.Cm, pc = plane - pn * p.Cm;
+  const int dc0 = blockIdx.x * GM_OW;
+  const int r0 = blockIdx.y * p.RH;
+  const int rows = min(p.RH, p.Hout - r0);
+  const int xin = (DOWN ? 2 * dc0 : dc0) + p.tma_d;
+  const int x0 = (xin / 16) * 16, sofs = xin - x0;
+
+  auto issue = [&](int rb) {
+    if (t == 0) mbar_expect_tx(&s_bar, G::TX);
+    fence_async_smem();
+    for (int i = t; i < 2 * G::RIN * G::NB; i += GM_T) {
+      const int img = i / (G::RIN * G::NB), rem = i - img * (G::RIN * G::NB);
+      const int row = rem / G::NB, box = rem - row * G::NB;
+      const int in_row = DOWN ? 2 * (r0 + rb) + row : (r0 + rb) + row;
+      unsigned char* dst = (img ? rawy : rawx) + row * G::IW + box * GMT_BOX;
+      tma_row(dst, img ? &p.tmy : &p.tmx, x0 + box * GMT_BOX, in_row, pc, pn, &s_bar);
+    }
+  };
+
+  if (t == 0) mbar_init(&s_bar, 1);
+  fence_async_smem();
+  __syncthreads();
+  issue(0);
+
+  double acc = 0.0, acc2 = 0.0;
+  for (int rb = 0, it = 0; rb < rows; rb += GM_R, ++it) {
+    const int nr = min(GM_R, rows - rb);
+    mbar_wait(&s_bar, it & 1);
+    // pool (or convert) the staged bytes into the float ring
+#pragma unroll
+    for (int q = 0; q < GM_R + 2; ++q) {
+      if (q < nr + 2) {
+#pragma unroll
+        for (int img = 0; img < 2; ++img) {
+          const unsigned char* raw = img ? rawy : rawx;
+          float2 v;
+          if (DOWN) {
+            const int o = sofs + 4 * t;
+            const unsigned a = gm_bytes4(raw + (2 * q) * G::IW, o);
+            const unsigned b = gm_bytes4(raw + (2 * q + 1) * G::IW, o);
+            v = make_float2(0.25f * (float)((int)(a & 0xff) + (int)((a >> 8) & 0xff) +
+                                            (int)(b & 0xff) + (int)((b >> 8) & 0xff)),
+                            0.25f * (float)((int)((a >> 16) & 0xff) + (int)(a >> 24) +
+                                            (int)((b >> 16) & 0xff) + (int)(b >> 24)));
+          } else {
+            const unsigned a = gm_bytes4(raw + q * G::IW, sofs + 2 * t);
+            v = make_float2((float)(a & 0xff), (float)((a >> 8) & 0xff));
+          }
+          reinterpret_cast<float2*>((img ? ringy : ringx) + q * G::RP)[t] = v;
+        }
+      }
+    }
+    __syncthreads();
+    if (rb + GM_R < rows) issue(rb + GM_R);  // the staging buffer is free again
+    float fs = 0.f, fs2 = 0.f;
+    gm_rows(p, ringx, ringy, G::RP, nr, t, dc0, plane, r0 + rb, fs, fs2);
+    acc += (double)fs;
+    acc2 += (double)fs2;
+    __syncthreads();  // the ring is rewritten next iteration
+  }
+  const int bpp = p.strips * p.chunks;
+  const long long pidx = ((long long)plane * bpp + blockIdx.y * p.strips + blockIdx.x) * 2;
+  acc = block_sum(acc, s_red);
+  if (t == 0) p.part[pidx] = acc;
+  acc2 = block_sum(acc2, s_red);
+  if (t == 0) p.part[pidx + 1] = acc2;
+  if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag))
+    gmsd_finalize(p, bpp);
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -226,8 +386,8 @@ static GmPlan gm_plan(int Hout, int Wout, int planes, int device) {
   GmPlan g;
   g.strips = (Wout + GM_OW - 1) / GM_OW;
   const int sms = sm_count(device);
-  // ~12 resident blocks per SM, a few waves
-  long long want = (24LL * sms + (long long)g.strips * planes - 1) / ((long long)g.strips * planes);
+  // about two waves of 4 resident blocks per SM, each streaming many rows
+  long long want = (8LL * sms + (long long)g.strips * planes - 1) / ((long long)g.strips * planes);
   if (want < 1) want = 1;
   long long maxc = (Hout + GM_R - 1) / GM_R;
   if (want > maxc) want = maxc;
@@ -256,6 +416,17 @@ template <typename T, bool DOWN, bool LUMA>
 static int gm_launch(GmsdArgs& p, cudaStream_t st) {
   dim3 grid(p.strips, p.chunks, p.P);
   gmsd_kernel<T, DOWN, LUMA><<<grid, GM_T, 0, st>>>(p);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+template <bool DOWN>
+static int gm_launch_tma(GmsdArgs& p, int device, cudaStream_t st) {
+  auto kern = gmsd_tma_kernel<DOWN>;
+  static bool done[64] = {false};
+  FAB_TRY(ensure_smem(kern, GmTma<DOWN>::SMEM, device, done));
+  dim3 grid(p.strips, p.chunks, p.P);
+  kern<<<grid, GM_T, GmTma<DOWN>::SMEM, st>>>(p);
   FAB_LAUNCH_CHECK();
   return FA_OK;
 }
@@ -295,6 +466,14 @@ int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, doubl
   p.part = reinterpret_cast<double*>(static_cast<char*>(ws) + FAB_COUNTER_BYTES);
   p.out_mean = out_mean; p.out_std = out_std;
   p.map = map_out;
+  if (dtype == FA_U8 && !luma) {
+    int dx = 0, dy = 0;
+    if (make_row_map(&p.tmx, x, FA_U8, GMT_BOX, &dx) && make_row_map(&p.tmy, y, FA_U8, GMT_BOX, &dy) &&
+        dx == dy) {
+      p.tma_d = dx;
+      return down ? gm_launch_tma<true>(p, device, st) : gm_launch_tma<false>(p, device, st);
+    }
+  }
   switch (dtype) {
     case FA_U8: return gm_disp<unsigned char>(p, down, luma != nullptr, st);
     case FA_F16: return gm_disp<f16_t>(p, down, luma != nullptr, st);
