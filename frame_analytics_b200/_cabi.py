@@ -101,6 +101,8 @@ PROTOTYPES = {
                      _i, _vp],
     "fa_b200_pixel_reduce_noalloc": [_pview, _pview, _vp, _i, _d, _d, _vp, _vp, _vp, _vp,
                                      _vp, _i, _vp],
+    "fa_b200_gmsd_backward": [_vp, _vp, _i, _i, _i, _i, _i, _d, _d, _vp, _vp, _vp, _vp,
+                              _vp, _vp, _i, _vp],
     "fa_b200_pixel_backward": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _vp, _i,
                                _vp, _vp, _i, _vp],
 }

@@ -347,3 +347,25 @@ def pixel_backward(x, y, g, *, op: int, param: float, per_image: bool, luma=None
           _luma_arg(luma), int(op), float(param), gd.data_ptr(), int(bool(per_image)),
           _ptr(dx), _ptr(dy), _dev(xf), _stream(xf))
     return (dx.to(x.dtype) if need_dx else None, dy.to(y.dtype) if need_dy else None)
+
+
+def gmsd_backward(x, y, *, T: float, eps: float, downsample: bool, mean, std,
+                  g_mean=None, g_std=None, need_dx: bool = True, need_dy: bool = True):
+    """Gradients of the per-image GMS (mean) and GMSD (std) w.r.t. x and y."""
+    L = lib()
+    xf = x.detach().to(torch.float32).contiguous()
+    yf = y.detach().to(torch.float32).contiguous()
+    n, c, h, w = xf.shape
+    odd = downsample and (h % 2 or w % 2)
+    alloc = torch.zeros_like if odd else torch.empty_like
+    dx = alloc(xf) if need_dx else None
+    dy = alloc(yf) if need_dy else None
+
+    def d64(t):
+        return None if t is None else t.detach().to(torch.float64).reshape(-1).contiguous()
+
+    gm, gs, mu, sd = d64(g_mean), d64(g_std), d64(mean), d64(std)
+    _call(xf, L.fa_b200_gmsd_backward, xf.data_ptr(), yf.data_ptr(), n, c, h, w,
+          int(bool(downsample)), float(T), float(eps), _ptr(gm), _ptr(gs), _ptr(mu), _ptr(sd),
+          _ptr(dx), _ptr(dy), _dev(xf), _stream(xf))
+    return (dx.to(x.dtype) if need_dx else None, dy.to(y.dtype) if need_dy else None)

@@ -32,6 +32,10 @@ int pixel_backward_impl(const float* x, const float* y, int N, int C, int H, int
                         const double* luma, int op, double param, const double* g,
                         int per_image, float* dx, float* dy, int device, cudaStream_t st);
 size_t gmsd_ws_bytes(int planes, int h, int w, int down, int device);
+int gmsd_backward_impl(const float* x, const float* y, int N, int C, int H, int W, int down,
+                       double T, double eps, const double* gm, const double* gsd,
+                       const double* mu, const double* sd, float* dx, float* dy, int device,
+                       cudaStream_t st);
 
 // The multiprocessor count sizes every grid; cudaDeviceGetAttribute costs
 // microseconds, so it is read once per device.
@@ -344,6 +348,16 @@ FA_B200_API int fa_b200_gmsd(const fa_view* x, const fa_view* y, const double* l
   return gmsd_impl(to_view(*x), to_view(*y), x->dtype, luma, T, eps, downsample, workspace,
                    workspace_bytes, map_out, out_mean, out_std, device,
                    static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_gmsd_backward(const float* x, const float* y, int N, int C, int H,
+                                      int W, int downsample, double T, double eps,
+                                      const double* g_mean, const double* g_std,
+                                      const double* mean, const double* std_, float* dx,
+                                      float* dy, int device, void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return gmsd_backward_impl(x, y, N, C, H, W, downsample, T, eps, g_mean, g_std, mean, std_, dx,
+                            dy, device, static_cast<cudaStream_t>(stream));
 }
 
 FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N, int C, int H,

@@ -485,3 +485,147 @@ int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, doubl
 }
 
 }  // namespace fab
+
+// ---------------------------------------------------------------------------
+// Backward of GMS / GMSD (the reference differentiates its portable torch
+// path, functional.py:925-971; here one fused kernel).
+//   dL/dq = gm/n + gs (q - mu) / (n sigma)     per image (n map values)
+//   q = (2 g1 g2 + T)/D, D = g1^2 + g2^2 + T:  dq/dg1 = 2 (g2 - q g1)/D
+//   g1 = sqrt(gx1^2 + gy1^2 + eps):            dg1/dgx1 = gx1 / g1
+//   gx = Prewitt_x/3 (*) pooled x  ->  d pooled = transposed Prewitt of the
+//   coefficients; the 2x2 mean pool spreads 1/4 to each of its inputs.
+// A block owns a 32x32 tile of pooled gradient positions: it pools the 36x36
+// input region it needs into shared memory, forms the four coefficient maps
+// on the 34x34 map positions that touch the tile, and gathers.
+// ---------------------------------------------------------------------------
+namespace fab {
+
+constexpr int GB_T = 32;           // pooled gradient tile
+constexpr int GB_C = GB_T + 2;     // coefficient positions that reach the tile
+constexpr int GB_P = GB_T + 4;     // pooled values the coefficients need
+
+struct GmsdBwdArgs {
+  const float* x;
+  const float* y;
+  int N, C, H, W, Hd, Wd, Hout, Wout, down;
+  float T, eps;
+  const double* gm;   // [N] dL/d(gms per image), nullable
+  const double* gsd;  // [N] dL/d(gmsd per image), nullable
+  const double* mu;   // [N] forward gms
+  const double* sd;   // [N] forward gmsd
+  double npix;        // C * Hout * Wout
+  float* dx;
+  float* dy;
+};
+
+__global__ void __launch_bounds__(256) gmsd_bwd_kernel(GmsdBwdArgs p) {
+  __shared__ float px[GB_P][GB_P + 1], py[GB_P][GB_P + 1];
+  __shared__ float c1x[GB_C][GB_C + 1], c1y[GB_C][GB_C + 1];  // dL/dgx1, dL/dgy1
+  __shared__ float c2x[GB_C][GB_C + 1], c2y[GB_C][GB_C + 1];  // dL/dgx2, dL/dgy2
+  const int plane = blockIdx.z, n = plane / p.C;
+  const int tr = blockIdx.y * GB_T, tc = blockIdx.x * GB_T;  // first pooled row/col of the tile
+  const long long pbase = (long long)plane * p.H * p.W;
+  const int tid = threadIdx.x;
+  // 1. pooled inputs on rows tr-2 .. tr+33, cols tc-2 .. tc+33 (zero outside)
+  for (int i = tid; i < GB_P * GB_P; i += 256) {
+    const int r = i / GB_P, c = i - r * GB_P;
+    const int pr = tr - 2 + r, pc = tc - 2 + c;
+    float a = 0.f, b = 0.f;
+    if (pr >= 0 && pr < p.Hd && pc >= 0 && pc < p.Wd) {
+      if (p.down) {
+        const long long o = pbase + (long long)(2 * pr) * p.W + 2 * pc;
+        a = 0.25f * (__ldg(p.x + o) + __ldg(p.x + o + 1) + __ldg(p.x + o + p.W) + __ldg(p.x + o + p.W + 1));
+        b = 0.25f * (__ldg(p.y + o) + __ldg(p.y + o + 1) + __ldg(p.y + o + p.W) + __ldg(p.y + o + p.W + 1));
+      } else {
+        const long long o = pbase + (long long)pr * p.W + pc;
+        a = __ldg(p.x + o);
+        b = __ldg(p.y + o);
+      }
+    }
+    px[r][c] = a;
+    py[r][c] = b;
+  }
+  __syncthreads();
+  // 2. coefficients at map positions tr-2 .. tr+31 (zero outside the map)
+  const double gm = p.gm ? p.gm[n] : 0.0, gs = p.gsd ? p.gsd[n] : 0.0;
+  const double sdn = p.sd[n];
+  const float alpha = (float)(gm / p.npix - (sdn > 0.0 ? gs * p.mu[n] / (p.npix * sdn) : 0.0));
+  const float beta = (float)(sdn > 0.0 ? gs / (p.npix * sdn) : 0.0);
+  constexpr float THIRD = 1.0f / 3.0f;
+  for (int i = tid; i < GB_C * GB_C; i += 256) {
+    const int r = i / GB_C, c = i - r * GB_C;
+    const int mr = tr - 2 + r, mc = tc - 2 + c;
+    float ax = 0.f, ay = 0.f, bx = 0.f, by = 0.f;
+    if (mr >= 0 && mr < p.Hout && mc >= 0 && mc < p.Wout) {
+      const float gx1 = ((px[r][c] - px[r][c + 2]) + (px[r + 1][c] - px[r + 1][c + 2]) +
+                         (px[r + 2][c] - px[r + 2][c + 2])) * THIRD;
+      const float gy1 = ((px[r][c] - px[r + 2][c]) + (px[r][c + 1] - px[r + 2][c + 1]) +
+                         (px[r][c + 2] - px[r + 2][c + 2])) * THIRD;
+      const float gx2 = ((py[r][c] - py[r][c + 2]) + (py[r + 1][c] - py[r + 1][c + 2]) +
+                         (py[r + 2][c] - py[r + 2][c + 2])) * THIRD;
+      const float gy2 = ((py[r][c] - py[r + 2][c]) + (py[r][c + 1] - py[r + 2][c + 1]) +
+                         (py[r][c + 2] - py[r + 2][c + 2])) * THIRD;
+      const float g1 = sqrtf(fmaf(gx1, gx1, fmaf(gy1, gy1, p.eps)));
+      const float g2 = sqrtf(fmaf(gx2, gx2, fmaf(gy2, gy2, p.eps)));
+      const float D = fmaf(g1, g1, fmaf(g2, g2, p.T));
+      const float q = fmaf(2.f * g1, g2, p.T) / D;
+      const float up = fmaf(beta, q, alpha);           // dL/dq
+      const float k1 = up * 2.f * (g2 - q * g1) / (D * g1);  // dL/dg1 / g1
+      const float k2 = up * 2.f * (g1 - q * g2) / (D * g2);
+      ax = k1 * gx1; ay = k1 * gy1; bx = k2 * gx2; by = k2 * gy2;
+    }
+    c1x[r][c] = ax; c1y[r][c] = ay; c2x[r][c] = bx; c2y[r][c] = by;
+  }
+  __syncthreads();
+  // 3. transposed Prewitt: pooled (i, j) gathers map positions (i-a, j-b)
+  for (int i = tid; i < GB_T * GB_T; i += 256) {
+    const int r = i / GB_T, c = i - r * GB_T;
+    const int pr = tr + r, pc = tc + c;
+    if (pr >= p.Hd || pc >= p.Wd) continue;
+    float sx = 0.f, sy = 0.f;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+#pragma unroll
+      for (int b = 0; b < 3; ++b) {
+        const int cr = r + 2 - a, cc = c + 2 - b;   // map position (pr - a, pc - b)
+        const float kx = (b == 0) ? THIRD : (b == 2 ? -THIRD : 0.f);
+        const float ky = (a == 0) ? THIRD : (a == 2 ? -THIRD : 0.f);
+        sx = fmaf(kx, c1x[cr][cc], fmaf(ky, c1y[cr][cc], sx));
+        sy = fmaf(kx, c2x[cr][cc], fmaf(ky, c2y[cr][cc], sy));
+      }
+    }
+    if (p.down) {
+      const long long o = pbase + (long long)(2 * pr) * p.W + 2 * pc;
+      const float gx = 0.25f * sx, gy = 0.25f * sy;
+      if (p.dx) { p.dx[o] = gx; p.dx[o + 1] = gx; p.dx[o + p.W] = gx; p.dx[o + p.W + 1] = gx; }
+      if (p.dy) { p.dy[o] = gy; p.dy[o + 1] = gy; p.dy[o + p.W] = gy; p.dy[o + p.W + 1] = gy; }
+    } else {
+      const long long o = pbase + (long long)pr * p.W + pc;
+      if (p.dx) p.dx[o] = sx;
+      if (p.dy) p.dy[o] = sy;
+    }
+  }
+}
+
+int gmsd_backward_impl(const float* x, const float* y, int N, int C, int H, int W, int down,
+                       double T, double eps, const double* gm, const double* gsd,
+                       const double* mu, const double* sd, float* dx, float* dy, int device,
+                       cudaStream_t st) {
+  (void)device;
+  if (!x || !y || !mu || !sd || (!dx && !dy) || (!gm && !gsd)) return FA_E_ARG;
+  if (N <= 0 || C <= 0 || H <= 0 || W <= 0) return FA_E_SHAPE;
+  GmsdBwdArgs p{};
+  if (!gm_dims(H, W, down, &p.Hd, &p.Wd, &p.Hout, &p.Wout)) return FA_E_SHAPE;
+  if ((long long)N * C > 65535) return FA_E_SHAPE;
+  p.x = x; p.y = y; p.N = N; p.C = C; p.H = H; p.W = W; p.down = down ? 1 : 0;
+  p.T = (float)T; p.eps = (float)eps;
+  p.gm = gm; p.gsd = gsd; p.mu = mu; p.sd = sd;
+  p.npix = (double)C * p.Hout * p.Wout;
+  p.dx = dx; p.dy = dy;
+  dim3 grid((p.Wd + GB_T - 1) / GB_T, (p.Hd + GB_T - 1) / GB_T, N * C);
+  gmsd_bwd_kernel<<<grid, 256, 0, st>>>(p);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+}  // namespace fab

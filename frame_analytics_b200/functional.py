@@ -508,6 +508,32 @@ def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = N
 # GMSD / GMS
 # --------------------------------------------------------------------------- #
 
+class _GmsdFn(torch.autograd.Function):
+    """Differentiable per-image (GMS mean, GMSD) -- the GMSD.loss path.
+    Forward: the fused kernel; backward: one fused kernel (transposed Prewitt
+    and pool) fed with the forward's statistics."""
+
+    @staticmethod
+    def forward(ctx, x, y, T, eps, downsample):
+        mean, std = backend.gmsd(x, y, T=T, eps=eps, downsample=downsample)
+        ctx.save_for_backward(x, y, mean, std)
+        ctx.consts = (T, eps, downsample)
+        return mean, std
+
+    @staticmethod
+    def backward(ctx, g_mean, g_std):
+        _reject_double_backward()
+        x, y, mean, std = ctx.saved_tensors
+        T, eps, down = ctx.consts
+        nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (nx or ny):
+            return (None,) * 5
+        dx, dy = backend.gmsd_backward(x, y, T=T, eps=eps, downsample=down, mean=mean,
+                                       std=std, g_mean=g_mean, g_std=g_std,
+                                       need_dx=nx, need_dy=ny)
+        return dx, dy, None, None, None
+
+
 def _gmsd_common(x, y, data_range, T, eps, downsample, luma, crop_border, reduction,
                  return_map, backend_hint):
     _check_reduction(reduction)
@@ -520,12 +546,18 @@ def _gmsd_common(x, y, data_range, T, eps, downsample, luma, crop_border, reduct
     if return_map:
         q = backend.gms_map(x4, y4, T=Tv, eps=ev, downsample=downsample, luma=lk)
         return q, None
-    if _grad_wanted(x4, y4):
-        raise NotImplementedError("GMS/GMSD gradients are not implemented yet")
     hd = x4.shape[-2] // 2 if downsample else x4.shape[-2]
     wd = x4.shape[-1] // 2 if downsample else x4.shape[-1]
     if hd < 3 or wd < 3:
         raise ValueError(f"image {hd}x{wd} is smaller than the 3x3 Prewitt window")
+    if _grad_wanted(x4, y4):
+        # the fused backward reads float32 planes: luma/crop/cast with
+        # differentiable torch ops first
+        if lk is not None:
+            x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
+        xf = x4.to(torch.float32).contiguous()
+        yf = y4.to(torch.float32).contiguous()
+        return None, _GmsdFn.apply(xf, yf, Tv, ev, bool(downsample))
     return None, backend.gmsd(x4.detach(), y4.detach(), T=Tv, eps=ev,
                               downsample=downsample, luma=lk)
 

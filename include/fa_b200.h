@@ -261,6 +261,22 @@ FA_B200_API int fa_b200_gmsd(const fa_view* x, const fa_view* y,
                              double* out_mean, double* out_std, int device,
                              void* stream);
 
+/* Gradient of GMS / GMSD w.r.t. the inputs, one launch, no scratch.  The
+ * reference differentiates its portable torch path instead
+ * (functional.py:925-971).  x, y: float32 contiguous [N, C, H, W] (channels
+ * pooled per image, as in the forward); mean / std_: the forward's per-image
+ * GMS and GMSD (device, [N] float64); g_mean / g_std: d loss / d those
+ * (device, [N] float64, either may be NULL).  dx / dy: [N, C, H, W] float32,
+ * nullable (not both); positions the 2x2 pool drops (an odd last row or
+ * column) are not written -- zero them first. */
+FA_B200_API int fa_b200_gmsd_backward(const float* x, const float* y, int N,
+                                      int C, int H, int W, int downsample,
+                                      double T, double eps,
+                                      const double* g_mean, const double* g_std,
+                                      const double* mean, const double* std_,
+                                      float* dx, float* dy, int device,
+                                      void* stream);
+
 /* Gradient of a pixel reduction (mse / l1 / charbonnier / huber) w.r.t. its
  * inputs.  Replaces the torch autograd the reference uses for these
  * (functional.py:1097-1141).  x, y: float32 contiguous [N, C, H, W];

@@ -63,3 +63,52 @@ def test_luma_and_crop():
     m, s = O.gmsd(a, b, luma="bt709", crop_border=3, eps=EPS_G)
     np.testing.assert_allclose(fa.gmsd(T(a), T(b), luma="bt709", crop_border=3,
                                        reduction="none").cpu().numpy(), s, atol=5e-6)
+
+
+def _torch_gms_stats(x, y, T, eps, down):
+    """float64 torch restatement of reference.gmsd_reference for gradients."""
+    import torch.nn.functional as F
+
+    if down:
+        x, y = F.avg_pool2d(x, 2), F.avg_pool2d(y, 2)
+    k = torch.tensor([[1.0, 0.0, -1.0]] * 3, dtype=x.dtype, device=x.device) / 3.0
+    kk = torch.stack([k, k.t()]).unsqueeze(1)
+    n, c, h, w = x.shape
+    gx = F.conv2d(x.reshape(n * c, 1, h, w), kk)
+    gy = F.conv2d(y.reshape(n * c, 1, h, w), kk)
+    g1 = torch.sqrt((gx * gx).sum(1) + eps)
+    g2 = torch.sqrt((gy * gy).sum(1) + eps)
+    q = ((2 * g1 * g2 + T) / (g1 * g1 + g2 * g2 + T)).reshape(n, -1)
+    return q.mean(1), q.std(1, correction=0)
+
+
+@pytest.mark.parametrize("down", [True, False])
+@pytest.mark.parametrize("shape", [(2, 3, 41, 53), (1, 1, 70, 97)])
+def test_gms_gmsd_gradients(down, shape):
+    torch.manual_seed(1)
+    a = torch.rand(shape, device="cuda", dtype=torch.float64)
+    b = (a + 0.1 * torch.randn_like(a)).clamp(0, 1)
+    T, eps = 170.0 / 255 ** 2, 1e-12
+    x = a.float().requires_grad_()
+    y = b.float().requires_grad_()
+    w1 = torch.randn(shape[0], device="cuda", dtype=torch.float64)
+    w2 = torch.randn(shape[0], device="cuda", dtype=torch.float64)
+    m = fa.gms(x, y, data_range=1.0, downsample=down, reduction="none")
+    s = fa.gmsd(x, y, data_range=1.0, downsample=down, reduction="none")
+    gx, gy = torch.autograd.grad((m * w1).sum() + (s * w2).sum(), (x, y))
+    xr, yr = a.clone().requires_grad_(), b.clone().requires_grad_()
+    mr, sr = _torch_gms_stats(xr, yr, T, (1e-6) ** 2, down)
+    rx, ry = torch.autograd.grad((mr * w1).sum() + (sr * w2).sum(), (xr, yr))
+    for got, want in ((gx, rx), (gy, ry)):
+        err = float((got.double() - want).abs().max() / want.abs().max())
+        assert err < 2e-3, err
+
+
+def test_gmsd_module_loss_backward():
+    torch.manual_seed(2)
+    a = torch.rand(2, 3, 64, 80, device="cuda")
+    p = (a + 0.05 * torch.randn_like(a)).clamp(0, 1).requires_grad_()
+    loss = fa.GMSD(data_range=1.0).loss(p, a)
+    loss.backward()
+    assert p.grad is not None and torch.isfinite(p.grad).all() and float(p.grad.abs().max()) > 0
+    assert abs(float(loss) - (1 - float(fa.gms(p.detach(), a, data_range=1.0)))) < 1e-12
