@@ -1,0 +1,82 @@
+"""Batch sharding of the metrics over the GPUs of one node.
+
+Images are independent, so the metric path shards by batch with no data
+exchange: rank r scores images [lo, hi) of the batch on its own GPU, and the
+per-image results (a few bytes each) are all-gathered so every rank holds the
+whole batch's values.  The reference has no multi-device code; this is the
+layer BASELINE.json's multi-GPU sweep needs.
+
+One process per GPU, `torch.distributed` initialised by the caller (NCCL on
+GPUs; the gather logic is backend-agnostic and is tested with gloo on CPU).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Dict, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(n: int, rank: int, world: int) -> Tuple[int, int]:
+    """Contiguous [lo, hi) of an n-image batch owned by `rank`; the first
+    n % world ranks hold one image more.  Every rank can compute every
+    rank's bounds, so no sizes are exchanged."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def gather_per_image(local: torch.Tensor, n: int, group=None) -> torch.Tensor:
+    """All-gather per-image values (1-D, this rank's shard) into the full
+    (n,) batch, in batch order, on every rank.  Uneven shards are padded to
+    the largest shard for the collective and trimmed after it."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    lo, hi = shard_bounds(n, rank, world)
+    if local.ndim != 1 or local.numel() != hi - lo:
+        raise ValueError(f"rank {rank} holds images [{lo}, {hi}) but passed {tuple(local.shape)}")
+    width = max(shard_bounds(n, r, world)[1] - shard_bounds(n, r, world)[0] for r in range(world))
+    buf = torch.zeros(width, dtype=local.dtype, device=local.device)
+    buf[: local.numel()] = local
+    out = torch.empty(world * width, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, buf, group=group)
+    parts = []
+    for r in range(world):
+        a, b = shard_bounds(n, r, world)
+        parts.append(out[r * width: r * width + (b - a)])
+    return torch.cat(parts)
+
+
+def batch_mean(per_image: torch.Tensor) -> torch.Tensor:
+    """Mean over the gathered batch, summed in batch order on every rank
+    (deterministic; equal to the single-GPU mean to ~1e-15 relative)."""
+    return per_image.sum() / per_image.numel()
+
+
+class ShardedMetrics:
+    """Score a batch sharded over ranks and return whole-batch per-image results.
+
+    ``metrics`` maps a name to a callable ``f(x, y) -> (n_local,)`` (e.g.
+    ``lambda x, y: fa.ssim(x, y, reduction='none')``).  Each rank passes its
+    own shard; the result holds every image's value on every rank.
+    """
+
+    def __init__(self, metrics: Dict[str, Callable], group=None):
+        self.metrics = dict(metrics)
+        self.group = group
+
+    def __call__(self, x_local: torch.Tensor, y_local: torch.Tensor, n: int) -> Dict[str, torch.Tensor]:
+        return {name: gather_per_image(fn(x_local, y_local).reshape(-1), n, self.group)
+                for name, fn in self.metrics.items()}
+
+
+def default_metrics(names: Sequence[str] = ("ssim", "gmsd"), **kw) -> Dict[str, Callable]:
+    """Per-image SSIM / GMSD / GMS / PSNR / MSE callables for ShardedMetrics."""
+    from . import functional as F
+
+    table = {"ssim": F.ssim, "gmsd": F.gmsd, "gms": F.gms, "psnr": F.psnr, "mse": F.mse,
+             "ms_ssim": F.ms_ssim}
+    return {n: (lambda f: (lambda x, y: f(x, y, reduction="none", **kw)))(table[n]) for n in names}
