@@ -142,10 +142,12 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
       float4 cf = make_float4(0.f, 0.f, 0.f, 0.f);
       if (L >= KW - 1 && o >= 0 && o < p.Hout && q_ok) {
         const Moments mo = moments(p, vblur_at<KW, 4>(p, ring1, k));
-        const float iB1 = 1.0f / mo.B1;
-        const float iB2 = 1.0f / mo.B2;
-        const float S = mo.A1 * mo.A2 * iB1 * iB2;
-        const float kk = 2.f * mo.A2 * iB1 * iB2;
+        // one reciprocal: 1/B1 = B2/(B1 B2), 1/B2 = B1/(B1 B2)
+        const float inv = 1.0f / (mo.B1 * mo.B2);
+        const float iB1 = mo.B2 * inv;
+        const float iB2 = mo.B1 * inv;
+        const float S = mo.A1 * mo.A2 * inv;
+        const float kk = 2.f * mo.A2 * inv;
         float g = gS, bb, cc;
         if (GMODE == G_MAP)
           g = __ldg(p.dmap + (long long)plane * p.Hout * p.Wout + (long long)o * p.Wout + q);
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
           cc = 2.f * (g * mo.A1 * iB1 + gCS) * iB2;
         } else {
           bb = -g * S * iB2;
-          cc = 2.f * g * mo.A1 * iB1 * iB2;
+          cc = 2.f * g * mo.A1 * inv;
         }
         cf.x = bb;
         cf.y = cc;
@@ -295,7 +297,7 @@ int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, co
     p.tma_d = tma ? dx_ : 0;
   }
   const int td = 32 * K - (K - 1);
-  const SsimPlan pl = plan_rows(H, (W + td - 1) / td, p.P, device, 1, 4);
+  const SsimPlan pl = plan_rows(H, (W + td - 1) / td, p.P, device, 1, 2 * (K - 1));
   p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
   if (dmap) return bwd_g<G_MAP>(p, tma, K, device, st);
   if (gscalar) return bwd_g<G_SCALAR>(p, tma, K, device, st);

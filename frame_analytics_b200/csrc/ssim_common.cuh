@@ -335,14 +335,19 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
 // output row needs slots K+1 .. K+KW (mod KW), oldest first.
 template <int KW, int K, int NPL>
 __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[KW]) {
-  float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+  // even and odd taps accumulate separately: twice the independent chains
+  float2 a0 = make_float2(0.f, 0.f), b0 = make_float2(0.f, 0.f);
+  float2 a1 = make_float2(0.f, 0.f), b1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < KW; ++j) {
     const float4 h = ring[(K + 1 + j) % KW];
+    float2& a = (j & 1) ? a1 : a0;
+    float2& b = (j & 1) ? b1 : b0;
     a = __ffma2_rn(p.w2[j], make_float2(h.x, h.y), a);
     if (NPL == 4) b = __ffma2_rn(p.w2[j], make_float2(h.z, h.w), b);
     else b.x = fmaf(p.w[j], h.z, b.x);
   }
+  const float2 a = __fadd2_rn(a0, a1), b = __fadd2_rn(b0, b1);
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
@@ -402,18 +407,28 @@ struct SsimPlan {
   int strips, chunks, RH;
 };
 
-// Split rows so that the grid holds about `waves` x SMs x blocks-per-SM blocks.
+// Split rows into chunks (one block per strip x plane x chunk).  The cost
+// model is waves x (rows per chunk + halo rows each chunk recomputes): few
+// chunks waste the halo less, but must still fill every SM slot.
 static inline SsimPlan plan_rows(int rows_total, int strips, int planes, int device,
-                                 int blocks_per_sm, int waves) {
-  const int sms = sm_count(device);
-  const long long target = (long long)waves * sms * blocks_per_sm;
+                                 int blocks_per_sm, int halo) {
+  const long long slots = (long long)sm_count(device) * blocks_per_sm;
   const long long per = (long long)strips * planes;
-  long long want = (target + per - 1) / per;
-  if (want < 1) want = 1;
-  if (want > rows_total) want = rows_total;
+  int best_c = 1;
+  double best = 1e300;
+  const int cmax = rows_total < 256 ? rows_total : 256;
+  for (int c = 1; c <= cmax; ++c) {
+    const long long rh = (rows_total + c - 1) / c;
+    const long long waves = (per * c + slots - 1) / slots;
+    const double cost = (double)waves * (double)(rh + halo);
+    if (cost < best * 0.999) {
+      best = cost;
+      best_c = c;
+    }
+  }
   SsimPlan pl;
   pl.strips = strips;
-  pl.RH = (int)((rows_total + want - 1) / want);
+  pl.RH = (rows_total + best_c - 1) / best_c;
   pl.chunks = (rows_total + pl.RH - 1) / pl.RH;
   return pl;
 }

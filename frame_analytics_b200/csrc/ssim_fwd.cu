@@ -161,7 +161,7 @@ static constexpr size_t fwd_smem() {
 
 static SsimPlan fwd_plan(int Hout, int Wout, int K, int planes, int device) {
   const int nt = 32 * K;
-  return plan_rows(Hout, (Wout + nt - 1) / nt, planes, device, 2, 4);
+  return plan_rows(Hout, (Wout + nt - 1) / nt, planes, device, 2, K - 1);
 }
 
 size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device) {
