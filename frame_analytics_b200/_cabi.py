@@ -105,6 +105,8 @@ PROTOTYPES = {
                               _vp, _vp, _i, _vp],
     "fa_b200_pixel_backward": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _vp, _i,
                                _vp, _vp, _i, _vp],
+    "fa_b200_pool2": [_pview, _vp, _vp, _i, _vp],
+    "fa_b200_pool2_backward": [_vp, _i, _i, _i, _i, _vp, _i, _vp],
 }
 _RESTYPE = {"fa_cuda_error_string": ctypes.c_char_p}
 

@@ -330,6 +330,33 @@ def gms_map(x, y, *, T: float, eps: float, downsample: bool, luma=None) -> torch
 
 
 # --------------------------------------------------------------------------- #
+# MS-SSIM pyramid pooling
+# --------------------------------------------------------------------------- #
+
+def pool2(x: torch.Tensor, luma=None) -> torch.Tensor:
+    """2x2 mean pool to float32 (``F.avg_pool2d(x.float(), 2)``), one read of
+    ``x`` in its own dtype and strides; ``luma`` projects RGB first."""
+    L = lib()
+    vx, x = as_view(kernel_dtype(x))
+    cm = 1 if luma is not None else vx.c
+    out = torch.empty((vx.n, cm, vx.h // 2, vx.w // 2), dtype=torch.float32, device=x.device)
+    _call(x, L.fa_b200_pool2, ctypes.byref(vx), _luma_arg(luma), out.data_ptr(), _dev(x),
+          _stream(x))
+    return out
+
+
+def pool2_backward(g: torch.Tensor, shape) -> torch.Tensor:
+    """Adjoint of :func:`pool2` for a float32 input of ``shape``."""
+    L = lib()
+    g = g.detach().to(torch.float32).contiguous()
+    n, c, h, w = shape
+    dx = torch.empty((n, c, h, w), dtype=torch.float32, device=g.device)
+    _call(g, L.fa_b200_pool2_backward, g.data_ptr(), n, c, h, w, dx.data_ptr(), _dev(g),
+          _stream(g))
+    return dx
+
+
+# --------------------------------------------------------------------------- #
 # pixel-loss backward
 # --------------------------------------------------------------------------- #
 

@@ -37,6 +37,11 @@ int gmsd_backward_impl(const float* x, const float* y, int N, int C, int H, int 
                        const double* mu, const double* sd, float* dx, float* dy, int device,
                        cudaStream_t st);
 
+int pool2_impl(const View& x, int dtype, const double* luma, float* out, int device,
+               cudaStream_t st);
+int pool2_backward_impl(const float* g, int N, int C, int H, int W, float* dx, int device,
+                        cudaStream_t st);
+
 // The multiprocessor count sizes every grid; cudaDeviceGetAttribute costs
 // microseconds, so it is read once per device.
 int sm_count(int device) {
@@ -367,6 +372,19 @@ FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N, in
   FAB_DEVICE_SCOPE(device);
   return pixel_backward_impl(x, y, N, C, H, W, luma, op, param, g, per_image, dx, dy, device,
                              static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_pool2(const fa_view* x, const double* luma, float* out, int device,
+                              void* stream) {
+  if (!view_ok(x) || !out) return FA_E_ARG;
+  FAB_DEVICE_SCOPE(device);
+  return pool2_impl(to_view(*x), x->dtype, luma, out, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_pool2_backward(const float* g, int N, int C, int H, int W, float* dx,
+                                       int device, void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return pool2_backward_impl(g, N, C, H, W, dx, device, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -1,0 +1,127 @@
+// 2x2 mean pooling between the scales of the MS-SSIM pyramid.
+//
+// The reference pools with torch (`F.avg_pool2d(x.to(float32), 2)`,
+// functional.py:717-725, used at :885 and :930), which for uint8 input first materialises a
+// full-resolution float copy.  This kernel reads the input once in its own
+// dtype and layout (strided views, optional luma projection) and writes the
+// pooled float32 plane: out = (a + b + c + d) / 4 over non-overlapping 2x2
+// blocks, an odd trailing row/column dropped (reference.py:231-241, `_avg_pool2`).
+// Its backward spreads a quarter of each pooled gradient over the 2x2 block.
+// Both are bandwidth-bound elementwise kernels: each thread produces two
+// adjacent outputs.
+#include "common.cuh"
+
+namespace fab {
+
+struct PoolArgs {
+  const char* x;
+  long long sn, sc, sh;
+  int N, C, H, W, Cm, Hp, Wp;
+  float k0, k1, k2, k3;
+  float* out;
+};
+
+template <typename T, bool LUMA>
+__device__ __forceinline__ float pool_px(const PoolArgs& p, const T* X, long long o) {
+  if constexpr (LUMA) {
+    return fmaf(p.k0, Ld<T>::f(ldro(X + o)),
+                fmaf(p.k1, Ld<T>::f(ldro(X + o + p.sc)), fmaf(p.k2, Ld<T>::f(ldro(X + o + 2 * p.sc)), p.k3)));
+  } else {
+    return Ld<T>::f(ldro(X + o));
+  }
+}
+
+template <typename T, bool LUMA>
+__global__ void __launch_bounds__(256) pool2_kernel(PoolArgs p) {
+  const T* X = reinterpret_cast<const T*>(p.x);
+  const int wp2 = (p.Wp + 1) / 2;  // output pairs per row
+  const long long total = (long long)p.N * p.Cm * p.Hp * wp2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j2 = (int)(i % wp2);
+    long long r = i / wp2;
+    const int hp = (int)(r % p.Hp);
+    r /= p.Hp;
+    const int c = (int)(r % p.Cm);
+    const int n = (int)(r / p.Cm);
+    const long long base = (long long)n * p.sn + (long long)c * p.sc + (long long)(2 * hp) * p.sh;
+    float* o = p.out + (((long long)n * p.Cm + c) * p.Hp + hp) * p.Wp;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int j = 2 * j2 + k;
+      if (j < p.Wp) {
+        const long long a = base + 2 * j;
+        const float s = pool_px<T, LUMA>(p, X, a) + pool_px<T, LUMA>(p, X, a + 1) +
+                        pool_px<T, LUMA>(p, X, a + p.sh) + pool_px<T, LUMA>(p, X, a + p.sh + 1);
+        o[j] = 0.25f * s;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) pool2_bwd_kernel(const float* __restrict__ g, int NC, int H,
+                                                         int W, int Hp, int Wp,
+                                                         float* __restrict__ dx) {
+  const long long total = (long long)NC * H * W;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int w = (int)(i % W);
+    const long long r = i / W;
+    const int h = (int)(r % H);
+    const long long pl = r / H;
+    const int hp = h >> 1, wp = w >> 1;
+    dx[i] = (hp < Hp && wp < Wp) ? 0.25f * __ldg(g + (pl * Hp + hp) * Wp + wp) : 0.f;
+  }
+}
+
+static unsigned grid_for(long long work, int device) {
+  long long b = (work + 255) / 256;
+  const long long cap = (long long)sm_count(device) * 16;
+  return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+template <typename T>
+static int pool_launch(const PoolArgs& p, bool luma, int device, cudaStream_t st) {
+  const long long work = (long long)p.N * p.Cm * p.Hp * ((p.Wp + 1) / 2);
+  if (luma) pool2_kernel<T, true><<<grid_for(work, device), 256, 0, st>>>(p);
+  else pool2_kernel<T, false><<<grid_for(work, device), 256, 0, st>>>(p);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+int pool2_impl(const View& x, int dtype, const double* luma, float* out, int device,
+               cudaStream_t st) {
+  if (!x.data || !out) return FA_E_ARG;
+  if (x.n <= 0 || x.c <= 0 || x.h < 2 || x.w < 2) return FA_E_SHAPE;
+  if (luma && x.c != 3) return FA_E_SHAPE;
+  PoolArgs p{};
+  p.x = static_cast<const char*>(x.data);
+  p.sn = x.sn; p.sc = x.sc; p.sh = x.sh;
+  p.N = x.n; p.C = x.c; p.H = x.h; p.W = x.w;
+  p.Cm = luma ? 1 : x.c;
+  p.Hp = x.h / 2; p.Wp = x.w / 2;
+  if (luma) {
+    p.k0 = (float)luma[0]; p.k1 = (float)luma[1]; p.k2 = (float)luma[2]; p.k3 = (float)luma[3];
+  }
+  p.out = out;
+  switch (dtype) {
+    case FA_U8: return pool_launch<unsigned char>(p, luma != nullptr, device, st);
+    case FA_F16: return pool_launch<f16_t>(p, luma != nullptr, device, st);
+    case FA_BF16: return pool_launch<bf16_t>(p, luma != nullptr, device, st);
+    case FA_F32: return pool_launch<float>(p, luma != nullptr, device, st);
+    case FA_F64: return pool_launch<double>(p, luma != nullptr, device, st);
+    default: return FA_E_DTYPE;
+  }
+}
+
+int pool2_backward_impl(const float* g, int N, int C, int H, int W, float* dx, int device,
+                        cudaStream_t st) {
+  if (!g || !dx) return FA_E_ARG;
+  if (N <= 0 || C <= 0 || H < 2 || W < 2) return FA_E_SHAPE;
+  const long long work = (long long)N * C * H * W;
+  pool2_bwd_kernel<<<grid_for(work, device), 256, 0, st>>>(g, N * C, H, W, H / 2, W / 2, dx);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+}  // namespace fab

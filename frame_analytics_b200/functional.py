@@ -441,6 +441,20 @@ class _FusedSSIMCS(torch.autograd.Function):
         return (dx if nx else None, dy if ny else None, None, None, None, None)
 
 
+class _Pool2Fn(torch.autograd.Function):
+    """2x2 mean pool between MS-SSIM scales (functional.py:885), forward and
+    adjoint both one kernel launch."""
+
+    @staticmethod
+    def forward(ctx, x):
+        ctx.shape, ctx.dtype = tuple(x.shape), x.dtype
+        return backend.pool2(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return backend.pool2_backward(g, ctx.shape).to(ctx.dtype)
+
+
 def _ms_weights(w, device) -> torch.Tensor:
     key = (w, str(device))
     t = _ms_weight_cache.get(key)
@@ -479,23 +493,30 @@ def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = N
     win = _kernel_window(win_size, sigma, x4.device)
     lk = _luma_k(mode, L)
     grad = _grad_wanted(x4, y4)
-    if lk is not None and (grad or len(w) > 1):
+    if lk is not None and grad:
         x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
         lk = None
-    n, c = x4.shape[0], x4.shape[1]
+    n = x4.shape[0]
     cx, cy = x4, y4
     terms = []
     for i in range(len(w)):
+        # Scale 0 reads the inputs as given (luma projected inside the SSIM
+        # kernel); the first pool projects too, so no full-resolution float
+        # or luma copy is ever written.
+        scale_lk = lk if i == 0 else None
         if i:
-            cx = F.avg_pool2d(cx.to(torch.float32), 2)
-            cy = F.avg_pool2d(cy.to(torch.float32), 2)
+            if grad:
+                cx, cy = _Pool2Fn.apply(cx), _Pool2Fn.apply(cy)
+            else:
+                pl = lk if i == 1 else None
+                cx, cy = backend.pool2(cx, luma=pl), backend.pool2(cy, luma=pl)
         if grad:
             xf = cx.to(torch.float32).contiguous()
             yf = cy.to(torch.float32).contiguous()
             s, cs = _FusedSSIMCS.apply(xf, yf, win, shift, C1, C2)
         else:
             res = backend.ssim_forward(cx.detach(), cy.detach(), win, shift=shift, C1=C1,
-                                       C2=C2, luma=lk, want_cs=True)
+                                       C2=C2, luma=scale_lk, want_cs=True)
             s, cs = res["plane_s"], res["plane_cs"]
         terms.append((s if i == len(w) - 1 else cs).view(n, -1))
     stacked = torch.stack(terms).clamp_min(0.0)

@@ -288,6 +288,23 @@ FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N,
                                        int per_image, float* dx, float* dy,
                                        int device, void* stream);
 
+/* 2x2 mean pooling between MS-SSIM scales: out[n, c, i, j] = mean of the
+ * 2x2 block x[n, c, 2i:2i+2, 2j:2j+2], an odd last row / column dropped
+ * (F.avg_pool2d(x, 2)).  Replaces the reference's cast-then-pool
+ * (functional.py:717-725, used at :885 and :930) by one pass over x in its
+ * own dtype and strides.  luma (4 host doubles, nullable) projects RGB to
+ * one channel first, as for fa_b200_pixel_reduce.  out: float32 contiguous
+ * [N, C', H/2, W/2].  H and W must be at least 2. */
+FA_B200_API int fa_b200_pool2(const fa_view* x, const double* luma, float* out,
+                              int device, void* stream);
+
+/* Adjoint of fa_b200_pool2 (no luma): dx[n, c, h, w] = g[n, c, h/2, w/2] / 4,
+ * zero on a dropped odd row / column.  g: float32 [N, C, H/2, W/2];
+ * dx: float32 [N, C, H, W], every element written. */
+FA_B200_API int fa_b200_pool2_backward(const float* g, int N, int C, int H,
+                                       int W, float* dx, int device,
+                                       void* stream);
+
 /* Pixel reduction for callers that cannot allocate device memory.  No
  * counterpart in the reference: its reductions always take caller-allocated
  * scratch.  Callers such as host-application plugins that only receive frame

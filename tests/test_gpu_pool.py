@@ -1,0 +1,113 @@
+"""MS-SSIM pyramid pooling on the GPU: the 2x2 mean-pool kernel and its
+adjoint against torch's avg_pool2d (the reference's own pooling,
+functional.py:717-725), and MS-SSIM through it against the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import fa_oracle as O
+from conftest import natural_pair
+
+import frame_analytics_b200 as fa
+from frame_analytics_b200 import backend
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair(n, c, h, w, noise, seed):
+    """Stack of natural_pair planes shaped (n, c, h, w), uint8 values."""
+    ps = [natural_pair(h, w, seed=seed + i, noise=noise) for i in range(n * c)]
+    a = np.stack([p[0] for p in ps]).reshape(n, c, h, w).astype(np.uint8)
+    b = np.stack([p[1] for p in ps]).reshape(n, c, h, w).astype(np.uint8)
+    return a, b
+
+
+def _rand(shape, dt, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    if dt == torch.uint8:
+        return torch.randint(0, 256, shape, generator=g, dtype=torch.uint8).cuda()
+    return (torch.rand(shape, generator=g, dtype=torch.float64) * 255).to(dt).cuda()
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 2, 2), (2, 3, 37, 53), (1, 3, 64, 129), (3, 1, 131, 66)])
+@pytest.mark.parametrize("dt", [torch.uint8, torch.float16, torch.bfloat16, torch.float32])
+def test_pool2_bitwise_vs_avg_pool2d(shape, dt):
+    x = _rand(shape, dt)
+    got = backend.pool2(x)
+    ref = F.avg_pool2d(x.to(torch.float32), 2)
+    assert got.dtype == torch.float32 and got.shape == ref.shape
+    assert torch.equal(got, ref)
+
+
+def test_pool2_float64_input():
+    x = _rand((2, 2, 41, 30), torch.float64)
+    got = backend.pool2(x)
+    ref = F.avg_pool2d(x, 2).to(torch.float32)
+    torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-4)
+
+
+def test_pool2_strided_views():
+    x = _rand((2, 3, 80, 100), torch.uint8)
+    crop = x[:, :, 3:-5, 7:-2]
+    assert not crop.is_contiguous()
+    assert torch.equal(backend.pool2(crop), F.avg_pool2d(crop.float(), 2))
+    nhwc = _rand((2, 50, 60, 3), torch.float32).permute(0, 3, 1, 2)
+    assert torch.equal(backend.pool2(nhwc), F.avg_pool2d(nhwc.contiguous(), 2))
+
+
+@pytest.mark.parametrize("mode", ["bt601", "bt709"])
+def test_pool2_luma(mode):
+    x = _rand((2, 3, 45, 62), torch.uint8)
+    lum = fa.rgb_to_luma(x, mode, data_range=255.0)
+    ref = F.avg_pool2d(lum.to(torch.float32), 2)
+    from frame_analytics_b200.functional import _luma_k
+    got = backend.pool2(x, luma=_luma_k(mode, 255.0))
+    torch.testing.assert_close(got, ref, rtol=0, atol=2e-4)
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 2, 2), (2, 3, 37, 53), (1, 2, 64, 129)])
+def test_pool2_backward_bitwise(shape):
+    x = _rand(shape, torch.float32).requires_grad_(True)
+    y = F.avg_pool2d(x, 2)
+    g = torch.randn_like(y)
+    (ref,) = torch.autograd.grad(y, x, g)
+    got = backend.pool2_backward(g, shape)
+    assert torch.equal(got, ref)
+
+
+def test_pool2_rejects_bad_input():
+    with pytest.raises(Exception):
+        backend.pool2(_rand((1, 1, 1, 8), torch.float32))
+    with pytest.raises(Exception):
+        backend.pool2(_rand((1, 2, 8, 8), torch.uint8), luma=(0.3, 0.5, 0.2, 0.0))
+
+
+@pytest.mark.parametrize("luma", [None, True, "bt709"])
+@pytest.mark.parametrize("hw", [(176, 176), (193, 241)])
+def test_ms_ssim_vs_oracle(luma, hw):
+    a, b = _pair(2, 3, *hw, 12.0, seed=5)
+    got = fa.ms_ssim(torch.as_tensor(a).cuda(), torch.as_tensor(b).cuda(), luma=luma,
+                     reduction="none").cpu().numpy()
+    np.testing.assert_allclose(got, O.ms_ssim(a, b, luma=luma, reduction="none"), atol=5e-6)
+
+
+def test_ms_ssim_grad_matches_torch_pooling():
+    """Gradient through the pool kernels equals the one through avg_pool2d."""
+    a, b = _pair(1, 3, 180, 200, 10.0, seed=9)
+    x0 = torch.as_tensor(a, dtype=torch.float32).cuda() / 255
+    y = torch.as_tensor(b, dtype=torch.float32).cuda() / 255
+    x = x0.clone().requires_grad_(True)
+    fa.ms_ssim(x, y, data_range=1.0).backward()
+    xr = x0.clone().requires_grad_(True)
+    from frame_analytics_b200 import functional as fn
+    orig = fn._Pool2Fn.apply
+    try:
+        fn._Pool2Fn.apply = staticmethod(lambda t: F.avg_pool2d(t.float(), 2))
+        fa.ms_ssim(xr, y, data_range=1.0).backward()
+    finally:
+        fn._Pool2Fn.apply = orig
+    torch.testing.assert_close(x.grad, xr.grad, rtol=1e-5, atol=1e-9)
