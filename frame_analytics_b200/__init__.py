@@ -25,6 +25,7 @@ from .functional import (  # noqa: F401
     psnr,
     rgb_to_luma,
     set_compile_enabled,
+    set_fused_loss_grad,
     ssim,
 )
 from .modules import GMSD, L1, MSE, MSSSIM, PSNR, SSIM, Charbonnier, Huber  # noqa: F401
@@ -34,6 +35,7 @@ __version__ = "0.1.0"
 __all__ = [
     "mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber",
     "rgb_to_luma", "gaussian_window_1d", "set_compile_enabled",
+    "set_fused_loss_grad",
     "MSE", "PSNR", "SSIM", "MSSSIM", "GMSD", "L1", "Charbonnier", "Huber",
     "backend_status",
 ]

@@ -292,6 +292,44 @@ def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
     return dx, dy
 
 
+def ssim_loss_grad(x: torch.Tensor, y: torch.Tensor, win: Taps, *, shift: float,
+                   C1: float, C2: float, need_dx: bool = True, need_dy: bool = True,
+                   want_per_image: bool = False):
+    """SSIM means and the unit gradient of the batch-mean SSIM, one launch.
+    Returns ``(total, per_image or None, dx, dy)``; x, y float32 (N,C,H,W)."""
+    L = lib()
+    x = x.detach().to(torch.float32).contiguous()
+    y = y.detach().to(torch.float32).contiguous()
+    n, c, h, w = x.shape
+    k = win.k
+    if h - k + 1 <= 0 or w - k + 1 <= 0:
+        raise ValueError(f"image {(h, w)} smaller than window {k}x{k}")
+    dev = _dev(x)
+    nb = _cached_ws("ssim_lg", L.fa_b200_ssim_loss_grad_workspace_bytes, n, c, h, w, k, dev)
+    ws = workspace(x, nb)
+    total = _f64(x)
+    per_image = _f64(x, n) if want_per_image else None
+    dx = torch.empty_like(x) if need_dx else None
+    dy = torch.empty_like(y) if need_dy else None
+    _call(x, L.fa_b200_ssim_loss_grad, x.data_ptr(), y.data_ptr(), n, c, h, w, win.arr, k,
+          float(shift), float(C1), float(C2), ws.data_ptr(), ws.numel(), None,
+          _ptr(per_image), total.data_ptr(), _ptr(dx), _ptr(dy), dev, _stream(x))
+    return total, per_image, dx, dy
+
+
+def grad_scale(unit: torch.Tensor, g: torch.Tensor, *, per_image: bool,
+               mult: float = 1.0) -> torch.Tensor:
+    """``unit * g * mult`` (``g`` one scalar, or one value per image when
+    ``per_image``), a new float32 tensor; ``g`` stays on the device."""
+    L = lib()
+    n = unit.shape[0]
+    gd = g.detach().to(torch.float64).reshape(-1).contiguous()
+    out = torch.empty_like(unit)
+    _call(unit, L.fa_b200_grad_scale, unit.data_ptr(), unit.numel() // n, n, gd.data_ptr(),
+          int(bool(per_image)), float(mult), out.data_ptr(), _dev(unit), _stream(unit))
+    return out
+
+
 # --------------------------------------------------------------------------- #
 # GMSD
 # --------------------------------------------------------------------------- #

@@ -37,6 +37,13 @@ int gmsd_backward_impl(const float* x, const float* y, int N, int C, int H, int 
                        const double* mu, const double* sd, float* dx, float* dy, int device,
                        cudaStream_t st);
 
+size_t ssim_loss_grad_ws_bytes(int N, int C, int H, int W, int K, int device);
+int ssim_loss_grad_impl(const float* x, const float* y, int N, int C, int H, int W,
+                        const float* taps, int K, double shift, double C1, double C2, void* ws,
+                        size_t ws_bytes, double* out_plane_s, double* out_per_image,
+                        double* out_total, float* dx, float* dy, int device, cudaStream_t st);
+int grad_scale_impl(const float* in, long long per_image, int n, const double* s,
+                    int per_image_scale, double mult, float* out, int device, cudaStream_t st);
 int pool2_impl(const View& x, int dtype, const double* luma, float* out, int device,
                cudaStream_t st);
 int pool2_backward_impl(const float* g, int N, int C, int H, int W, float* dx, int device,
@@ -333,6 +340,27 @@ FA_B200_API int fa_b200_ssim_backward(const float* x, const float* y, int N, int
                        dy, device, static_cast<cudaStream_t>(stream));
 }
 
+FA_B200_API int fa_b200_ssim_loss_grad_workspace_bytes(int n, int c, int h, int w, int K,
+                                                       int device, size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
+  if (n <= 0 || c <= 0 || h - K + 1 <= 0 || w - K + 1 <= 0) return FA_E_SHAPE;
+  *out_bytes = ssim_loss_grad_ws_bytes(n, c, h, w, K, device);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_ssim_loss_grad(const float* x, const float* y, int N, int C, int H, int W,
+                                       const float* win, int K, double shift, double C1,
+                                       double C2, void* workspace, size_t workspace_bytes,
+                                       double* out_plane_s, double* out_per_image,
+                                       double* out_total, float* dx, float* dy, int device,
+                                       void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return ssim_loss_grad_impl(x, y, N, C, H, W, win, K, shift, C1, C2, workspace, workspace_bytes,
+                             out_plane_s, out_per_image, out_total, dx, dy, device,
+                             static_cast<cudaStream_t>(stream));
+}
+
 FA_B200_API int fa_b200_gmsd_workspace_bytes(int n, int c, int h, int w, int downsample,
                                              int device, size_t* out_bytes) {
   if (!out_bytes) return FA_E_ARG;
@@ -385,6 +413,14 @@ FA_B200_API int fa_b200_pool2_backward(const float* g, int N, int C, int H, int 
                                        int device, void* stream) {
   FAB_DEVICE_SCOPE(device);
   return pool2_backward_impl(g, N, C, H, W, dx, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_grad_scale(const float* in, long long per_image, int n, const double* s,
+                                   int per_image_scale, double mult, float* out, int device,
+                                   void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return grad_scale_impl(in, per_image, n, s, per_image_scale, mult, out, device,
+                         static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -47,6 +47,7 @@ struct SsimArgs {
   float w[12];        // Gaussian taps
   float2 w2[12];      // the same taps as {w, w} pairs for packed f32x2 FMAs
   int strips, chunks, RH;
+  int sym;            // the taps are symmetric: w[j] == w[K-1-j]
   // forward
   float* map_out;
   unsigned int* counter;
@@ -263,6 +264,14 @@ __device__ __forceinline__ void stage_store(float* sx, float* sy, const float (&
 // blurs
 // ---------------------------------------------------------------------------
 
+// Tap index: with SYM the window is known to be symmetric (w[j] == w[KW-1-j],
+// checked on the host), so only the first (KW+1)/2 taps are read and fewer
+// registers hold them.
+template <int KW, bool SYM>
+__device__ __forceinline__ constexpr int tap(int j) {
+  return (SYM && j > KW - 1 - j) ? KW - 1 - j : j;
+}
+
 // Horizontal blur of the (x', y') planes: KW adjacent outputs from 2KW-1
 // staged inputs; out[o].xy = sum_j w[j] * plane(o + j).
 template <int KW>
@@ -309,7 +318,7 @@ __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __res
 
 // Horizontal blur of two float components of float4 rows (backward scatter).
 // HALF selects .xy (0) or .zw (1); NC = 1 blurs only the first of the pair.
-template <int KW, int HALF, int NC>
+template <int KW, int HALF, int NC, bool SYM = false>
 __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __restrict__ sc,
                                            float4* __restrict__ out) {
   float2 acc[KW];
@@ -322,8 +331,8 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
       if (j >= 0 && j < KW) {
-        if (NC == 2) acc[o] = __ffma2_rn(p.w2[j], v, acc[o]);
-        else acc[o].x = fmaf(p.w[j], v.x, acc[o].x);
+        if (NC == 2) acc[o] = __ffma2_rn(p.w2[tap<KW, SYM>(j)], v, acc[o]);
+        else acc[o].x = fmaf(p.w2[tap<KW, SYM>(j)].x, v.x, acc[o].x);
       }
     }
   }
@@ -333,7 +342,7 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
 
 // Vertical blur over the register ring: the newest row sits in slot K, the
 // output row needs slots K+1 .. K+KW (mod KW), oldest first.
-template <int KW, int K, int NPL>
+template <int KW, int K, int NPL, bool SYM = false>
 __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[KW]) {
   // even and odd taps accumulate separately: twice the independent chains
   float2 a0 = make_float2(0.f, 0.f), b0 = make_float2(0.f, 0.f);
@@ -343,20 +352,21 @@ __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[
     const float4 h = ring[(K + 1 + j) % KW];
     float2& a = (j & 1) ? a1 : a0;
     float2& b = (j & 1) ? b1 : b0;
-    a = __ffma2_rn(p.w2[j], make_float2(h.x, h.y), a);
-    if (NPL == 4) b = __ffma2_rn(p.w2[j], make_float2(h.z, h.w), b);
-    else b.x = fmaf(p.w[j], h.z, b.x);
+    const float2 wj = p.w2[tap<KW, SYM>(j)];
+    a = __ffma2_rn(wj, make_float2(h.x, h.y), a);
+    if (NPL == 4) b = __ffma2_rn(wj, make_float2(h.z, h.w), b);
+    else b.x = fmaf(wj.x, h.z, b.x);
   }
   const float2 a = __fadd2_rn(a0, a1), b = __fadd2_rn(b0, b1);
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
 // Static-slot dispatch of vblur for a loop index k that the unroller resolves.
-template <int KW, int NPL>
+template <int KW, int NPL, bool SYM = false>
 __device__ __forceinline__ float4 vblur_at(const SsimArgs& p, const float4 (&ring)[KW], int k) {
   switch (k) {
 #define FAB_VB(KK) \
-  case KK: return vblur<KW, (KK < KW ? KK : 0), NPL>(p, ring);
+  case KK: return vblur<KW, (KK < KW ? KK : 0), NPL, SYM>(p, ring);
     FAB_VB(0) FAB_VB(1) FAB_VB(2) FAB_VB(3) FAB_VB(4) FAB_VB(5)
     FAB_VB(6) FAB_VB(7) FAB_VB(8) FAB_VB(9) FAB_VB(10)
 #undef FAB_VB
@@ -431,6 +441,41 @@ static inline SsimPlan plan_rows(int rows_total, int strips, int planes, int dev
   pl.RH = (rows_total + best_c - 1) / best_c;
   pl.chunks = (rows_total + pl.RH - 1) / pl.RH;
   return pl;
+}
+
+// Last block of a launch that accumulates SSIM sums (the forward kernel, and
+// the backward kernel in its fused forward mode): per-plane sums in a fixed
+// order, then per-image and batch means.
+static __device__ __noinline__ void ssim_fwd_finalize(const SsimArgs& p, int bpp) {
+  __shared__ double s_red[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const double npix = (double)p.Hout * (double)p.Wout;
+  for (int pl = wid; pl < p.P; pl += nw) {
+    double s = 0.0, c = 0.0;
+    for (int i = lane; i < bpp; i += 32) {
+      s += p.part_s[(long long)pl * bpp + i];
+      if (p.part_cs) c += p.part_cs[(long long)pl * bpp + i];
+    }
+    s = warp_sum(s);
+    c = warp_sum(c);
+    if (lane == 0) {
+      p.part_s[(long long)pl * bpp] = s;
+      if (p.out_plane_s) p.out_plane_s[pl] = s / npix;
+      if (p.out_plane_cs) p.out_plane_cs[pl] = c / npix;
+    }
+  }
+  __syncthreads();
+  __threadfence_block();
+  double t = 0.0;
+  for (int n = threadIdx.x; n < p.N; n += blockDim.x) {
+    double s = 0.0;
+    for (int c = 0; c < p.Cm; ++c) s += p.part_s[(long long)(n * p.Cm + c) * bpp];
+    if (p.out_per_image) p.out_per_image[n] = s / (npix * p.Cm);
+    t += s;
+  }
+  t = block_sum(t, s_red);
+  if (threadIdx.x == 0 && p.out_total) *p.out_total = t / (npix * p.Cm * (double)p.N);
 }
 
 }  // namespace fab

@@ -6,39 +6,6 @@
 
 namespace fab {
 
-// Last block: per-plane sums in a fixed order, then per-image and batch means.
-__device__ void ssim_fwd_finalize(const SsimArgs& p, int bpp) {
-  __shared__ double s_red[32];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int nw = blockDim.x >> 5;
-  const double npix = (double)p.Hout * (double)p.Wout;
-  for (int pl = wid; pl < p.P; pl += nw) {
-    double s = 0.0, c = 0.0;
-    for (int i = lane; i < bpp; i += 32) {
-      s += p.part_s[(long long)pl * bpp + i];
-      if (p.part_cs) c += p.part_cs[(long long)pl * bpp + i];
-    }
-    s = warp_sum(s);
-    c = warp_sum(c);
-    if (lane == 0) {
-      p.part_s[(long long)pl * bpp] = s;
-      if (p.out_plane_s) p.out_plane_s[pl] = s / npix;
-      if (p.out_plane_cs) p.out_plane_cs[pl] = c / npix;
-    }
-  }
-  __syncthreads();
-  __threadfence_block();
-  double t = 0.0;
-  for (int n = threadIdx.x; n < p.N; n += blockDim.x) {
-    double s = 0.0;
-    for (int c = 0; c < p.Cm; ++c) s += p.part_s[(long long)(n * p.Cm + c) * bpp];
-    if (p.out_per_image) p.out_per_image[n] = s / (npix * p.Cm);
-    t += s;
-  }
-  t = block_sum(t, s_red);
-  if (threadIdx.x == 0 && p.out_total) *p.out_total = t / (npix * p.Cm * (double)p.N);
-}
-
 template <typename T, int KW, bool CS, int STAGE>
 __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_constant__ SsimArgs p) {
   using G = Geo<KW>;

@@ -20,6 +20,7 @@ from . import backend
 __all__ = [
     "mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier",
     "huber", "rgb_to_luma", "gaussian_window_1d", "set_compile_enabled",
+    "set_fused_loss_grad",
     "MS_SSIM_WEIGHTS", "LUMA_COEFFS",
 ]
 
@@ -340,6 +341,51 @@ class _FusedSSIM(torch.autograd.Function):
                 None, None, None, None, None)
 
 
+class _SSIMLossGrad(torch.autograd.Function):
+    """Differentiable scalar / per-image SSIM computed together with its
+    gradient (one launch, no separate forward).  The kernel returns the
+    gradient of the batch-mean SSIM for an upstream gradient of 1; backward
+    only scales it: by ``g`` for the batch mean, by ``g[n] * N`` per image
+    for ``reduction='none'``.  The gradient is computed even if backward is
+    never called, so :func:`set_fused_loss_grad` turns this off for callers
+    that evaluate with gradients enabled but rarely backpropagate."""
+
+    @staticmethod
+    def forward(ctx, x, y, win, shift, C1, C2, mode, nx, ny):
+        total, per_image, dx, dy = backend.ssim_loss_grad(
+            x, y, win, shift=shift, C1=C1, C2=C2, need_dx=nx, need_dy=ny,
+            want_per_image=(mode == "none"))
+        ctx.unit = (dx, dy)
+        ctx.mode, ctx.n = mode, x.shape[0]
+        return per_image if mode == "none" else total
+
+    @staticmethod
+    def backward(ctx, g):
+        _reject_double_backward()
+        per_image = ctx.mode == "none"
+        mult = float(ctx.n) if per_image else 1.0
+        dx, dy = ctx.unit
+        nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+
+        def scaled(u):
+            return backend.grad_scale(u, g, per_image=per_image, mult=mult)
+
+        return (scaled(dx) if (nx and dx is not None) else None,
+                scaled(dy) if (ny and dy is not None) else None,
+                None, None, None, None, None, None, None)
+
+
+_fused_loss_grad = True
+
+
+def set_fused_loss_grad(enabled: bool) -> None:
+    """Compute the SSIM gradient in the same pass as the value whenever an
+    input requires grad (default on).  Off: the forward computes the value
+    only and the backward recomputes the moments."""
+    global _fused_loss_grad
+    _fused_loss_grad = bool(enabled)
+
+
 def _matlab_downsample(x: torch.Tensor, f: int) -> torch.Tensor:
     """MATLAB ssim.m's automatic box downsample (functional.py:575-586)."""
     if f <= 1:
@@ -393,6 +439,9 @@ def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None
         xf = x4 if x4.dtype == torch.float32 else x4.to(torch.float32)
         yf = y4 if y4.dtype == torch.float32 else y4.to(torch.float32)
         m = "map" if return_map else reduction
+        if _fused_loss_grad and m != "map":
+            return _SSIMLossGrad.apply(xf.contiguous(), yf.contiguous(), win, shift, C1, C2, m,
+                                       xf.requires_grad, yf.requires_grad)
         return _FusedSSIM.apply(xf.contiguous(), yf.contiguous(), win, shift, C1, C2, m)
 
     x4, y4 = x4.detach(), y4.detach()

@@ -225,6 +225,45 @@ FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y,
                              double* out_plane_cs, double* out_per_image,
                              double* out_total, int device, void* stream);
 
+/* SSIM loss value and gradient in one pass (training steps).  No single
+ * counterpart in the reference: it runs its forward (fa_cuda_ssim,
+ * fa_cuda.cu:1167-1283) and later its backward (fa_cuda_ssim_backward,
+ * fa_cuda.cu:1299-1414), both reading x and y and recomputing the moments.
+ * Since d(mean SSIM)/dx is linear in the upstream scalar, this call returns
+ * the SSIM means (as fa_b200_ssim: out_plane_s [N*C], out_per_image [N],
+ * out_total [1], each nullable) together with dx / dy = the gradient of the
+ * batch-mean SSIM (out_total) for an upstream gradient of 1; the caller
+ * multiplies by its real upstream gradient.  Per image n,
+ * d(out_per_image[n])/dx = N * dx restricted to image n.
+ * x, y: float32 contiguous [N, C, H, W]; dx / dy nullable (not both);
+ * taps_host: host memory.  workspace: device memory of the size
+ * fa_b200_ssim_loss_grad_workspace_bytes reports, zeroed once before first
+ * use and reused only by calls serialised on one stream. */
+FA_B200_API int fa_b200_ssim_loss_grad_workspace_bytes(int n, int c, int h,
+                                                       int w, int K,
+                                                       int device,
+                                                       size_t* out_bytes);
+FA_B200_API int fa_b200_ssim_loss_grad(const float* x, const float* y, int N,
+                                       int C, int H, int W,
+                                       const float* taps_host, int K,
+                                       double shift, double C1, double C2,
+                                       void* workspace, size_t workspace_bytes,
+                                       double* out_plane_s,
+                                       double* out_per_image,
+                                       double* out_total, float* dx,
+                                       float* dy, int device, void* stream);
+
+/* out = in * (s * mult), elementwise over n images of per_image floats: s is
+ * one device double (per_image_scale = 0) or n of them (one per image).
+ * Applies the upstream gradient to the unit gradient fa_b200_ssim_loss_grad
+ * returns (mult = N for per-image upstream gradients).  No counterpart in
+ * the reference, whose backward receives the upstream gradient directly.
+ * in and out may alias. */
+FA_B200_API int fa_b200_grad_scale(const float* in, long long per_image, int n,
+                                   const double* s, int per_image_scale,
+                                   double mult, float* out, int device,
+                                   void* stream);
+
 /* Fused SSIM backward, one launch, no scratch.  Replaces fa_cuda_ssim_backward
  * and fa_cuda_ssim_cs_backward (fa_cuda.cu:1299-1414, backend.py:429-455).
  * Upstream gradient, exactly one form:

@@ -229,3 +229,90 @@ def test_ms_ssim_backward_vs_finite_differences():
         m[t] -= h
         fd = (O.ms_ssim(a, p, data_range=1.0) - O.ms_ssim(a, m, data_range=1.0)) / (2 * h)
         assert abs(g[t] - fd) <= 2e-3 * abs(fd) + 1e-8
+
+
+@pytest.mark.parametrize("reduction", ["mean", "none"])
+@pytest.mark.parametrize("hw", [(67, 90), (120, 129)])
+@pytest.mark.parametrize("which", ["x", "y", "both"])
+def test_fused_loss_grad_matches_two_pass(reduction, hw, which):
+    """Value + unit gradient in one launch (then scaled by the upstream
+    gradient) equals the forward followed by the separate backward."""
+    g = torch.Generator().manual_seed(3)
+    a = torch.rand((2, 3) + hw, generator=g).cuda()
+    b = (a + 0.05 * torch.randn(a.shape, generator=g).cuda()).clamp(0, 1)
+    up = torch.randn(2, generator=g, dtype=torch.float64).cuda() if reduction == "none" else None
+    res = {}
+    for fused in (True, False):
+        fa.set_fused_loss_grad(fused)
+        try:
+            x = a.clone().requires_grad_(which in ("x", "both"))
+            y = b.clone().requires_grad_(which in ("y", "both"))
+            v = fa.ssim(x, y, data_range=1.0, reduction=reduction)
+            (1.0 - v).sum().backward() if up is None else (v * up).sum().backward()
+            res[fused] = (v.detach(), x.grad, y.grad)
+        finally:
+            fa.set_fused_loss_grad(True)
+    (v1, gx1, gy1), (v0, gx0, gy0) = res[True], res[False]
+    torch.testing.assert_close(v1, v0, rtol=0, atol=1e-9)
+    for g1, g0 in ((gx1, gx0), (gy1, gy0)):
+        assert (g1 is None) == (g0 is None)
+        if g1 is not None:
+            # the two paths apply the upstream gradient at different points:
+            # rounding differs, relative to the gradient's scale
+            torch.testing.assert_close(g1, g0, rtol=1e-5, atol=1e-5 * float(g0.abs().max()))
+
+
+@pytest.mark.parametrize("shape", [(3, 2, 17, 31), (2, 3, 64, 96)])
+@pytest.mark.parametrize("per_image", [False, True])
+def test_grad_scale(shape, per_image):
+    from frame_analytics_b200 import backend
+    u = torch.randn(shape, device="cuda")
+    g = torch.randn(shape[0] if per_image else (), dtype=torch.float64, device="cuda")
+    got = backend.grad_scale(u, g, per_image=per_image, mult=shape[0])
+    f = (g * shape[0]).to(torch.float32)
+    ref = u * (f.view(-1, 1, 1, 1) if per_image else f)
+    assert torch.equal(got, ref)
+
+
+def _torch_ssim_mean(x, y, w, shift, C1, C2):
+    """float64 torch SSIM batch mean with an arbitrary separable window."""
+    k = w.numel()
+    xs, ys = x - shift, y - shift
+    n, c, h, wd = x.shape
+
+    def blur(t):
+        t = t.reshape(n * c, 1, h, wd)
+        t = torch.nn.functional.conv2d(t, w.view(1, 1, k, 1))
+        t = torch.nn.functional.conv2d(t, w.view(1, 1, 1, k))
+        return t
+    ux, uy = blur(xs), blur(ys)
+    sxx = blur(xs * xs) - ux * ux
+    syy = blur(ys * ys) - uy * uy
+    sxy = blur(xs * ys) - ux * uy
+    mx, my = ux + shift, uy + shift
+    s = ((2 * mx * my + C1) * (2 * sxy + C2)) / ((mx * mx + my * my + C1) * (sxx + syy + C2))
+    return s.mean()
+
+
+@pytest.mark.parametrize("taps", [[0.1, 0.2, 0.4, 0.2, 0.1], [0.05, 0.15, 0.5, 0.2, 0.1],
+                                  [0.2, 0.3, 0.5]])
+@pytest.mark.parametrize("fused", [True, False])
+def test_backward_symmetric_and_asymmetric_windows(taps, fused):
+    """Symmetric windows take the warp-specialised kernel, asymmetric ones the
+    general one; both match float64 torch autograd."""
+    from frame_analytics_b200 import backend
+    g = torch.Generator().manual_seed(11)
+    a = torch.rand((2, 2, 40, 72), generator=g).cuda()
+    b = (a + 0.05 * torch.randn(a.shape, generator=g).cuda()).clamp(0, 1)
+    win = backend.Taps(taps)
+    C1, C2, shift = 1e-4, 9e-4, 0.5
+    if fused:
+        _, _, dx, dy = backend.ssim_loss_grad(a, b, win, shift=shift, C1=C1, C2=C2)
+    else:
+        one = torch.ones((), device="cuda")
+        dx, dy = backend.ssim_backward(a, b, win, shift=shift, C1=C1, C2=C2, gscalar=one)
+    xd, yd = a.double().requires_grad_(True), b.double().requires_grad_(True)
+    wt = torch.tensor(taps, dtype=torch.float64, device="cuda")
+    _torch_ssim_mean(xd, yd, wt, shift, C1, C2).backward()
+    for got, ref in ((dx, xd.grad), (dy, yd.grad)):
+        torch.testing.assert_close(got.double(), ref, rtol=1e-3, atol=2e-3 * float(ref.abs().max()))
