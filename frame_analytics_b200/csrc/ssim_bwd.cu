@@ -190,8 +190,8 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
     {
       const float4* rc = sC + warp * B::SCW + lane * KW;
       float4* out = sH + warp * G::NT + lane * KW;
-      hblur_pair<KW, 0, 2>(p, rc, out);
-      hblur_pair<KW, 1, NPL - 2>(p, rc, out);
+      hblur_pair<KW, 0, 2, false, true>(p, rc, out);  // reversed window: adjoint
+      hblur_pair<KW, 1, NPL - 2, false, true>(p, rc, out);
     }
     if constexpr (TMA) mbar_wait(&s_bar[1], m & 1);
     __syncthreads();
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(32 * KW, 1) ssim_bwd_kernel(const __grid_const
       const int L = m * KW + k;
       const int r = i0 + L - (KW - 1);  // gradient row
       if (L >= 2 * (KW - 1) && r < r0 + rows && d_ok) {
-        const float4 s = vblur_at<KW, NPL>(p, ring2, k);
+        const float4 s = vblur_at<KW, NPL, false, true>(p, ring2, k);
         const long long off = (long long)r * p.W + dcol;
         float xs, ys;
         if constexpr (TMA) {

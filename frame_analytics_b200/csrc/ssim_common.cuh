@@ -272,6 +272,13 @@ __device__ __forceinline__ constexpr int tap(int j) {
   return (SYM && j > KW - 1 - j) ? KW - 1 - j : j;
 }
 
+// Transposed (adjoint) blurs correlate with the reversed window; FLIP selects
+// w[KW-1-j].  For a symmetric window both orders give the same taps.
+template <int KW, bool SYM, bool FLIP>
+__device__ __forceinline__ constexpr int tapf(int j) {
+  return tap<KW, SYM>(FLIP ? KW - 1 - j : j);
+}
+
 // Horizontal blur of the (x', y') planes: KW adjacent outputs from 2KW-1
 // staged inputs; out[o].xy = sum_j w[j] * plane(o + j).
 template <int KW>
@@ -318,7 +325,7 @@ __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __res
 
 // Horizontal blur of two float components of float4 rows (backward scatter).
 // HALF selects .xy (0) or .zw (1); NC = 1 blurs only the first of the pair.
-template <int KW, int HALF, int NC, bool SYM = false>
+template <int KW, int HALF, int NC, bool SYM = false, bool FLIP = false>
 __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __restrict__ sc,
                                            float4* __restrict__ out) {
   float2 acc[KW];
@@ -331,8 +338,8 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
       if (j >= 0 && j < KW) {
-        if (NC == 2) acc[o] = __ffma2_rn(p.w2[tap<KW, SYM>(j)], v, acc[o]);
-        else acc[o].x = fmaf(p.w2[tap<KW, SYM>(j)].x, v.x, acc[o].x);
+        if (NC == 2) acc[o] = __ffma2_rn(p.w2[tapf<KW, SYM, FLIP>(j)], v, acc[o]);
+        else acc[o].x = fmaf(p.w2[tapf<KW, SYM, FLIP>(j)].x, v.x, acc[o].x);
       }
     }
   }
@@ -342,7 +349,7 @@ __device__ __forceinline__ void hblur_pair(const SsimArgs& p, const float4* __re
 
 // Vertical blur over the register ring: the newest row sits in slot K, the
 // output row needs slots K+1 .. K+KW (mod KW), oldest first.
-template <int KW, int K, int NPL, bool SYM = false>
+template <int KW, int K, int NPL, bool SYM = false, bool FLIP = false>
 __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[KW]) {
   // even and odd taps accumulate separately: twice the independent chains
   float2 a0 = make_float2(0.f, 0.f), b0 = make_float2(0.f, 0.f);
@@ -352,7 +359,7 @@ __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[
     const float4 h = ring[(K + 1 + j) % KW];
     float2& a = (j & 1) ? a1 : a0;
     float2& b = (j & 1) ? b1 : b0;
-    const float2 wj = p.w2[tap<KW, SYM>(j)];
+    const float2 wj = p.w2[tapf<KW, SYM, FLIP>(j)];
     a = __ffma2_rn(wj, make_float2(h.x, h.y), a);
     if (NPL == 4) b = __ffma2_rn(wj, make_float2(h.z, h.w), b);
     else b.x = fmaf(wj.x, h.z, b.x);
@@ -362,11 +369,11 @@ __device__ __forceinline__ float4 vblur(const SsimArgs& p, const float4 (&ring)[
 }
 
 // Static-slot dispatch of vblur for a loop index k that the unroller resolves.
-template <int KW, int NPL, bool SYM = false>
+template <int KW, int NPL, bool SYM = false, bool FLIP = false>
 __device__ __forceinline__ float4 vblur_at(const SsimArgs& p, const float4 (&ring)[KW], int k) {
   switch (k) {
 #define FAB_VB(KK) \
-  case KK: return vblur<KW, (KK < KW ? KK : 0), NPL, SYM>(p, ring);
+  case KK: return vblur<KW, (KK < KW ? KK : 0), NPL, SYM, FLIP>(p, ring);
     FAB_VB(0) FAB_VB(1) FAB_VB(2) FAB_VB(3) FAB_VB(4) FAB_VB(5)
     FAB_VB(6) FAB_VB(7) FAB_VB(8) FAB_VB(9) FAB_VB(10)
 #undef FAB_VB
