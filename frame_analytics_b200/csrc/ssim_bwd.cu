@@ -19,6 +19,8 @@
 // upstream gradient of 1.  A training step then needs no separate forward
 // launch; the caller scales the unit gradient when the real upstream
 // gradient arrives.
+#include <type_traits>
+
 #include "ssim_common.cuh"
 
 namespace fab {
@@ -397,41 +399,52 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
       __syncthreads();
       if (m < iters) {
         if (m + 1 < iters) stage_tma<float, KW>(p, pn, pc, i0 + (m + 1) * KW, xs0, sX, sY, &s_bar);
+        const int o0 = i0 + m * KW - (KW - 1);  // moment row of slot 0
         float fs = 0.f;
+        // CHK: per-row tests; interior batches (every row a valid, owned
+        // moment row) skip them
+        auto rows_step = [&](auto chk) {
+          constexpr bool CHK = decltype(chk)::value;
 #pragma unroll
-        for (int k = 0; k < KW; ++k) {
-          ring[k] = sH[k * NT + t];
-          const int L = m * KW + k;
-          const int o = i0 + L - (KW - 1);  // moment row
-          float4 cf = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (L >= KW - 1 && o >= 0 && o < p.Hout && q_ok) {
-            const Moments mo = moments(p, vblur_at<KW, 4, true>(p, ring, k));
-            const float inv = 1.0f / (mo.B1 * mo.B2);
-            const float iB1 = mo.B2 * inv;
-            const float iB2 = mo.B1 * inv;
-            const float S = mo.A1 * mo.A2 * inv;
-            const float kk = 2.f * mo.A2 * inv;
-            if (FWD && own_col && o >= r0 && o < r0 + rows) fs += S;
-            float g = gS, bb, cc;
-            if (GMODE == G_MAP)
-              g = __ldg(p.dmap + (long long)plane * p.Hout * p.Wout + (long long)o * p.Wout + q);
-            if (GMODE == G_PLANE) {
-              const float CS = mo.A2 * iB2;
-              bb = -(g * S + gCS * CS) * iB2;
-              cc = 2.f * (g * mo.A1 * iB1 + gCS) * iB2;
-            } else {
-              bb = -g * S * iB2;
-              cc = 2.f * g * mo.A1 * inv;
+          for (int k = 0; k < KW; ++k) {
+            ring[k] = sH[k * NT + t];
+            const int o = o0 + k;
+            float4 cf = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (q_ok && (!CHK || (m * KW + k >= KW - 1 && o >= 0 && o < p.Hout))) {
+              const Moments mo = moments(p, vblur_at<KW, 4, true>(p, ring, k));
+              // one approximate reciprocal (a few ulp) serves S, cs and the
+              // coefficients
+              const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
+              const float iB1 = mo.B2 * inv;
+              const float iB2 = mo.B1 * inv;
+              const float S = mo.A1 * mo.A2 * inv;
+              const float kk = 2.f * mo.A2 * inv;
+              if (FWD && own_col && (!CHK || (o >= r0 && o < r0 + rows))) fs += S;
+              float g = gS, bb, cc;
+              if (GMODE == G_MAP)
+                g = __ldg(p.dmap + (long long)plane * p.Hout * p.Wout + (long long)o * p.Wout + q);
+              if (GMODE == G_PLANE) {
+                const float CS = mo.A2 * iB2;
+                bb = -(g * S + gCS * CS) * iB2;
+                cc = 2.f * (g * mo.A1 * iB1 + gCS) * iB2;
+              } else {
+                bb = -g * S * iB2;
+                cc = 2.f * g * mo.A1 * inv;
+              }
+              cf.x = bb;
+              cf.y = cc;
+              // both first-moment terms, whichever gradients are stored: the
+              // uniform four-component layout compiles without spills
+              cf.z = g * kk * (mo.my - mo.mx * mo.A1 * iB1) - 2.f * bb * mo.ux - cc * mo.uy;
+              cf.w = g * kk * (mo.mx - mo.my * mo.A1 * iB1) - 2.f * bb * mo.uy - cc * mo.ux;
             }
-            cf.x = bb;
-            cf.y = cc;
-            // both first-moment terms, whichever gradients are stored: the
-            // uniform four-component layout compiles without spills
-            cf.z = g * kk * (mo.my - mo.mx * mo.A1 * iB1) - 2.f * bb * mo.ux - cc * mo.uy;
-            cf.w = g * kk * (mo.mx - mo.my * mo.A1 * iB1) - 2.f * bb * mo.uy - cc * mo.ux;
+            sC[k * B::SCW + t] = cf;
           }
-          sC[k * B::SCW + t] = cf;
-        }
+        };
+        const bool interior = m >= 1 && o0 >= 0 && o0 + KW - 1 < p.Hout &&
+                              (!FWD || (o0 >= r0 && o0 + KW - 1 < r0 + rows));
+        if (interior) rows_step(std::false_type{});
+        else rows_step(std::true_type{});
         if constexpr (FWD) acc_s += (double)fs;
       }
       __syncthreads();
@@ -450,20 +463,26 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
       }
       __syncthreads();
       if (m >= 1) {
+        const int rb = i0 + (m - 1) * KW - (KW - 1);  // gradient row of slot 0
+        const long long off0 = pbase + (long long)rb * p.W + dcol;
+        auto rows_step = [&](auto chk) {
+          constexpr bool CHK = decltype(chk)::value;
 #pragma unroll
-        for (int k = 0; k < KW; ++k) {
-          ring[k] = sS[k * NT + t];
-          const int L = (m - 1) * KW + k;
-          const int r = i0 + L - (KW - 1);  // gradient row
-          if (L >= 2 * (KW - 1) && r < r0 + rows && d_ok) {
-            const float4 sv = vblur_at<KW, 4, true>(p, ring, k);
-            const long long off = pbase + (long long)r * p.W + dcol;
-            const float xs = __ldg(X + off) - p.shift;
-            const float ys = __ldg(Y + off) - p.shift;
-            if (p.dx) p.dx[off] = fmaf(2.f * xs, sv.x, fmaf(ys, sv.y, sv.z));
-            if (p.dy) p.dy[off] = fmaf(2.f * ys, sv.x, fmaf(xs, sv.y, sv.w));
+          for (int k = 0; k < KW; ++k) {
+            ring[k] = sS[k * NT + t];
+            if (d_ok && (!CHK || ((m - 1) * KW + k >= 2 * (KW - 1) && rb + k < r0 + rows))) {
+              const float4 sv = vblur_at<KW, 4, true>(p, ring, k);
+              const long long off = off0 + (long long)k * p.W;
+              const float xs = __ldg(X + off) - p.shift;
+              const float ys = __ldg(Y + off) - p.shift;
+              if (p.dx) p.dx[off] = fmaf(2.f * xs, sv.x, fmaf(ys, sv.y, sv.z));
+              if (p.dy) p.dy[off] = fmaf(2.f * ys, sv.x, fmaf(xs, sv.y, sv.w));
+            }
           }
-        }
+        };
+        const bool interior = (m - 1) * KW >= 2 * (KW - 1) && rb + KW - 1 < r0 + rows;
+        if (interior) rows_step(std::false_type{});
+        else rows_step(std::true_type{});
       }
       __syncthreads();
     }
