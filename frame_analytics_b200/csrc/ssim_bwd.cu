@@ -277,7 +277,7 @@ __device__ __forceinline__ void hblur_raw_part(const SsimArgs& p, const float* _
     const float xv = sx[q], yv = sy[q];
     const float dv = xv - yv;
     const float2 c = __fadd2_rn(make_float2(xv, yv), nsh);  // shifted x', y'
-    const float2 v = make_float2(c.x * c.y, dv * dv);
+    const float2 v = __fmul2_rn(make_float2(c.x, dv), make_float2(c.y, dv));  // x'y', (x'-y')^2
 #pragma unroll
     for (int o = 0; o < NO; ++o) {
       const int j = q - (O0 + o);
@@ -377,7 +377,10 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
   float4 ring[KW];
 #pragma unroll
   for (int k = 0; k < KW; ++k) ring[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  double acc_s = 0.0;
+  // per-thread float partial of the owned SSIM values (at most a column of
+  // one chunk: relative rounding ~1e-7, far below the metric's tolerance;
+  // block and plane sums are double)
+  float acc_hi = 0.f;
 
   if (grpA) {
     // ---------------- group A: moments -> coefficients ----------------
@@ -445,7 +448,7 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
                               (!FWD || (o0 >= r0 && o0 + KW - 1 < r0 + rows));
         if (interior) rows_step(std::false_type{});
         else rows_step(std::true_type{});
-        if constexpr (FWD) acc_s += (double)fs;
+        if constexpr (FWD) acc_hi += fs;
       }
       __syncthreads();
     }
@@ -489,7 +492,7 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
   }
   if constexpr (FWD) {
     const int bpp = p.strips * p.chunks;
-    acc_s = block_sum(acc_s, s_red);
+    const double acc_s = block_sum((double)acc_hi, s_red);
     if (threadIdx.x == 0) p.part_s[(long long)plane * bpp + blockIdx.y * p.strips + blockIdx.x] = acc_s;
     if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag))
       ssim_fwd_finalize(p, bpp);
