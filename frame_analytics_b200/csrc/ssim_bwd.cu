@@ -277,7 +277,7 @@ __device__ __forceinline__ void hblur_raw_part(const SsimArgs& p, const float* _
     const float xv = sx[q], yv = sy[q];
     const float dv = xv - yv;
     const float2 c = __fadd2_rn(make_float2(xv, yv), nsh);  // shifted x', y'
-    const float2 v = __fmul2_rn(make_float2(c.x, dv), make_float2(c.y, dv));  // x'y', (x'-y')^2
+    const float2 v = make_float2(c.x * c.y, dv * dv);  // x'y', (x'-y')^2
 #pragma unroll
     for (int o = 0; o < NO; ++o) {
       const int j = q - (O0 + o);
