@@ -463,6 +463,14 @@ def run_ours(args):
         extra["ssim_u8_fwd"] = {"workload": "SSIM fwd uint8 8x3x1080x1920, L2 flushed by a 256 MB read",
                                 "ms": sm, "Gpixel/s": int(np.prod(PIX_SHAPE)) / (sm / 1e3) / 1e9,
                                 "GB/s": pbytes / (sm / 1e3) / 1e9}
+        # SSIM + MSE + PSNR of the same pair: one fused launch
+        fm = timed_stream(lambda: fa.metrics(xu, yu, ("mse", "psnr", "ssim")), ev, flush,
+                          reps=max(5, args.steps // 2))
+        extra["ssim_mse_psnr_u8"] = {
+            "workload": "SSIM + MSE + PSNR uint8 8x3x1080x1920 in one launch (fa.metrics), "
+                        "L2 flushed by a 256 MB read",
+            "ms": fm, "Gpixel/s": int(np.prod(PIX_SHAPE)) / (fm / 1e3) / 1e9,
+            "separate_ms": sm + pm}
         # config 3: MS-SSIM forward, 5 scales, uint8 input read in place
         ca, cb = u8_pair(PIX_SHAPE, 8.0, 0)
         xm, ym = torch.from_numpy(ca).to(dev), torch.from_numpy(cb).to(dev)

@@ -25,17 +25,19 @@ from .functional import (  # noqa: F401
     psnr,
     rgb_to_luma,
     set_compile_enabled,
+    metrics,
     set_fused_loss_grad,
     ssim,
 )
-from .modules import GMSD, L1, MSE, MSSSIM, PSNR, SSIM, Charbonnier, Huber  # noqa: F401
+from .modules import (GMSD, L1, MSE, MSSSIM, PSNR, SSIM, Charbonnier, Huber,  # noqa: F401
+                      StreamingMetrics)
 
 __version__ = "0.1.0"
 
 __all__ = [
     "mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber",
     "rgb_to_luma", "gaussian_window_1d", "set_compile_enabled",
-    "set_fused_loss_grad",
+    "set_fused_loss_grad", "metrics", "StreamingMetrics",
     "MSE", "PSNR", "SSIM", "MSSSIM", "GMSD", "L1", "Charbonnier", "Huber",
     "backend_status",
 ]

@@ -105,6 +105,8 @@ PROTOTYPES = {
                               _vp, _vp, _i, _vp],
     "fa_b200_pixel_backward": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _vp, _i,
                                _vp, _vp, _i, _vp],
+    "fa_b200_ssim_mse": [_pview, _pview, _vp, _i, _d, _d, _d, _d, _vp, _sz, _vp, _vp, _vp,
+                         _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "fa_b200_ssim_loss_grad_workspace_bytes": [_i, _i, _i, _i, _i, _i, _vp],
     "fa_b200_ssim_loss_grad": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _d, _d, _vp, _sz,
                                _vp, _vp, _vp, _vp, _vp, _i, _vp],

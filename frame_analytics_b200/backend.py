@@ -264,6 +264,35 @@ def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
     return res
 
 
+def ssim_mse(x: torch.Tensor, y: torch.Tensor, win: Taps, *, shift: float, C1: float,
+             C2: float, psnr_bias: float, per_image: bool) -> dict:
+    """SSIM, MSE and PSNR from one read of the frame pair (one launch).
+    Returns a dict of float64 tensors, (N,) when ``per_image`` else 0-d; uint8
+    input also gives the exact per-image sums of squared differences."""
+    L = lib()
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    k = win.k
+    if vx.h - k + 1 <= 0 or vx.w - k + 1 <= 0:
+        raise ValueError(f"image {(vx.h, vx.w)} smaller than window {k}x{k}")
+    dev = _dev(x)
+    nb = _cached_ws("ssim", L.fa_b200_ssim_workspace_bytes, vx.n, vx.c, vx.h, vx.w, k, dev)
+    ws = workspace(x, nb)
+    shape = (vx.n,) if per_image else ()
+    res = {"ssim": _f64(x, *shape), "mse": _f64(x, *shape), "psnr": _f64(x, *shape)}
+    res["ssd"] = (torch.empty(vx.n, dtype=torch.int64, device=x.device)
+                  if x.dtype == torch.uint8 else None)
+    pi = (lambda t: t) if per_image else (lambda t: None)
+    tot = (lambda t: None) if per_image else (lambda t: t)
+    _call(x, L.fa_b200_ssim_mse, ctypes.byref(vx), ctypes.byref(vy), win.arr, k,
+          float(shift), float(C1), float(C2), float(psnr_bias), ws.data_ptr(), ws.numel(),
+          None, _ptr(pi(res["ssim"])), _ptr(tot(res["ssim"])), _ptr(pi(res["mse"])),
+          _ptr(tot(res["mse"])), _ptr(pi(res["psnr"])), _ptr(tot(res["psnr"])),
+          _ptr(res["ssd"]), dev, _stream(x))
+    return res
+
+
 def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                   shift: float, C1: float, C2: float,
                   dmap: Optional[torch.Tensor] = None,

@@ -19,7 +19,8 @@ size_t pixel_ws_bytes(int n_images, int device);
 int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, const float* win,
                   int K, double shift, double C1, double C2, float* map_out, void* ws,
                   size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
-                  double* out_per_image, double* out_total, int device, cudaStream_t st);
+                  double* out_per_image, double* out_total, int device, cudaStream_t st,
+                  const SqOut* sq = nullptr);
 size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device);
 int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* win,
                   int K, double shift, double C1, double C2, const float* dmap,
@@ -338,6 +339,23 @@ FA_B200_API int fa_b200_ssim_backward(const float* x, const float* y, int N, int
   FAB_DEVICE_SCOPE(device);
   return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, dL_dmap, g_scalar, gs, gcs, dx,
                        dy, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_ssim_mse(const fa_view* x, const fa_view* y, const float* win, int K,
+                                 double shift, double C1, double C2, double psnr_bias,
+                                 void* workspace, size_t workspace_bytes, double* out_plane_s,
+                                 double* out_per_image, double* out_total,
+                                 double* out_mse_per_image, double* out_mse_total,
+                                 double* out_psnr_per_image, double* out_psnr_total,
+                                 uint64_t* out_ssd_per_image, int device, void* stream) {
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  const SqOut sq{psnr_bias, out_mse_per_image, out_mse_total, out_psnr_per_image,
+                 out_psnr_total, reinterpret_cast<unsigned long long*>(out_ssd_per_image)};
+  return ssim_fwd_impl(to_view(*x), to_view(*y), x->dtype, nullptr, win, K, shift, C1, C2,
+                       nullptr, workspace, workspace_bytes, out_plane_s, nullptr, out_per_image,
+                       out_total, device, static_cast<cudaStream_t>(stream), &sq);
 }
 
 FA_B200_API int fa_b200_ssim_loss_grad_workspace_bytes(int n, int c, int h, int w, int K,

@@ -150,6 +150,17 @@ struct DeviceScope {
 
 int sm_count(int device);
 
+// Host-side request for the squared-difference outputs of the fused SSIM
+// forward (SSIM + MSE/PSNR from one read of the frame pair).
+struct SqOut {
+  double psnr_bias;
+  double* mse_per_image;
+  double* mse_total;
+  double* psnr_per_image;
+  double* psnr_total;
+  unsigned long long* ssd_per_image;  // uint8 input only
+};
+
 }  // namespace fab
 
 #define FAB_TRY(EXPR)                                   \

@@ -59,6 +59,58 @@ __global__ void __launch_bounds__(256) pool2_kernel(PoolArgs p) {
   }
 }
 
+// Vector path (no luma; 16-byte aligned base and strides; W a multiple of
+// V = 16 / sizeof(T)): one thread reads a 16-byte chunk of each of the two
+// rows and writes V/2 pooled values, float4 stores when the output rows are
+// 16-byte aligned.  The sum order (a + b + c + d, row-major in the block) is
+// that of the scalar path.
+template <typename T>
+struct Vec16 {
+  static constexpr int V = 16 / (int)sizeof(T);
+  __device__ static __forceinline__ void load(const T* p, float (&v)[V]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = Ld<T>::f(e[i]);
+  }
+};
+
+template <typename T, bool VST>
+__global__ void __launch_bounds__(256) pool2_vec_kernel(PoolArgs p) {
+  constexpr int V = Vec16<T>::V;
+  const T* X = reinterpret_cast<const T*>(p.x);
+  const int nch = p.W / V;  // chunks per row
+  const long long total = (long long)p.N * p.C * p.Hp * nch;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ch = (int)(i % nch);
+    long long r = i / nch;
+    const int hp = (int)(r % p.Hp);
+    r /= p.Hp;
+    const int c = (int)(r % p.C);
+    const int n = (int)(r / p.C);
+    const T* a = X + (long long)n * p.sn + (long long)c * p.sc + (long long)(2 * hp) * p.sh +
+                 (long long)ch * V;
+    float u[V], w[V];
+    Vec16<T>::load(a, u);
+    Vec16<T>::load(a + p.sh, w);
+    float o[V / 2];
+#pragma unroll
+    for (int k = 0; k < V / 2; ++k) o[k] = 0.25f * (u[2 * k] + u[2 * k + 1] + w[2 * k] + w[2 * k + 1]);
+    float* out = p.out + (((long long)n * p.C + c) * p.Hp + hp) * p.Wp + (long long)ch * (V / 2);
+    if constexpr (VST && V / 2 >= 4) {
+#pragma unroll
+      for (int k = 0; k < V / 2; k += 4)
+        *reinterpret_cast<float4*>(out + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+    } else if constexpr (VST && V / 2 == 2) {
+      *reinterpret_cast<float2*>(out) = make_float2(o[0], o[1]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < V / 2; ++k) out[k] = o[k];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) pool2_bwd_kernel(const float* __restrict__ g, int NC, int H,
                                                          int W, int Hp, int Wp,
                                                          float* __restrict__ dx) {
@@ -82,6 +134,21 @@ static unsigned grid_for(long long work, int device) {
 
 template <typename T>
 static int pool_launch(const PoolArgs& p, bool luma, int device, cudaStream_t st) {
+  constexpr int V = Vec16<T>::V;
+  const bool vec = !luma && V >= 2 && p.W % V == 0 &&
+                   ((reinterpret_cast<uintptr_t>(p.x) |
+                     (uintptr_t)(p.sh * (long long)sizeof(T)) |
+                     (uintptr_t)(p.sc * (long long)sizeof(T)) |
+                     (uintptr_t)(p.sn * (long long)sizeof(T))) & 15u) == 0;
+  if (vec) {
+    const long long work = (long long)p.N * p.C * p.Hp * (p.W / V);
+    const bool vst = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0 && (p.Wp * 4) % 16 == 0 &&
+                     V / 2 >= 2;
+    if (vst) pool2_vec_kernel<T, true><<<grid_for(work, device), 256, 0, st>>>(p);
+    else pool2_vec_kernel<T, false><<<grid_for(work, device), 256, 0, st>>>(p);
+    FAB_LAUNCH_CHECK();
+    return FA_OK;
+  }
   const long long work = (long long)p.N * p.Cm * p.Hp * ((p.Wp + 1) / 2);
   if (luma) pool2_kernel<T, true><<<grid_for(work, device), 256, 0, st>>>(p);
   else pool2_kernel<T, false><<<grid_for(work, device), 256, 0, st>>>(p);

@@ -57,6 +57,14 @@ struct SsimArgs {
   double* out_plane_cs;
   double* out_per_image;
   double* out_total;
+  // fused squared-difference sums (SSIM with MSE / PSNR from the same read)
+  void* part_sq;                       // [P][bpp] uint64 (uint8 input) or double
+  double psnr_bias;
+  double* out_mse_per_image;
+  double* out_mse_total;
+  double* out_psnr_per_image;
+  double* out_psnr_total;
+  unsigned long long* out_ssd_per_image;  // uint8 input: exact sums
   // backward
   const float* dmap;
   const float* gscalar;
@@ -281,7 +289,7 @@ __device__ __forceinline__ constexpr int tapf(int j) {
 
 // Horizontal blur of the (x', y') planes: KW adjacent outputs from 2KW-1
 // staged inputs; out[o].xy = sum_j w[j] * plane(o + j).
-template <int KW>
+template <int KW, bool SYM = false>
 __device__ __forceinline__ void hblur_xy(const SsimArgs& p, const float* __restrict__ sx,
                                          const float* __restrict__ sy, float4* __restrict__ out) {
   float2 acc[KW];
@@ -293,7 +301,7 @@ __device__ __forceinline__ void hblur_xy(const SsimArgs& p, const float* __restr
 #pragma unroll
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
-      if (j >= 0 && j < KW) acc[o] = __ffma2_rn(p.w2[j], v, acc[o]);
+      if (j >= 0 && j < KW) acc[o] = __ffma2_rn(p.w2[tap<KW, SYM>(j)], v, acc[o]);
     }
   }
 #pragma unroll
@@ -301,7 +309,7 @@ __device__ __forceinline__ void hblur_xy(const SsimArgs& p, const float* __restr
 }
 
 // Horizontal blur of the product planes (x'y', (x'-y')^2) -> out[o].zw.
-template <int KW>
+template <int KW, bool SYM = false>
 __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __restrict__ sx,
                                            const float* __restrict__ sy,
                                            float4* __restrict__ out) {
@@ -316,11 +324,51 @@ __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __res
 #pragma unroll
     for (int o = 0; o < KW; ++o) {
       const int j = q - o;
-      if (j >= 0 && j < KW) acc[o] = __ffma2_rn(p.w2[j], v, acc[o]);
+      if (j >= 0 && j < KW) acc[o] = __ffma2_rn(p.w2[tap<KW, SYM>(j)], v, acc[o]);
     }
   }
 #pragma unroll
   for (int o = 0; o < KW; ++o) reinterpret_cast<float2*>(out + o)[1] = acc[o];
+}
+
+// Horizontal blur of the four moment planes from shifted staged rows, in
+// three passes of at most (KW+2)/3 outputs: out[o] = (blur x', blur y',
+// blur x'y', blur (x'-y')^2).  Fewer live accumulators than two full-width
+// passes, for the same number of shared loads.
+template <int KW, bool SYM, int O0, int NO>
+__device__ __forceinline__ void hblur4_part(const SsimArgs& p, const float* __restrict__ sx,
+                                            const float* __restrict__ sy,
+                                            float4* __restrict__ out) {
+  float2 a[NO], b[NO];
+#pragma unroll
+  for (int o = 0; o < NO; ++o) a[o] = b[o] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int q = O0; q < O0 + NO + KW - 1; ++q) {
+    const float xv = sx[q], yv = sy[q];
+    const float dv = xv - yv;
+    const float2 c = make_float2(xv, yv);
+    const float2 v = make_float2(xv * yv, dv * dv);
+#pragma unroll
+    for (int o = 0; o < NO; ++o) {
+      const int j = q - (O0 + o);
+      if (j >= 0 && j < KW) {
+        const float2 w = p.w2[tap<KW, SYM>(j)];
+        a[o] = __ffma2_rn(w, c, a[o]);
+        b[o] = __ffma2_rn(w, v, b[o]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < NO; ++o) out[O0 + o] = make_float4(a[o].x, a[o].y, b[o].x, b[o].y);
+}
+
+template <int KW, bool SYM>
+__device__ __forceinline__ void hblur4(const SsimArgs& p, const float* sx, const float* sy,
+                                       float4* out) {
+  constexpr int H = (KW + 2) / 3;
+  hblur4_part<KW, SYM, 0, H>(p, sx, sy, out);
+  hblur4_part<KW, SYM, H, H>(p, sx, sy, out);
+  hblur4_part<KW, SYM, 2 * H, KW - 2 * H>(p, sx, sy, out);
 }
 
 // Horizontal blur of two float components of float4 rows (backward scatter).

@@ -20,7 +20,7 @@ from . import backend
 __all__ = [
     "mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier",
     "huber", "rgb_to_luma", "gaussian_window_1d", "set_compile_enabled",
-    "set_fused_loss_grad",
+    "set_fused_loss_grad", "metrics",
     "MS_SSIM_WEIGHTS", "LUMA_COEFFS",
 ]
 
@@ -455,6 +455,65 @@ def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None
             out = out.to(torch.float64)
         return out
     return res["per_image"] if reduction == "none" else res["total"]
+
+
+# --------------------------------------------------------------------------- #
+# several metrics of one frame pair
+# --------------------------------------------------------------------------- #
+
+METRIC_NAMES = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber")
+
+
+def metrics(x: torch.Tensor, y: torch.Tensor, names: Sequence[str] = ("mse", "psnr", "ssim"),
+            *, data_range: Optional[float] = None, reduction: str = "mean",
+            win_size: int = 11, sigma: float = 1.5,
+            K: Sequence[float] = (0.01, 0.03)) -> dict:
+    """Several metrics of one batch of frame pairs, as a dict name -> tensor.
+
+    SSIM together with MSE and/or PSNR comes from a single kernel that sums the
+    squared differences while it stages the frames for SSIM: one read of the
+    pair instead of two, one launch instead of two.  The values equal those of
+    :func:`ssim`, :func:`mse` and :func:`psnr` (uint8 MSE exact); the other
+    names are computed by their own functions.  This is the computation behind
+    the reference's StreamingMetrics (modules.py:373-402), with the same
+    defaults."""
+    _check_reduction(reduction)
+    names = tuple(names)
+    bad = [n for n in names if n not in METRIC_NAMES]
+    if bad:
+        raise ValueError(f"unknown metric(s) {bad}; expected any of {list(METRIC_NAMES)}")
+    x4, y4, L, _ = _prep(x, y, None, 0, data_range)
+    backend.require_cuda(x4)
+    out = {}
+    fused = "ssim" in names and ("mse" in names or "psnr" in names) and \
+        not _grad_wanted(x4, y4) and min(x4.shape[-2:]) >= win_size
+    if fused:
+        K1, K2 = float(K[0]), float(K[1])
+        res = backend.ssim_mse(x4.detach(), y4.detach(), _kernel_window(win_size, sigma, x4.device),
+                               shift=0.5 * L, C1=(K1 * L) ** 2, C2=(K2 * L) ** 2,
+                               psnr_bias=math.log10(L * L) * 10.0,
+                               per_image=(reduction == "none"))
+        for n in ("mse", "psnr", "ssim"):
+            if n in names:
+                out[n] = res[n]
+    kw_range = {"data_range": L}
+    table = {
+        "mse": lambda: mse(x4, y4, reduction=reduction),
+        "psnr": lambda: psnr(x4, y4, reduction=reduction, **kw_range),
+        "ssim": lambda: ssim(x4, y4, reduction=reduction, win_size=win_size, sigma=sigma, K=K,
+                             **kw_range),
+        "ms_ssim": lambda: ms_ssim(x4, y4, reduction=reduction, win_size=win_size, sigma=sigma,
+                                   K=K, **kw_range),
+        "gmsd": lambda: gmsd(x4, y4, reduction=reduction, **kw_range),
+        "gms": lambda: gms(x4, y4, reduction=reduction, **kw_range),
+        "l1": lambda: l1(x4, y4, reduction=reduction),
+        "charbonnier": lambda: charbonnier(x4, y4, reduction=reduction),
+        "huber": lambda: huber(x4, y4, reduction=reduction),
+    }
+    for n in names:
+        if n not in out:
+            out[n] = table[n]()
+    return out
 
 
 # --------------------------------------------------------------------------- #

@@ -12,7 +12,8 @@ from torch import nn
 from .functional import (MS_SSIM_WEIGHTS, charbonnier, gms, gmsd, huber, l1, ms_ssim,
                          mse, psnr, ssim)
 
-__all__ = ["MSE", "PSNR", "SSIM", "MSSSIM", "GMSD", "L1", "Charbonnier", "Huber"]
+__all__ = ["MSE", "PSNR", "SSIM", "MSSSIM", "GMSD", "L1", "Charbonnier", "Huber",
+           "StreamingMetrics"]
 
 
 class MSE(nn.Module):
@@ -152,3 +153,97 @@ class Huber(_PixelLoss):
     def __init__(self, delta: float = 1.0, **kwargs):
         super().__init__(**kwargs)
         self.extra = {"delta": float(delta)}
+
+
+class StreamingMetrics:
+    """Score a stream of frame pairs of one fixed shape (modules.py:308-451 of
+    the reference): the metrics are computed into static device buffers, by
+    one CUDA-graph replay per pair when capture succeeds.
+
+    ``metrics`` defaults to ``("mse", "psnr", "ssim")``, which
+    :func:`frame_analytics_b200.metrics` computes in a single launch and one
+    read of the pair.  Host frames are staged through pinned buffers.  The
+    reference's ``lpips`` and ``ssimulacra2`` are outside this package and
+    raise ``NotImplementedError``."""
+
+    _KNOWN = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber")
+    _ELSEWHERE = ("lpips", "ssimulacra2")
+
+    def __init__(self, shape, device="cuda", dtype=torch.uint8,
+                 data_range: Optional[float] = None, metrics=("mse", "psnr", "ssim"),
+                 use_cuda_graph: bool = True, pinned_staging: bool = True):
+        from .functional import _infer_data_range
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise TypeError("StreamingMetrics runs on a CUDA device")
+        self.dtype = dtype
+        self.shape = tuple(shape)
+        self.metrics = tuple(metrics)
+        other = [m for m in self.metrics if m in self._ELSEWHERE]
+        if other:
+            raise NotImplementedError(f"{other} are not part of frame_analytics_b200")
+        unknown = [m for m in self.metrics if m not in self._KNOWN]
+        if unknown:
+            raise ValueError(f"unknown metric(s) {unknown}; expected any of {list(self._KNOWN)}")
+        self.ref = torch.zeros(self.shape, dtype=dtype, device=self.device)
+        self.dist = torch.zeros(self.shape, dtype=dtype, device=self.device)
+        self._L = float(data_range) if data_range is not None else _infer_data_range(self.ref)
+        self._host = None
+        if pinned_staging:
+            self._host = (torch.empty(self.shape, dtype=dtype, pin_memory=True),
+                          torch.empty(self.shape, dtype=dtype, pin_memory=True))
+        self._graph = None
+        self._static_out = None
+        if use_cuda_graph:
+            self._try_capture()
+
+    def _compute(self):
+        from .functional import metrics as _metrics
+        return _metrics(self.ref, self.dist, self.metrics, data_range=self._L)
+
+    def _try_capture(self):
+        try:
+            side = torch.cuda.Stream(device=self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(3):  # kernels' one-time attributes, workspaces
+                    self._compute()
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._static_out = self._compute()
+            self._graph = g
+        except Exception:  # capture is an optimisation: fall back to eager calls
+            self._graph = None
+            self._static_out = None
+
+    def _stage(self, buf: torch.Tensor, src, slot: int) -> None:
+        if not torch.is_tensor(src):
+            src = torch.from_numpy(src)
+        if tuple(src.shape) != self.shape:
+            src = src.reshape(self.shape)
+        if src.is_cuda:
+            buf.copy_(src, non_blocking=True)
+        elif self._host is not None:
+            self._host[slot].copy_(src)
+            buf.copy_(self._host[slot], non_blocking=True)
+        else:
+            buf.copy_(src)
+
+    def update(self, ref, dist, *, as_float: bool = True):
+        """Score one frame pair; returns a dict metric -> value."""
+        self._stage(self.ref, ref, 0)
+        self._stage(self.dist, dist, 1)
+        if self._graph is not None:
+            self._graph.replay()
+            out = self._static_out
+        else:
+            out = self._compute()
+        if as_float:
+            return {k: float(v) for k, v in out.items()}
+        return {k: v.clone() for k, v in out.items()}
+
+    @property
+    def graph_captured(self) -> bool:
+        return self._graph is not None

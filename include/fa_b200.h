@@ -225,6 +225,28 @@ FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y,
                              double* out_plane_cs, double* out_per_image,
                              double* out_total, int device, void* stream);
 
+/* SSIM, MSE and PSNR from one read of the frame pair (the reference's
+ * StreamingMetrics default set, modules.py:373-402, which runs mse and ssim
+ * as separate kernels, fa_cuda.cu:1078-1156 and 1167-1283).  SSIM outputs as
+ * fa_b200_ssim (no map, no cs, no luma); the squared differences are summed
+ * over every input sample while the SSIM kernel stages it: exact uint64 sums
+ * for uint8 (out_ssd_per_image, [N]; NULL for other dtypes), float terms
+ * summed in double otherwise (double terms for f64), as
+ * fa_b200_pixel_reduce with FA_OP_MSE.  MSE per image / batch and PSNR
+ * (psnr_bias - 10 log10 mse) as there.  Every output is nullable.  The
+ * workspace is sized by fa_b200_ssim_workspace_bytes. */
+FA_B200_API int fa_b200_ssim_mse(const fa_view* x, const fa_view* y,
+                                 const float* taps_host, int K, double shift,
+                                 double C1, double C2, double psnr_bias,
+                                 void* workspace, size_t workspace_bytes,
+                                 double* out_plane_s, double* out_per_image,
+                                 double* out_total, double* out_mse_per_image,
+                                 double* out_mse_total,
+                                 double* out_psnr_per_image,
+                                 double* out_psnr_total,
+                                 uint64_t* out_ssd_per_image, int device,
+                                 void* stream);
+
 /* SSIM loss value and gradient in one pass (training steps).  No single
  * counterpart in the reference: it runs its forward (fa_cuda_ssim,
  * fa_cuda.cu:1167-1283) and later its backward (fa_cuda_ssim_backward,

@@ -1,0 +1,115 @@
+"""SSIM + MSE + PSNR from one kernel (``fa.metrics``) against the separate
+metric functions, and ``StreamingMetrics`` (the reference's streaming scorer,
+modules.py:308-451) with and without CUDA-graph capture."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import baseline_pair
+
+import frame_analytics_b200 as fa
+from frame_analytics_b200 import backend
+
+pytestmark = pytest.mark.gpu
+
+
+def _u8(shape, sigma=8.0, seed=0):
+    a, b = baseline_pair(shape, sigma, seed=seed)
+    return torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 64, 96), (1, 1, 37, 53), (3, 2, 131, 66),
+                                   (2, 3, 1080, 1920), (1, 3, 11, 11)])
+@pytest.mark.parametrize("reduction", ["mean", "none"])
+def test_fused_uint8_matches_separate(shape, reduction):
+    x, y = _u8(shape)
+    got = fa.metrics(x, y, ("mse", "psnr", "ssim"), reduction=reduction)
+    # exact integer sums: MSE and PSNR equal the standalone kernels bit for bit
+    assert torch.equal(got["mse"], fa.mse(x, y, reduction=reduction))
+    assert torch.equal(got["psnr"], fa.psnr(x, y, reduction=reduction))
+    # the SSIM kernel is the same code with the same partition
+    assert torch.equal(got["ssim"], fa.ssim(x, y, reduction=reduction))
+    # reference in host doubles (a CUDA tensor divided by a scalar is a
+    # multiplication by its reciprocal, which can differ in the last bit)
+    ssd = ((x.long() - y.long()) ** 2).flatten(1).sum(1).tolist()
+    per = x[0].numel()
+    ref = [v / per for v in ssd] if reduction == "none" else [sum(ssd) / (per * x.shape[0])]
+    assert got["mse"].reshape(-1).tolist() == ref
+
+
+def test_fused_exact_ssd_backend():
+    x, y = _u8((3, 3, 200, 333))
+    r = backend.ssim_mse(x, y, backend.host_taps(11, 1.5), shift=127.5, C1=(0.01 * 255) ** 2,
+                         C2=(0.03 * 255) ** 2, psnr_bias=20 * math.log10(255), per_image=True)
+    ref = ((x.long() - y.long()) ** 2).flatten(1).sum(1)
+    assert torch.equal(r["ssd"], ref)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
+@pytest.mark.parametrize("shape", [(2, 3, 70, 96), (1, 2, 45, 61)])
+def test_fused_float_matches_separate(dt, shape):
+    g = torch.Generator().manual_seed(1)
+    a = torch.rand(shape, generator=g, dtype=torch.float64)
+    b = (a + 0.05 * torch.randn(shape, generator=g, dtype=torch.float64)).clamp(0, 1)
+    x, y = a.to(dt).cuda(), b.to(dt).cuda()
+    got = fa.metrics(x, y, ("mse", "psnr", "ssim"), data_range=1.0, reduction="none")
+    torch.testing.assert_close(got["mse"], fa.mse(x, y, reduction="none"), rtol=1e-12, atol=0)
+    torch.testing.assert_close(got["psnr"], fa.psnr(x, y, data_range=1.0, reduction="none"),
+                               rtol=1e-12, atol=1e-12)
+    assert torch.equal(got["ssim"], fa.ssim(x, y, data_range=1.0, reduction="none"))
+
+
+def test_fused_strided_views():
+    x, y = _u8((2, 3, 90, 120))
+    xc, yc = x[:, :, 4:-4, 4:-4], y[:, :, 4:-4, 4:-4]
+    got = fa.metrics(xc, yc, ("mse", "ssim"), reduction="none")
+    assert torch.equal(got["mse"], fa.mse(xc, yc, reduction="none"))
+    assert torch.equal(got["ssim"], fa.ssim(xc, yc, reduction="none"))
+
+
+def test_identical_inputs():
+    x, _ = _u8((1, 3, 64, 64))
+    got = fa.metrics(x, x.clone(), ("mse", "psnr", "ssim"))
+    assert float(got["mse"]) == 0.0
+    assert math.isinf(float(got["psnr"]))
+    assert abs(float(got["ssim"]) - 1.0) < 1e-6
+
+
+def test_other_metrics_and_errors():
+    x, y = _u8((2, 3, 200, 200))
+    got = fa.metrics(x, y, ("gmsd", "l1", "ssim", "ms_ssim"))
+    assert torch.equal(got["gmsd"], fa.gmsd(x, y))
+    assert torch.equal(got["l1"], fa.l1(x, y))
+    assert torch.equal(got["ms_ssim"], fa.ms_ssim(x, y))
+    with pytest.raises(ValueError):
+        fa.metrics(x, y, ("vmaf",))
+
+
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_streaming_metrics(use_graph):
+    shape = (1, 3, 120, 160)
+    sm = fa.StreamingMetrics(shape, metrics=("mse", "psnr", "ssim", "gmsd"),
+                             use_cuda_graph=use_graph)
+    assert sm.graph_captured == use_graph
+    for seed in range(3):
+        a, b = baseline_pair(shape, 6.0, seed=seed)
+        got = sm.update(a, b)  # host numpy frames through pinned staging
+        x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        assert got["mse"] == float(fa.mse(x, y))
+        assert got["psnr"] == float(fa.psnr(x, y))
+        assert got["ssim"] == float(fa.ssim(x, y))
+        assert got["gmsd"] == float(fa.gmsd(x, y))
+        got_dev = sm.update(x, y, as_float=False)  # device frames
+        assert torch.equal(got_dev["ssim"], fa.ssim(x, y))
+
+
+def test_streaming_metrics_rejects():
+    with pytest.raises(NotImplementedError):
+        fa.StreamingMetrics((1, 3, 64, 64), metrics=("lpips",), use_cuda_graph=False)
+    with pytest.raises(ValueError):
+        fa.StreamingMetrics((1, 3, 64, 64), metrics=("nope",), use_cuda_graph=False)

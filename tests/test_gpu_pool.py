@@ -33,7 +33,8 @@ def _rand(shape, dt, seed=0):
     return (torch.rand(shape, generator=g, dtype=torch.float64) * 255).to(dt).cuda()
 
 
-@pytest.mark.parametrize("shape", [(1, 1, 2, 2), (2, 3, 37, 53), (1, 3, 64, 129), (3, 1, 131, 66)])
+@pytest.mark.parametrize("shape", [(1, 1, 2, 2), (2, 3, 37, 53), (1, 3, 64, 129), (3, 1, 131, 66),
+                                   (2, 3, 34, 64), (1, 2, 7, 32), (1, 1, 6, 96)])
 @pytest.mark.parametrize("dt", [torch.uint8, torch.float16, torch.bfloat16, torch.float32])
 def test_pool2_bitwise_vs_avg_pool2d(shape, dt):
     x = _rand(shape, dt)
@@ -48,6 +49,14 @@ def test_pool2_float64_input():
     got = backend.pool2(x)
     ref = F.avg_pool2d(x, 2).to(torch.float32)
     torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-4)
+
+
+def test_pool2_vector_path_with_row_padding():
+    """16-byte aligned row pitch wider than the row: the vector path with strides."""
+    for dt in (torch.uint8, torch.float16, torch.float32):
+        x = _rand((2, 3, 41, 80), dt)[..., :64]
+        assert not x.is_contiguous()
+        assert torch.equal(backend.pool2(x), F.avg_pool2d(x.float(), 2))
 
 
 def test_pool2_strided_views():
