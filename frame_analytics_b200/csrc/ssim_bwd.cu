@@ -274,9 +274,8 @@ __device__ __forceinline__ void hblur_raw_part(const SsimArgs& p, const float* _
   for (int o = 0; o < NO; ++o) a[o] = b[o] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int q = O0; q < O0 + NO + KW - 1; ++q) {
-    const float xv = sx[q], yv = sy[q];
-    const float dv = xv - yv;
-    const float2 c = __fadd2_rn(make_float2(xv, yv), nsh);  // shifted x', y'
+    const float2 c = __fadd2_rn(make_float2(sx[q], sy[q]), nsh);  // shifted x', y'
+    const float dv = c.x - c.y;  // from the shifted values, as the forward kernel forms it
     const float2 v = make_float2(c.x * c.y, dv * dv);  // x'y', (x'-y')^2
 #pragma unroll
     for (int o = 0; o < NO; ++o) {
@@ -377,10 +376,7 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
   float4 ring[KW];
 #pragma unroll
   for (int k = 0; k < KW; ++k) ring[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  // per-thread float partial of the owned SSIM values (at most a column of
-  // one chunk: relative rounding ~1e-7, far below the metric's tolerance;
-  // block and plane sums are double)
-  float acc_hi = 0.f;
+  double acc_s = 0.0;  // owned SSIM values: float per batch, double across batches
 
   if (grpA) {
     // ---------------- group A: moments -> coefficients ----------------
@@ -448,7 +444,7 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
                               (!FWD || (o0 >= r0 && o0 + KW - 1 < r0 + rows));
         if (interior) rows_step(std::false_type{});
         else rows_step(std::true_type{});
-        if constexpr (FWD) acc_hi += fs;
+        if constexpr (FWD) acc_s += (double)fs;
       }
       __syncthreads();
     }
@@ -492,7 +488,7 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
   }
   if constexpr (FWD) {
     const int bpp = p.strips * p.chunks;
-    const double acc_s = block_sum((double)acc_hi, s_red);
+    acc_s = block_sum(acc_s, s_red);
     if (threadIdx.x == 0) p.part_s[(long long)plane * bpp + blockIdx.y * p.strips + blockIdx.x] = acc_s;
     if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag))
       ssim_fwd_finalize(p, bpp);

@@ -253,7 +253,9 @@ def test_fused_loss_grad_matches_two_pass(reduction, hw, which):
         finally:
             fa.set_fused_loss_grad(True)
     (v1, gx1, gy1), (v0, gx0, gy0) = res[True], res[False]
-    torch.testing.assert_close(v1, v0, rtol=0, atol=1e-9)
+    # the fused kernel owns 32K-(K-1)-column strips, the forward 32K-column
+    # ones: float per-batch partials group differently (~1e-9)
+    torch.testing.assert_close(v1, v0, rtol=0, atol=1e-7)
     for g1, g0 in ((gx1, gx0), (gy1, gy0)):
         assert (g1 is None) == (g0 is None)
         if g1 is not None:
