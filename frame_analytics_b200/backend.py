@@ -412,6 +412,31 @@ def pool2(x: torch.Tensor, luma=None) -> torch.Tensor:
     return out
 
 
+def box_downsample(x: torch.Tensor, f: int, luma=None) -> torch.Tensor:
+    """MATLAB-mode f x f box downsample (replicated borders) to float32."""
+    L = lib()
+    vx, x = as_view(kernel_dtype(x))
+    cm = 1 if luma is not None else vx.c
+    pad = f // 2
+    ho = (vx.h + 2 * pad - f + 1 + f - 1) // f
+    wo = (vx.w + 2 * pad - f + 1 + f - 1) // f
+    out = torch.empty((vx.n, cm, ho, wo), dtype=torch.float32, device=x.device)
+    _call(x, L.fa_b200_box_downsample, ctypes.byref(vx), _luma_arg(luma), int(f),
+          out.data_ptr(), _dev(x), _stream(x))
+    return out
+
+
+def box_downsample_backward(g: torch.Tensor, shape, f: int) -> torch.Tensor:
+    """Adjoint of :func:`box_downsample` for a float32 input of ``shape``."""
+    L = lib()
+    g = g.detach().to(torch.float32).contiguous()
+    n, c, h, w = shape
+    dx = torch.empty((n, c, h, w), dtype=torch.float32, device=g.device)
+    _call(g, L.fa_b200_box_downsample_backward, g.data_ptr(), n, c, h, w, int(f),
+          dx.data_ptr(), _dev(g), _stream(g))
+    return dx
+
+
 def pool2_backward(g: torch.Tensor, shape) -> torch.Tensor:
     """Adjoint of :func:`pool2` for a float32 input of ``shape``."""
     L = lib()

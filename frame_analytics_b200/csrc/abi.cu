@@ -47,6 +47,10 @@ int grad_scale_impl(const float* in, long long per_image, int n, const double* s
                     int per_image_scale, double mult, float* out, int device, cudaStream_t st);
 int pool2_impl(const View& x, int dtype, const double* luma, float* out, int device,
                cudaStream_t st);
+int box_down_impl(const View& x, int dtype, const double* luma, int f, float* out, int device,
+                  cudaStream_t st);
+int box_down_backward_impl(const float* g, int N, int C, int H, int W, int f, float* dx,
+                           int device, cudaStream_t st);
 int pool2_backward_impl(const float* g, int N, int C, int H, int W, float* dx, int device,
                         cudaStream_t st);
 
@@ -439,6 +443,20 @@ FA_B200_API int fa_b200_grad_scale(const float* in, long long per_image, int n, 
   FAB_DEVICE_SCOPE(device);
   return grad_scale_impl(in, per_image, n, s, per_image_scale, mult, out, device,
                          static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_box_downsample(const fa_view* x, const double* luma, int f, float* out,
+                                       int device, void* stream) {
+  if (!view_ok(x) || !out) return FA_E_ARG;
+  FAB_DEVICE_SCOPE(device);
+  return box_down_impl(to_view(*x), x->dtype, luma, f, out, device,
+                       static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_box_downsample_backward(const float* g, int N, int C, int H, int W,
+                                                int f, float* dx, int device, void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return box_down_backward_impl(g, N, C, H, W, f, dx, device, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

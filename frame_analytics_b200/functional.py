@@ -386,18 +386,29 @@ def set_fused_loss_grad(enabled: bool) -> None:
     _fused_loss_grad = bool(enabled)
 
 
-def _matlab_downsample(x: torch.Tensor, f: int) -> torch.Tensor:
-    """MATLAB ssim.m's automatic box downsample (functional.py:575-586)."""
+class _BoxDownFn(torch.autograd.Function):
+    """MATLAB ssim.m's automatic downsample (functional.py:575-586): f x f box
+    mean with replicated borders, every f-th sample; forward and adjoint are
+    one kernel each."""
+
+    @staticmethod
+    def forward(ctx, x, f):
+        ctx.shape, ctx.dtype, ctx.f = tuple(x.shape), x.dtype, f
+        return backend.box_downsample(x, f)
+
+    @staticmethod
+    def backward(ctx, g):
+        return backend.box_downsample_backward(g, ctx.shape, ctx.f).to(ctx.dtype), None
+
+
+def _matlab_downsample(x: torch.Tensor, f: int, luma=None) -> torch.Tensor:
+    """The automatic downsample MATLAB's ssim.m applies to large images, to
+    float32; ``luma`` projects RGB inside the same kernel (no gradient)."""
     if f <= 1:
         return x
-    n, c, h, w = x.shape
-    ker = x.new_full((1, 1, f, f), 1.0 / (f * f))
-    pad = f // 2
-    xp = F.pad(x.reshape(n * c, 1, h, w), (pad, pad, pad, pad), mode="replicate")
-    with torch.autocast(device_type=x.device.type, enabled=False):
-        lp = F.conv2d(xp, ker)
-    lp = lp.reshape(n, c, lp.shape[-2], lp.shape[-1])
-    return lp[:, :, ::f, ::f].contiguous()
+    if luma is not None or not (torch.is_grad_enabled() and x.requires_grad):
+        return backend.box_downsample(x.detach(), f, luma=luma)
+    return _BoxDownFn.apply(x, f)
 
 
 def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
@@ -419,13 +430,15 @@ def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None
     grad = _grad_wanted(x4, y4)
 
     if downsample:
-        if lk is not None:
+        f = max(1, int(round(min(x4.shape[-2], x4.shape[-1]) / 256.0)))
+        if lk is not None and (grad or f == 1):
             x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
             lk = None
-        f = max(1, int(round(min(x4.shape[-2], x4.shape[-1]) / 256.0)))
         if f > 1:
-            x4 = _matlab_downsample(x4.to(torch.float32), f)
-            y4 = _matlab_downsample(y4.to(torch.float32), f)
+            # luma (when still pending) is projected inside the downsample kernel
+            x4 = _matlab_downsample(x4, f, luma=lk)
+            y4 = _matlab_downsample(y4, f, luma=lk)
+            lk = None
 
     if x4.shape[-2] < win_size or x4.shape[-1] < win_size:
         raise ValueError(f"image {tuple(x4.shape[-2:])} smaller than window {win_size}x{win_size}")

@@ -359,6 +359,22 @@ FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N,
 FA_B200_API int fa_b200_pool2(const fa_view* x, const double* luma, float* out,
                               int device, void* stream);
 
+/* MATLAB ssim.m's automatic downsample (the reference's _matlab_downsample,
+ * functional.py:575-586, torch pad + conv2d + strided slice): an f x f box
+ * mean with replicated borders (pad f/2), sampled every f-th row and column.
+ * out: float32 contiguous [N, C', ceil((H + 2(f/2) - f + 1)/f),
+ * ceil((W + 2(f/2) - f + 1)/f)]; luma as for fa_b200_pool2.  2 <= f <= 64. */
+FA_B200_API int fa_b200_box_downsample(const fa_view* x, const double* luma,
+                                       int f, float* out, int device,
+                                       void* stream);
+
+/* Adjoint of fa_b200_box_downsample (no luma): g float32 [N, C, Ho, Wo] ->
+ * dx float32 [N, C, H, W], every element written; border samples collect
+ * the weight of each replicated copy. */
+FA_B200_API int fa_b200_box_downsample_backward(const float* g, int N, int C,
+                                                int H, int W, int f, float* dx,
+                                                int device, void* stream);
+
 /* Adjoint of fa_b200_pool2 (no luma): dx[n, c, h, w] = g[n, c, h/2, w/2] / 4,
  * zero on a dropped odd row / column.  g: float32 [N, C, H/2, W/2];
  * dx: float32 [N, C, H, W], every element written. */

@@ -96,6 +96,22 @@ def avg_pool2(x: np.ndarray) -> np.ndarray:
 # input conventions (functional.py:141-271)
 # --------------------------------------------------------------------------- #
 
+def matlab_downsample(x: np.ndarray, f: int) -> np.ndarray:
+    """MATLAB ssim.m's automatic downsample as the reference writes it
+    (functional.py:575-586): replicate-pad f//2, f x f box mean (valid), then
+    every f-th row and column.  x: (..., H, W) float64."""
+    if f <= 1:
+        return x
+    pad = f // 2
+    xp = np.pad(x, [(0, 0)] * (x.ndim - 2) + [(pad, pad), (pad, pad)], mode="edge")
+    h, w = xp.shape[-2] - f + 1, xp.shape[-1] - f + 1
+    acc = np.zeros(x.shape[:-2] + (h, w))
+    for a in range(f):
+        for b in range(f):
+            acc += xp[..., a:a + h, b:b + w]
+    return (acc / (f * f))[..., ::f, ::f]
+
+
 def as_nchw(a: np.ndarray) -> np.ndarray:
     a = np.asarray(a)
     if a.ndim == 2:

@@ -182,6 +182,16 @@ def main():
     out["cfg1_ssd"] = (d * d).reshape(8, -1).sum(axis=1)
     out["cfg1_a_sum"] = int(a.astype(np.int64).sum())
 
+    # 7. MATLAB-mode SSIM downsample, from the reference's own implementation
+    #    (frame_analytics/functional.py _matlab_downsample, torch on the CPU)
+    import torch
+    from frame_analytics import functional as ref_f
+    rng = np.random.default_rng(7)
+    dsx = rng.integers(0, 256, (1, 2, 41, 58)).astype(np.float32)
+    out["mdown_x"] = dsx
+    for f in (2, 3, 4):
+        out[f"mdown_f{f}"] = ref_f._matlab_downsample(torch.from_numpy(dsx), f).numpy()
+
     np.savez_compressed(HERE / "golden.npz", **out)
     print(f"wrote {HERE / 'golden.npz'}: {len(out)} arrays")
 

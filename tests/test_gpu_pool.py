@@ -120,3 +120,74 @@ def test_ms_ssim_grad_matches_torch_pooling():
     finally:
         fn._Pool2Fn.apply = orig
     torch.testing.assert_close(x.grad, xr.grad, rtol=1e-5, atol=1e-9)
+
+
+@pytest.mark.parametrize("f", [2, 3, 4, 5])
+@pytest.mark.parametrize("hw", [(37, 53), (64, 96), (101, 80)])
+def test_box_downsample_vs_oracle(f, hw):
+    x = _rand((2, 3) + hw, torch.uint8)
+    got = backend.box_downsample(x, f).double().cpu().numpy()
+    ref = O.matlab_downsample(x.double().cpu().numpy(), f)
+    assert got.shape == ref.shape
+    # float32 sums of values up to 255 with an inexact 1/f^2 (f = 3, 5): a few
+    # float32 ulp, as in the reference's own float32 conv
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-5)
+
+
+def test_box_downsample_luma_and_strides():
+    x = _rand((2, 3, 90, 120), torch.uint8)
+    xc = x[:, :, 3:-2, 5:-4]
+    lk = (0.299, 0.587, 0.114, 0.0)
+    got = backend.box_downsample(xc, 3, luma=lk).double().cpu().numpy()
+    lum = np.tensordot(np.array(lk[:3]), xc.double().cpu().numpy(), axes=([0], [1]))[:, None]
+    np.testing.assert_allclose(got, O.matlab_downsample(lum, 3), rtol=2e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("f", [2, 3, 4])
+@pytest.mark.parametrize("hw", [(37, 53), (64, 96)])
+def test_box_downsample_backward(f, hw):
+    # float64 reference: cuDNN may run a float32 conv2d in TF32
+    x = _rand((1, 2) + hw, torch.float64).requires_grad_(True)
+    pad = f // 2
+    ker = torch.full((1, 1, f, f), 1.0 / (f * f), device="cuda", dtype=torch.float64)
+    xp = F.pad(x.reshape(2, 1, *hw), (pad, pad, pad, pad), mode="replicate")
+    d = F.conv2d(xp, ker)[:, :, ::f, ::f]
+    y = d.reshape(1, 2, d.shape[-2], d.shape[-1])
+    g = torch.randn_like(y)
+    (ref,) = torch.autograd.grad(y, x, g)
+    got = backend.box_downsample_backward(g.float(), tuple(x.shape), f)
+    torch.testing.assert_close(got.double(), ref, rtol=1e-5, atol=1e-6)
+
+
+def test_ssim_matlab_downsample_mode():
+    a, b = _pair(1, 3, 600, 800, 10.0, seed=2)  # min side 600 -> f = 2
+    got = float(fa.ssim(torch.as_tensor(a).cuda(), torch.as_tensor(b).cuda(), downsample=True))
+    da = O.matlab_downsample(a.astype(np.float64), 2)
+    db = O.matlab_downsample(b.astype(np.float64), 2)
+    assert abs(got - O.ssim(da, db)) < 5e-6
+    # luma folded into the downsample kernel
+    got_l = float(fa.ssim(torch.as_tensor(a).cuda(), torch.as_tensor(b).cuda(), downsample=True,
+                          luma="bt601"))
+    la = O.rgb_to_luma(a.astype(np.float64), "bt601", 255.0)
+    lb = O.rgb_to_luma(b.astype(np.float64), "bt601", 255.0)
+    assert abs(got_l - O.ssim(O.matlab_downsample(la, 2), O.matlab_downsample(lb, 2))) < 5e-6
+
+
+def test_ssim_matlab_downsample_gradient():
+    """Training through the downsample: the native adjoint against autograd
+    through the torch formulation of the same downsample."""
+    a, b = _pair(1, 3, 520, 530, 8.0, seed=4)
+    y0 = torch.as_tensor(b, dtype=torch.float32).cuda() / 255
+    x = torch.as_tensor(a, dtype=torch.float32).cuda() / 255
+    y = y0.clone().requires_grad_(True)
+    fa.ssim(x, y, data_range=1.0, downsample=True).backward()
+    y2 = y0.clone().requires_grad_(True)
+    f = 2
+    ker = torch.full((1, 1, f, f), 0.25, device="cuda", dtype=torch.float64)
+
+    def down(t):  # float64 conv (no TF32), result back to float32
+        tp = F.pad(t.double().reshape(3, 1, 520, 530), (1, 1, 1, 1), mode="replicate")
+        d = F.conv2d(tp, ker)[:, :, ::2, ::2]
+        return d.reshape(1, 3, d.shape[-2], d.shape[-1]).float()
+    fa.ssim(down(x), down(y2), data_range=1.0).backward()
+    torch.testing.assert_close(y.grad, y2.grad, rtol=1e-3, atol=1e-3 * float(y2.grad.abs().max()))

@@ -102,3 +102,12 @@ def test_ssim_grad_matches_finite_differences():
             else:
                 fd = (O.ssim(x, p, data_range=1.0) - O.ssim(x, m, data_range=1.0)) / (2 * h)
             assert abs(g[0, c, i, j] - fd) <= 1e-6 * max(1.0, abs(fd)) + 1e-9
+
+
+@pytest.mark.parametrize("f", [2, 3, 4])
+def test_matlab_downsample_pinned(golden, f):
+    """The oracle's MATLAB-mode downsample equals the reference's own
+    (functional.py:575-586, run by make_golden.py)."""
+    x = golden["mdown_x"].astype(np.float64)
+    # the reference computes in float32: relative agreement to a few float32 ulp
+    np.testing.assert_allclose(O.matlab_downsample(x, f), golden[f"mdown_f{f}"], rtol=1e-6, atol=0)
