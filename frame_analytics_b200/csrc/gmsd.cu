@@ -114,11 +114,14 @@ __device__ __forceinline__ void gm_row_terms(const float* s, float (&D)[GM_CPT],
 // Output rows 0..nr-1 of one iteration from pooled rows 0..nr+1 of a ring
 // (row pitch `pitch` floats): this thread's GM_CPT columns, summed into
 // fs (d = q - 1) and fs2 (d^2); the map is written when requested.
+template <bool MAP>
 __device__ __forceinline__ void gm_rows(const GmsdArgs& p, const float* sxr, const float* syr,
                                         int pitch, int nr, int t, int dc0, int plane, int orow0,
                                         float& fs, float& fs2) {
     const int c0t = t * GM_CPT;
     constexpr float NINTH = 1.0f / 9.0f;
+    // output columns of this thread inside the strip and the map
+    const int ncol = min(min(GM_OW, p.Wout - dc0) - c0t, GM_CPT);
     // Sliding 3-row window of column differences D (for gx) and row sums R
     // (for gy) of this thread's 4 output columns, per image; the ring slot
     // of pooled row r is r % 3, static because the loop is unrolled.
@@ -133,7 +136,7 @@ __device__ __forceinline__ void gm_rows(const GmsdArgs& p, const float* sxr, con
 #pragma unroll
           for (int i = 0; i < GM_CPT; ++i) {
             const int c = c0t + i;
-            if (c < GM_OW && dc0 + c < p.Wout) {
+            if (i < ncol) {
               // 3x the Prewitt/3 responses
               const float gx1 = Dx[s0][i] + Dx[s1][i] + Dx[s2][i], gy1 = Rx[s0][i] - Rx[s2][i];
               const float gx2 = Dy[s0][i] + Dy[s1][i] + Dy[s2][i], gy2 = Ry[s0][i] - Ry[s2][i];
@@ -142,17 +145,73 @@ __device__ __forceinline__ void gm_rows(const GmsdArgs& p, const float* sxr, con
               // G1 - G2 from differences and sums of the gradients: no cancellation
               const float dG = fmaf(gx1 - gx2, gx1 + gx2, (gy1 - gy2) * (gy1 + gy2)) * NINTH;
               const float S = G1 + G2;
-              // q - 1 = -(g1 - g2)^2 / (g1^2 + g2^2 + T),  (g1 - g2)^2 = dG^2 / (g1 + g2)^2
-              const float d = -(dG * dG) / ((S + 2.f * sqrtf(G1 * G2)) * (S + p.T));
+              // q - 1 = -(g1 - g2)^2 / (g1^2 + g2^2 + T),  (g1 - g2)^2 = dG^2 / (g1 + g2)^2.
+              // g1 g2 = G12 rsqrt(G12) (G12 >= eps^2 > 0) and one approximate
+              // division: a few ulp of d, which is small where q is near 1
+              const float G12 = G1 * G2;
+              const float d = -__fdividef(dG * dG, (S + 2.f * G12 * rsqrtf(G12)) * (S + p.T));
               fs += d;
               fs2 = fmaf(d, d, fs2);
-              if (p.map)
+              if constexpr (MAP)
                 p.map[((long long)plane * p.Hout + (orow0 + k)) * p.Wout + dc0 + c] = 1.0f + d;
             }
           }
         }
       }
     }
+}
+
+// gm_rows for the uint8 TMA kernel: the ring holds (x, y) pairs per column
+// (float2), as exact integer 2x2 sums (DOWN) or bytes, so both images go
+// through the Prewitt sums and g^2 in packed f32x2 instructions.  The 1/4 of
+// the pool and the 1/3 of Prewitt are folded into K = 1/144 (1/9 without the
+// pool); integer inputs keep gx, gy exact.
+template <bool MAP, bool DOWN>
+__device__ __forceinline__ void gm_rows_packed(const GmsdArgs& p, const float2* ring, int pitch,
+                                               int nr, int t, int dc0, int plane, int orow0,
+                                               float& fs, float& fs2) {
+  static_assert(GM_CPT == 2, "two output columns per thread");
+  constexpr float K = DOWN ? 1.0f / 144.0f : 1.0f / 9.0f;
+  const int c0t = t * GM_CPT;
+  const int ncol = min(min(GM_OW, p.Wout - dc0) - c0t, GM_CPT);
+  const float2 kk = make_float2(K, K), ee = make_float2(p.eps, p.eps);
+  const float2 m1 = make_float2(-1.f, -1.f);
+  float2 D[3][GM_CPT], R[3][GM_CPT];  // column differences / 3-sums, ring slot r % 3
+#pragma unroll
+  for (int r = 0; r < GM_R + 2; ++r) {
+    if (r < nr + 2) {
+      const float2* rowp = ring + r * pitch;
+      const float4 A = *reinterpret_cast<const float4*>(rowp + c0t);
+      const float4 B = *reinterpret_cast<const float4*>(rowp + c0t + 2);
+      const float2 P0 = make_float2(A.x, A.y), P1 = make_float2(A.z, A.w);
+      const float2 P2 = make_float2(B.x, B.y), P3 = make_float2(B.z, B.w);
+      D[r % 3][0] = __ffma2_rn(P2, m1, P0);
+      D[r % 3][1] = __ffma2_rn(P3, m1, P1);
+      const float2 s12 = __fadd2_rn(P1, P2);
+      R[r % 3][0] = __fadd2_rn(P0, s12);
+      R[r % 3][1] = __fadd2_rn(s12, P3);
+      if (r >= 2) {
+        const int k = r - 2, s0 = (r - 2) % 3, s1 = (r - 1) % 3, s2 = r % 3;
+#pragma unroll
+        for (int i = 0; i < GM_CPT; ++i) {
+          if (i < ncol) {
+            const float2 gx = __fadd2_rn(__fadd2_rn(D[s0][i], D[s1][i]), D[s2][i]);
+            const float2 gy = __ffma2_rn(R[s2][i], m1, R[s0][i]);
+            const float2 G = __ffma2_rn(__ffma2_rn(gx, gx, __fmul2_rn(gy, gy)), kk, ee);
+            // G1 - G2 from differences and sums of the gradients: no cancellation
+            const float dG = fmaf(gx.x - gx.y, gx.x + gx.y, (gy.x - gy.y) * (gy.x + gy.y)) * K;
+            const float S = G.x + G.y;
+            const float G12 = G.x * G.y;
+            const float d = -__fdividef(dG * dG, (S + 2.f * G12 * rsqrtf(G12)) * (S + p.T));
+            fs += d;
+            fs2 = fmaf(d, d, fs2);
+            if constexpr (MAP)
+              p.map[((long long)plane * p.Hout + (orow0 + k)) * p.Wout + dc0 + c0t + i] = 1.0f + d;
+          }
+        }
+      }
+    }
+  }
 }
 
 __device__ void gmsd_finalize(const GmsdArgs& p, int bpp) {
@@ -179,7 +238,7 @@ __device__ void gmsd_finalize(const GmsdArgs& p, int bpp) {
   }
 }
 
-template <typename T, bool DOWN, bool LUMA>
+template <typename T, bool DOWN, bool LUMA, bool MAP>
 __global__ void __launch_bounds__(GM_T, 2) gmsd_kernel(GmsdArgs p) {
   __shared__ __align__(16) float sx[GM_RING][GM_DW + 4];
   __shared__ __align__(16) float sy[GM_RING][GM_DW + 4];
@@ -239,7 +298,7 @@ __global__ void __launch_bounds__(GM_T, 2) gmsd_kernel(GmsdArgs p) {
     }
     __syncthreads();
     float fs = 0.f, fs2 = 0.f;
-    gm_rows(p, &sx[0][0], &sy[0][0], GM_DW + 4, nr, t, dc0, plane, r0 + rb, fs, fs2);
+    gm_rows<MAP>(p, &sx[0][0], &sy[0][0], GM_DW + 4, nr, t, dc0, plane, r0 + rb, fs, fs2);
     acc += (double)fs;
     acc2 += (double)fs2;
     __syncthreads();
@@ -281,7 +340,7 @@ struct GmTma {
   static constexpr unsigned TX = 2u * RIN * IW;                   // bytes per iteration
   static constexpr int RP = GM_DW + 4;                            // ring pitch, floats
   static constexpr size_t RAW = (size_t)2 * RIN * IW;
-  static constexpr size_t SMEM = RAW + sizeof(float) * 2 * (GM_R + 2) * RP;
+  static constexpr size_t SMEM = RAW + sizeof(float2) * (GM_R + 2) * RP;
   static_assert(RAW % 128 == 0, "ring must stay 16-byte aligned");
 };
 
@@ -291,14 +350,13 @@ __device__ __forceinline__ unsigned gm_bytes4(const unsigned char* row, int o) {
   return __funnelshift_r(w[0], w[1], (o & 3) * 8);
 }
 
-template <bool DOWN>
+template <bool DOWN, bool MAP>
 __global__ void __launch_bounds__(GM_T, 2) gmsd_tma_kernel(const __grid_constant__ GmsdArgs p) {
   using G = GmTma<DOWN>;
   extern __shared__ __align__(128) unsigned char s_gm[];
   unsigned char* rawx = s_gm;
   unsigned char* rawy = s_gm + G::RIN * G::IW;
-  float* ringx = reinterpret_cast<float*>(s_gm + G::RAW);
-  float* ringy = ringx + (GM_R + 2) * G::RP;
+  float2* ring = reinterpret_cast<float2*>(s_gm + G::RAW);  // [GM_R+2][RP] (x, y) pairs
   __shared__ __align__(8) unsigned long long s_bar;
   __shared__ double s_red[32];
   __shared__ int s_flag;
@@ -333,34 +391,47 @@ __global__ void __launch_bounds__(GM_T, 2) gmsd_tma_kernel(const __grid_constant
   for (int rb = 0, it = 0; rb < rows; rb += GM_R, ++it) {
     const int nr = min(GM_R, rows - rb);
     mbar_wait(&s_bar, it & 1);
-    // pool (or convert) the staged bytes into the float ring
+    // pool (or convert) the staged bytes into the ring: exact integer 2x2
+    // sums by dp4a (the 1/4 is folded into the Prewitt constant)
+    const bool al4 = (sofs & 3) == 0;  // uniform: staged words are aligned
 #pragma unroll
     for (int q = 0; q < GM_R + 2; ++q) {
       if (q < nr + 2) {
-#pragma unroll
-        for (int img = 0; img < 2; ++img) {
-          const unsigned char* raw = img ? rawy : rawx;
-          float2 v;
-          if (DOWN) {
-            const int o = sofs + 4 * t;
-            const unsigned a = gm_bytes4(raw + (2 * q) * G::IW, o);
-            const unsigned b = gm_bytes4(raw + (2 * q + 1) * G::IW, o);
-            v = make_float2(0.25f * (float)((int)(a & 0xff) + (int)((a >> 8) & 0xff) +
-                                            (int)(b & 0xff) + (int)((b >> 8) & 0xff)),
-                            0.25f * (float)((int)((a >> 16) & 0xff) + (int)(a >> 24) +
-                                            (int)((b >> 16) & 0xff) + (int)(b >> 24)));
+        float4 v;
+        if (DOWN) {
+          const int o = sofs + 4 * t;
+          const unsigned char* x0r = rawx + (2 * q) * G::IW;
+          const unsigned char* y0r = rawy + (2 * q) * G::IW;
+          unsigned ax, bx, ay, by;
+          if (al4) {
+            ax = *reinterpret_cast<const unsigned*>(x0r + o);
+            bx = *reinterpret_cast<const unsigned*>(x0r + G::IW + o);
+            ay = *reinterpret_cast<const unsigned*>(y0r + o);
+            by = *reinterpret_cast<const unsigned*>(y0r + G::IW + o);
           } else {
-            const unsigned a = gm_bytes4(raw + q * G::IW, sofs + 2 * t);
-            v = make_float2((float)(a & 0xff), (float)((a >> 8) & 0xff));
+            ax = gm_bytes4(x0r, o);
+            bx = gm_bytes4(x0r + G::IW, o);
+            ay = gm_bytes4(y0r, o);
+            by = gm_bytes4(y0r + G::IW, o);
           }
-          reinterpret_cast<float2*>((img ? ringy : ringx) + q * G::RP)[t] = v;
+          constexpr unsigned LO = 0x00000101u, HI = 0x01010000u;
+          v = make_float4((float)__dp4a(ax, LO, __dp4a(bx, LO, 0u)),
+                          (float)__dp4a(ay, LO, __dp4a(by, LO, 0u)),
+                          (float)__dp4a(ax, HI, __dp4a(bx, HI, 0u)),
+                          (float)__dp4a(ay, HI, __dp4a(by, HI, 0u)));
+        } else {
+          const unsigned a = gm_bytes4(rawx + q * G::IW, sofs + 2 * t);
+          const unsigned b = gm_bytes4(rawy + q * G::IW, sofs + 2 * t);
+          v = make_float4((float)(a & 0xff), (float)(b & 0xff), (float)((a >> 8) & 0xff),
+                          (float)((b >> 8) & 0xff));
         }
+        reinterpret_cast<float4*>(ring + q * G::RP)[t] = v;
       }
     }
     __syncthreads();
     if (rb + GM_R < rows) issue(rb + GM_R);  // the staging buffer is free again
     float fs = 0.f, fs2 = 0.f;
-    gm_rows(p, ringx, ringy, G::RP, nr, t, dc0, plane, r0 + rb, fs, fs2);
+    gm_rows_packed<MAP, DOWN>(p, ring, G::RP, nr, t, dc0, plane, r0 + rb, fs, fs2);
     acc += (double)fs;
     acc2 += (double)fs2;
     __syncthreads();  // the ring is rewritten next iteration
@@ -415,14 +486,15 @@ size_t gmsd_ws_bytes(int planes, int h, int w, int down, int device) {
 template <typename T, bool DOWN, bool LUMA>
 static int gm_launch(GmsdArgs& p, cudaStream_t st) {
   dim3 grid(p.strips, p.chunks, p.P);
-  gmsd_kernel<T, DOWN, LUMA><<<grid, GM_T, 0, st>>>(p);
+  if (p.map) gmsd_kernel<T, DOWN, LUMA, true><<<grid, GM_T, 0, st>>>(p);
+  else gmsd_kernel<T, DOWN, LUMA, false><<<grid, GM_T, 0, st>>>(p);
   FAB_LAUNCH_CHECK();
   return FA_OK;
 }
 
-template <bool DOWN>
+template <bool DOWN, bool MAP>
 static int gm_launch_tma(GmsdArgs& p, int device, cudaStream_t st) {
-  auto kern = gmsd_tma_kernel<DOWN>;
+  auto kern = gmsd_tma_kernel<DOWN, MAP>;
   static bool done[64] = {false};
   FAB_TRY(ensure_smem(kern, GmTma<DOWN>::SMEM, device, done));
   dim3 grid(p.strips, p.chunks, p.P);
@@ -471,7 +543,11 @@ int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, doubl
     if (make_row_map(&p.tmx, x, FA_U8, GMT_BOX, &dx) && make_row_map(&p.tmy, y, FA_U8, GMT_BOX, &dy) &&
         dx == dy) {
       p.tma_d = dx;
-      return down ? gm_launch_tma<true>(p, device, st) : gm_launch_tma<false>(p, device, st);
+      if (p.map)
+        return down ? gm_launch_tma<true, true>(p, device, st)
+                    : gm_launch_tma<false, true>(p, device, st);
+      return down ? gm_launch_tma<true, false>(p, device, st)
+                  : gm_launch_tma<false, false>(p, device, st);
     }
   }
   switch (dtype) {
