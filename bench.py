@@ -407,27 +407,54 @@ def run_ours(args):
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(dom_name)
 
-    # e2e through the public API from pinned host memory
+    # e2e through the public API from pinned host memory.  Every step copies
+    # its two fp32 frames host->device and reads its loss back.  The copies run
+    # on a copy stream into two alternating device slots, so step i+1's upload
+    # overlaps step i's kernels (double buffering, as a training loop's data
+    # loader does); a slot is refilled only after the step that used it ended.
     e2e_steps = 0 if args.no_extra else max(3, args.steps // 2)
     loss_h = torch.empty(1, dtype=torch.float64).pin_memory()
+    cstream = torch.cuda.Stream(device=dev)
+    slots = [(torch.empty_like(a), torch.empty_like(b.detach())) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
 
-    def e2e_step():
-        x = a_h.to(dev, non_blocking=True)
-        y = b_h.to(dev, non_blocking=True).requires_grad_(True)
-        loss, _ = step(x, y)
-        loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
+    def upload(i):
+        k = i % 2
+        with torch.cuda.stream(cstream):
+            if used[k]:
+                cstream.wait_event(freed[k])
+            slots[k][0].copy_(a_h, non_blocking=True)
+            slots[k][1].copy_(b_h, non_blocking=True)
+            ready[k].record(cstream)
+
+    def e2e_run(n, e0=None, e1=None):
+        if e0 is not None:
+            e0.record()
+            cstream.wait_event(e0)
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            k = i % 2
+            torch.cuda.current_stream().wait_event(ready[k])
+            x, y = slots[k][0], slots[k][1].detach().requires_grad_(True)
+            loss, _ = step(x, y)
+            loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
+            freed[k].record()
+            used[k] = True
+        if e1 is not None:
+            e1.record()
 
     e2e_value = None
     if e2e_steps:
-        e2e_step()
+        e2e_run(2)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = ev(), ev()
-        e0.record()
-        for _ in range(e2e_steps):
-            e2e_step()
-        e1.record()
+        e2e_run(e2e_steps, e0, e1)
         torch.cuda.synchronize()
         e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
         if world > 1:
@@ -536,7 +563,7 @@ def run_ours(args):
                      "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                      "fp32_peak_tflops_at_clock": fp32_peak_tflops(sm_mhz)},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "Gpixel/s",
+        "e2e": {"value": e2e_value, "unit": "Gpixel/s", "overlap": "double-buffered uploads",
                 "h2d_bytes_per_step": 2 * 4 * px_step, "d2h_bytes_per_step": 8,
                 "steps": e2e_steps},
         "gpu_launches": 2 * args.steps,

@@ -111,4 +111,4 @@ def test_gmsd_module_loss_backward():
     loss = fa.GMSD(data_range=1.0).loss(p, a)
     loss.backward()
     assert p.grad is not None and torch.isfinite(p.grad).all() and float(p.grad.abs().max()) > 0
-    assert abs(float(loss) - (1 - float(fa.gms(p.detach(), a, data_range=1.0)))) < 1e-12
+    assert abs(float(loss.detach()) - (1 - float(fa.gms(p.detach(), a, data_range=1.0)))) < 1e-12
