@@ -49,6 +49,12 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+# Useful FLOP per pixel of the fused SSIM value+gradient kernel: horizontal
+# moments 4 x 11 x 2 + prep 5, vertical moments 88, coefficients 35,
+# horizontal and vertical scatter of 3 planes 2 x 66, final combination 5.
+FUSED_FLOP_PER_PX = 93 + 88 + 35 + 66 + 66 + 5
+
+
 def fp32_peak_tflops(sm_mhz: float) -> float:
     # 148 SMs x 128 FP32 lanes x 2 flop per FMA
     return 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
@@ -574,7 +580,17 @@ def run_ours(args):
                      "traffic": traffic, "peak_source": hbm_kind,
                      "kernel_ms": dom_ms, "algorithmic_bytes": dom_bytes,
                      "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-                     "fp32_peak_tflops_at_clock": fp32_peak_tflops(sm_mhz)},
+                     "fp32_peak_tflops_at_clock": fp32_peak_tflops(sm_mhz),
+                     # the kernel's binding roof is the FP32 pipes, not HBM:
+                     # useful FLOP per pixel by algorithm count (moments 4 planes
+                     # x 11 taps x 2 both ways, the x'y' / (x'-y')^2 prep, the
+                     # coefficients, 3-plane scatter both ways)
+                     "fp32_flop_per_px": FUSED_FLOP_PER_PX,
+                     "fp32_tflops": (FUSED_FLOP_PER_PX * px_step / (dom_ms / 1e3) / 1e12
+                                     if dom_name == "ssim_loss_grad" else None),
+                     "fp32_frac": (FUSED_FLOP_PER_PX * px_step / (dom_ms / 1e3) / 1e12
+                                   / fp32_peak_tflops(sm_mhz)
+                                   if dom_name == "ssim_loss_grad" else None)},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "Gpixel/s", "overlap": "double-buffered uploads",
                 "h2d_bytes_per_step": 2 * 4 * px_step, "d2h_bytes_per_step": 8,

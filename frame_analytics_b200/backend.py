@@ -26,6 +26,7 @@ DTYPE_CODE = {
     torch.bfloat16: 2,
     torch.float32: 3,
     torch.float64: 4,
+    torch.uint16: 5,  # extension code: read natively, exact integer MSE / L1
 }
 PSNR_NONE = -1.0e300
 OP_MSE, OP_L1, OP_CHARB, OP_HUBER = 0, 1, 2, 3

@@ -39,7 +39,9 @@ template <> struct Ld<bf16_t> {
 // Read-only scalar load through the non-coherent path.
 template <typename T>
 __device__ __forceinline__ T ldro(const T* p) {
-  if constexpr (sizeof(T) == 2) {
+  if constexpr (std::is_same<T, unsigned short>::value) {
+    return __ldg(p);
+  } else if constexpr (sizeof(T) == 2) {  // f16_t / bf16_t bit containers
     const unsigned short b = __ldg(reinterpret_cast<const unsigned short*>(p));
     T v;
     v.bits = b;

@@ -556,6 +556,7 @@ int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, doubl
     case FA_BF16: return gm_disp<bf16_t>(p, down, luma != nullptr, st);
     case FA_F32: return gm_disp<float>(p, down, luma != nullptr, st);
     case FA_F64: return gm_disp<double>(p, down, luma != nullptr, st);
+    case FA_U16: return gm_disp<unsigned short>(p, down, luma != nullptr, st);
     default: return FA_E_DTYPE;
   }
 }

@@ -26,7 +26,8 @@ template <typename T, int OP>
 struct PixTraits {
   // integer-exact accumulation: uint8 MSE and L1
   static constexpr bool kExact =
-      std::is_same<T, unsigned char>::value && (OP == FA_OP_MSE || OP == FA_OP_L1);
+      (std::is_same<T, unsigned char>::value || std::is_same<T, unsigned short>::value) &&
+      (OP == FA_OP_MSE || OP == FA_OP_L1);
   // uint8 Charbonnier / Huber read their term from a 256-entry table
   static constexpr bool kLut =
       std::is_same<T, unsigned char>::value && (OP == FA_OP_CHARB || OP == FA_OP_HUBER);
@@ -72,7 +73,18 @@ __device__ __forceinline__ void accum_vec(const uint4& va, const uint4& vb,
                                           typename PixTraits<T, OP>::Acc& acc,
                                           const float* lut, float pf, double pd) {
   using Tr = PixTraits<T, OP>;
-  if constexpr (Tr::kExact) {
+  if constexpr (Tr::kExact && sizeof(T) == 2) {
+    // uint16: |d| < 2^16, d^2 < 2^32 per element, summed in 64 bits
+    const unsigned short* ea = reinterpret_cast<const unsigned short*>(&va);
+    const unsigned short* eb = reinterpret_cast<const unsigned short*>(&vb);
+    unsigned long long s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const unsigned d = ea[i] > eb[i] ? (unsigned)ea[i] - eb[i] : (unsigned)eb[i] - ea[i];
+      s += (OP == FA_OP_MSE) ? (unsigned long long)(d * d) : (unsigned long long)d;
+    }
+    acc += s;
+  } else if constexpr (Tr::kExact) {
     const unsigned wa[4] = {va.x, va.y, va.z, va.w};
     const unsigned wb[4] = {vb.x, vb.y, vb.z, vb.w};
     unsigned s = 0;
@@ -122,7 +134,7 @@ __device__ __forceinline__ void accum_one(T x, T y, typename PixTraits<T, OP>::A
                                           const float* lut, float pf, double pd) {
   using Tr = PixTraits<T, OP>;
   if constexpr (Tr::kExact) {
-    const int d = (int)x - (int)y;
+    const long long d = (long long)x - (long long)y;
     acc += (OP == FA_OP_MSE) ? (unsigned long long)(d * d)
                              : (unsigned long long)(d < 0 ? -d : d);
   } else if constexpr (Tr::kLut) {
@@ -456,6 +468,7 @@ int pixel_reduce_impl(const View& a, const View& b, int dtype, const double* lum
     case FA_BF16: return launch_pixel_t<bf16_t>(p, op, device, st);
     case FA_F32: return launch_pixel_t<float>(p, op, device, st);
     case FA_F64: return launch_pixel_t<double>(p, op, device, st);
+    case FA_U16: return launch_pixel_t<unsigned short>(p, op, device, st);
     default: return FA_E_DTYPE;
   }
 }

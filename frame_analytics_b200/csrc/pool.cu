@@ -260,6 +260,7 @@ int pool2_impl(const View& x, int dtype, const double* luma, float* out, int dev
     case FA_BF16: return pool_launch<bf16_t>(p, luma != nullptr, device, st);
     case FA_F32: return pool_launch<float>(p, luma != nullptr, device, st);
     case FA_F64: return pool_launch<double>(p, luma != nullptr, device, st);
+    case FA_U16: return pool_launch<unsigned short>(p, luma != nullptr, device, st);
     default: return FA_E_DTYPE;
   }
 }
@@ -296,6 +297,7 @@ int box_down_impl(const View& x, int dtype, const double* luma, int f, float* ou
     case FA_BF16: FAB_BOX(bf16_t); break;
     case FA_F32: FAB_BOX(float); break;
     case FA_F64: FAB_BOX(double); break;
+    case FA_U16: FAB_BOX(unsigned short); break;
     default: return FA_E_DTYPE;
   }
 #undef FAB_BOX

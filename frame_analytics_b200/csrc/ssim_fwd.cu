@@ -9,7 +9,8 @@ namespace fab {
 // Squared-difference accumulator: exact for uint8, double otherwise (float
 // terms for f16/bf16/f32 as the pixel reductions form them, double for f64).
 template <typename T>
-using SqAcc = typename std::conditional<std::is_same<T, unsigned char>::value,
+using SqAcc = typename std::conditional<std::is_same<T, unsigned char>::value ||
+                                            std::is_same<T, unsigned short>::value,
                                         unsigned long long, double>::type;
 
 // stage_convert plus the squared differences of the staged elements this
@@ -74,6 +75,9 @@ __device__ __forceinline__ void stage_convert_sq(const SsimArgs& p, const T* raw
             if constexpr (std::is_same<T, double>::value) {
               const double d = ex[j] - ey[j];
               acc += d * d;
+            } else if constexpr (std::is_same<T, unsigned short>::value) {
+              const long long d = (long long)ex[j] - (long long)ey[j];
+              acc += (unsigned long long)(d * d);
             } else {
               const float d = Ld<T>::f(ex[j]) - Ld<T>::f(ey[j]);
               acc += (double)(d * d);
@@ -123,8 +127,9 @@ __device__ __forceinline__ void stage_direct(const SsimArgs& p, long long base, 
         b = Ld<T>::f(rb);
         if constexpr (SQ) {
           if (gr >= rlo && gr < rhi && gc >= clo && gc < chi) {
-            if constexpr (std::is_same<T, unsigned char>::value) {
-              const int d = (int)ra - (int)rb;
+            if constexpr (std::is_same<T, unsigned char>::value ||
+                          std::is_same<T, unsigned short>::value) {
+              const long long d = (long long)ra - (long long)rb;
               acc += (unsigned long long)(d * d);
             } else if constexpr (std::is_same<T, double>::value) {
               const double d = ra - rb;
@@ -402,12 +407,13 @@ static EncodeTiledFn encode_fn() {
 }
 
 bool make_row_map(CUtensorMap* map, const View& v, int dtype, int box_w, int* d) {
-  static const int esz[5] = {1, 2, 2, 4, 8};
-  static const CUtensorMapDataType dts[5] = {
+  static const int esz[6] = {1, 2, 2, 4, 8, 2};
+  static const CUtensorMapDataType dts[6] = {
       CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-      CU_TENSOR_MAP_DATA_TYPE_FLOAT64};
-  if (dtype < 0 || dtype > 4) return false;
+      CU_TENSOR_MAP_DATA_TYPE_FLOAT64,
+      CU_TENSOR_MAP_DATA_TYPE_UINT16};
+  if (dtype < 0 || dtype > 5) return false;
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const long long E = esz[dtype];
@@ -442,6 +448,7 @@ static int box_width(int dtype) {
     case FA_F16: return Raw<f16_t, KW>::BW;
     case FA_BF16: return Raw<bf16_t, KW>::BW;
     case FA_F32: return Raw<float, KW>::BW;
+    case FA_U16: return Raw<unsigned short, KW>::BW;
     default: return Raw<double, KW>::BW;
   }
 }
@@ -501,13 +508,13 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
     p.out_mse_total = sq->mse_total;
     p.out_psnr_per_image = sq->psnr_per_image;
     p.out_psnr_total = sq->psnr_total;
-    p.out_ssd_per_image = dtype == FA_U8 ? sq->ssd_per_image : nullptr;
+    p.out_ssd_per_image = (dtype == FA_U8 || dtype == FA_U16) ? sq->ssd_per_image : nullptr;
   }
   p.map_out = map_out;
   p.out_plane_s = out_plane_s; p.out_plane_cs = out_plane_cs;
   p.out_per_image = out_per_image; p.out_total = out_total;
   const bool cs = out_plane_cs != nullptr;
-  if (dtype < 0 || dtype > 4) return FA_E_DTYPE;
+  if (dtype < 0 || dtype > 5) return FA_E_DTYPE;
   int stage = luma ? STAGE_LUMA : STAGE_GENERIC;
   bool sym = true;  // the TMA kernels read only the first (K+1)/2 taps
   for (int j = 0; j < K; ++j) sym = sym && taps[j] == taps[K - 1 - j];
@@ -525,6 +532,7 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
     case FA_F16: return fwd_dispatch<f16_t>(p, stage, cs, K, device, st);
     case FA_BF16: return fwd_dispatch<bf16_t>(p, stage, cs, K, device, st);
     case FA_F32: return fwd_dispatch<float>(p, stage, cs, K, device, st);
+    case FA_U16: return fwd_dispatch<unsigned short>(p, stage, cs, K, device, st);
     default: return fwd_dispatch<double>(p, stage, cs, K, device, st);
   }
 }

@@ -56,6 +56,34 @@ def batch_mean(per_image: torch.Tensor) -> torch.Tensor:
     return per_image.sum() / per_image.numel()
 
 
+def exact_mse_from_ssd(ssd_local: torch.Tensor, n: int, samples_per_image: int,
+                       group=None) -> Tuple[torch.Tensor, float]:
+    """Batch MSE of integer frames from each rank's exact per-image sums of
+    squared differences (int64, as the uint8 / uint16 kernels return them).
+    The sums are gathered, not the float MSEs, so the per-image values and
+    the batch total equal the single-GPU results bit for bit: the total is
+    (sum of all sums) / (samples * n) in float64, as the kernel forms it."""
+    if ssd_local.dtype != torch.int64:
+        raise TypeError("exact MSE needs the int64 per-image sums")
+    ssd = gather_per_image(ssd_local, n, group)
+    per_image = ssd.to(torch.float64) / float(samples_per_image)
+    total = float(int(ssd.sum().item())) / float(samples_per_image * n)
+    return per_image, total
+
+
+def sharded_mse(x_local: torch.Tensor, y_local: torch.Tensor, n: int,
+                group=None) -> Tuple[torch.Tensor, float]:
+    """Exact batch MSE of sharded integer (uint8 / uint16) frames: each rank's
+    kernel returns its per-image sums, which are gathered."""
+    from . import backend
+    from .functional import _as_nchw
+    x4, y4 = _as_nchw(x_local), _as_nchw(y_local)
+    if x4.dtype not in (torch.uint8, torch.uint16):
+        raise TypeError("sharded_mse is the exact path for uint8 / uint16 frames")
+    _, ssd = backend.pixel(x4, y4, op=backend.OP_MSE, per_image=True, want_isum=True)
+    return exact_mse_from_ssd(ssd, n, x4[0].numel(), group)
+
+
 class ShardedMetrics:
     """Score a batch sharded over ranks and return whole-batch per-image results.
 

@@ -61,6 +61,10 @@ extern "C" {
 #define FA_BF16 2
 #define FA_F32 3
 #define FA_F64 4
+/* Extension, no counterpart in the reference (which widens uint16 to float32
+ * in torch first): uint16 samples, e.g. 10-16-bit video.  Accepted by the
+ * fa_b200_* calls; MSE / L1 of uint16 are exact integer sums, like uint8. */
+#define FA_U16 5
 
 /* pixel-loss selector (fa_abi.h:50-54) */
 #define FA_OP_MSE 0

@@ -13,7 +13,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from frame_analytics_b200.distributed import batch_mean, gather_per_image, shard_bounds
+from frame_analytics_b200.distributed import (batch_mean, exact_mse_from_ssd, gather_per_image,
+                                              shard_bounds)
 
 
 def _port():
@@ -45,6 +46,14 @@ def _worker(rank, world, port, n, mode, q):
         if mode == "die" and rank == 1:
             raise SystemExit(3)  # leaves before the gather, with nothing in flight
         full = gather_per_image(local, n)
+        if mode == "ssd":
+            # integer sums near 2^53 / n: the exact path must not round them
+            ssd = (torch.arange(lo, hi, dtype=torch.int64) * 1_000_003 + (1 << 40))
+            per, total = exact_mse_from_ssd(ssd, n, 6220800)
+            q.put((rank, "ok", per.tolist(), total))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         q.put((rank, "ok", full.tolist(), float(batch_mean(full))))
         dist.barrier()
         dist.destroy_process_group()
@@ -83,3 +92,15 @@ def test_dead_rank_fails_the_gather_instead_of_hanging():
     out = _run(2, 6, "die")
     assert out[1][1] == "died"
     assert out[0][1] == "error", out
+
+
+@pytest.mark.parametrize("world,n", [(2, 5), (3, 8)])
+def test_exact_mse_gathers_integer_sums(world, n):
+    """Sharded integer MSE: the gathered int64 sums give the per-image MSE and
+    the batch total exactly as one GPU forms them ((sum ssd) / (samples n))."""
+    out = _run(world, n, "ssd")
+    ssd = [i * 1_000_003 + (1 << 40) for i in range(n)]
+    for rank, status, per, total in out:
+        assert status == "ok", out
+        assert per == [v / 6220800 for v in ssd]
+        assert total == float(sum(ssd)) / float(6220800 * n)

@@ -1,0 +1,57 @@
+"""The sharded exact-MSE path through the real kernels and NCCL (one rank in a
+child process: the same code the multi-GPU sweep runs per rank)."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _child(port, q):
+    import torch.distributed as dist
+
+    import frame_analytics_b200 as fa
+    from frame_analytics_b200.distributed import sharded_mse
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        g = torch.Generator(device="cuda").manual_seed(0)
+        res = []
+        for dt in (torch.uint8, torch.uint16):
+            hi = 256 if dt == torch.uint8 else 65536
+            x = torch.randint(0, hi, (5, 3, 70, 90), generator=g, device="cuda",
+                              dtype=torch.int32).to(dt)
+            y = torch.randint(0, hi, (5, 3, 70, 90), generator=g, device="cuda",
+                              dtype=torch.int32).to(dt)
+            per, total = sharded_mse(x, y, 5)
+            res.append(torch.equal(per, fa.mse(x, y, reduction="none"))
+                       and total == float(fa.mse(x, y)))
+        q.put(res)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_exact_mse_one_rank_nccl():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_child, args=(_port(), q))
+    p.start()
+    res = q.get(timeout=300)
+    p.join(timeout=60)
+    assert res == [True, True]
