@@ -66,8 +66,12 @@ def exact_mse_from_ssd(ssd_local: torch.Tensor, n: int, samples_per_image: int,
     if ssd_local.dtype != torch.int64:
         raise TypeError("exact MSE needs the int64 per-image sums")
     ssd = gather_per_image(ssd_local, n, group)
-    per_image = ssd.to(torch.float64) / float(samples_per_image)
-    total = float(int(ssd.sum().item())) / float(samples_per_image * n)
+    # true float64 divisions, as the kernel's finaliser does them (a device
+    # tensor divided by a scalar may become a multiplication by its reciprocal)
+    sums = [int(v) for v in ssd.tolist()]
+    per_image = torch.tensor([v / float(samples_per_image) for v in sums], dtype=torch.float64,
+                             device=ssd.device)
+    total = float(sum(sums)) / float(samples_per_image * n)
     return per_image, total
 
 
