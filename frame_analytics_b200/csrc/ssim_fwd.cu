@@ -2,6 +2,8 @@
 // image and batch means -- one launch.  Replaces the reference's
 // ssim_fused_kernel REDUCE/MAP/CS modes + finalize (fa_cuda.cu:389-637,
 // 182-234, host 1167-1283).  Layout notes: ssim_common.cuh.
+#include <type_traits>
+
 #include "ssim_common.cuh"
 
 namespace fab {
@@ -265,23 +267,30 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
     if constexpr (TMA) {
       if (more) stage_tma<T, KW>(p, pn, pc, r0 + (m + 1) * KW, x0, rawX, rawY, &s_bar);
     }
-    // vertical + epilogue
+    // vertical + epilogue; interior batches (every slot a map row of this
+    // chunk) skip the per-row tests
     float fs = 0.f, fcs = 0.f;
+    auto rows_step = [&](auto chk) {
+      constexpr bool CHK = decltype(chk)::value;
 #pragma unroll
-    for (int k = 0; k < KW; ++k) {
-      ring[k] = sH[k * G::NT + t];
-      const int o = m * KW + k - (KW - 1);
-      if (o >= 0 && o < rows && col_ok) {
-        const Moments mo = moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
-        // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
-        // cs = A2 / B2 = A2 B1 / (B1 B2)
-        const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
-        const float S = mo.A1 * mo.A2 * inv;
-        if (CS) fcs += mo.A2 * mo.B1 * inv;
-        fs += S;
-        if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
+      for (int k = 0; k < KW; ++k) {
+        ring[k] = sH[k * G::NT + t];
+        const int o = m * KW + k - (KW - 1);
+        if (col_ok && (!CHK || (o >= 0 && o < rows))) {
+          const Moments mo = moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
+          // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
+          // cs = A2 / B2 = A2 B1 / (B1 B2)
+          const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
+          const float S = mo.A1 * mo.A2 * inv;
+          if (CS) fcs += mo.A2 * mo.B1 * inv;
+          fs += S;
+          if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
+        }
       }
-    }
+    };
+    const int o_first = m * KW - (KW - 1);
+    if (o_first >= 0 && o_first + KW - 1 < rows) rows_step(std::false_type{});
+    else rows_step(std::true_type{});
     acc_s += (double)fs;
     acc_cs += (double)fcs;
   }
