@@ -413,9 +413,11 @@ def run_ours(args):
     bwd_ms = statistics.mean(r[1].elapsed_time(r[2]) for r in recs)
     clocks = clk.summary()
 
-    # The step is two launches: the fused SSIM value + unit-gradient kernel
-    # (reads a, b: 8 B/px; writes d/db: 4 B/px) inside the forward, and the
-    # upstream-gradient scale (reads and writes d/db: 8 B/px) in the backward.
+    # The step is two launches: the fused SSIM value + gradient kernel (reads
+    # a, b: 8 B/px; writes d/db: 4 B/px, for the upstream gradient -1 of
+    # 1 - ssim) inside the forward, and the in-place upstream-gradient rescale
+    # in the backward (a factor of exactly 1 here: it returns at once; other
+    # upstream gradients read and write d/db, 8 B/px).
     fwd_bytes, bwd_bytes = 12 * px_step, 8 * px_step
     dom_ms, dom_bytes, dom_name = (fwd_ms, fwd_bytes, "ssim_loss_grad") if fwd_ms >= bwd_ms else \
         (bwd_ms, bwd_bytes, "grad_scale")

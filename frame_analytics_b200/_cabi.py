@@ -108,7 +108,7 @@ PROTOTYPES = {
     "fa_b200_ssim_mse": [_pview, _pview, _vp, _i, _d, _d, _d, _d, _vp, _sz, _vp, _vp, _vp,
                          _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "fa_b200_ssim_loss_grad_workspace_bytes": [_i, _i, _i, _i, _i, _i, _vp],
-    "fa_b200_ssim_loss_grad": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _d, _d, _vp, _sz,
+    "fa_b200_ssim_loss_grad": [_vp, _vp, _i, _i, _i, _i, _vp, _i, _d, _d, _d, _d, _vp, _sz,
                                _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "fa_b200_grad_scale": [_vp, ctypes.c_longlong, _i, _vp, _i, _d, _vp, _i, _vp],
     "fa_b200_box_downsample": [_pview, _vp, _i, _vp, _i, _vp],

@@ -324,8 +324,9 @@ def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
 
 def ssim_loss_grad(x: torch.Tensor, y: torch.Tensor, win: Taps, *, shift: float,
                    C1: float, C2: float, need_dx: bool = True, need_dy: bool = True,
-                   want_per_image: bool = False):
-    """SSIM means and the unit gradient of the batch-mean SSIM, one launch.
+                   want_per_image: bool = False, upstream: float = 1.0):
+    """SSIM means and the gradient of the batch-mean SSIM for the upstream
+    gradient ``upstream`` (1: the unit gradient), one launch.
     Returns ``(total, per_image or None, dx, dy)``; x, y float32 (N,C,H,W)."""
     L = lib()
     x = x.detach().to(torch.float32).contiguous()
@@ -342,19 +343,21 @@ def ssim_loss_grad(x: torch.Tensor, y: torch.Tensor, win: Taps, *, shift: float,
     dx = torch.empty_like(x) if need_dx else None
     dy = torch.empty_like(y) if need_dy else None
     _call(x, L.fa_b200_ssim_loss_grad, x.data_ptr(), y.data_ptr(), n, c, h, w, win.arr, k,
-          float(shift), float(C1), float(C2), ws.data_ptr(), ws.numel(), None,
+          float(shift), float(C1), float(C2), float(upstream), ws.data_ptr(), ws.numel(), None,
           _ptr(per_image), total.data_ptr(), _ptr(dx), _ptr(dy), dev, _stream(x))
     return total, per_image, dx, dy
 
 
 def grad_scale(unit: torch.Tensor, g: torch.Tensor, *, per_image: bool,
-               mult: float = 1.0) -> torch.Tensor:
+               mult: float = 1.0, inplace: bool = False) -> torch.Tensor:
     """``unit * g * mult`` (``g`` one scalar, or one value per image when
-    ``per_image``), a new float32 tensor; ``g`` stays on the device."""
+    ``per_image``); ``g`` stays on the device.  A new float32 tensor, or
+    ``unit`` itself rescaled when ``inplace`` (a factor of exactly 1 then
+    costs no memory traffic)."""
     L = lib()
     n = unit.shape[0]
     gd = g.detach().to(torch.float64).reshape(-1).contiguous()
-    out = torch.empty_like(unit)
+    out = unit if inplace else torch.empty_like(unit)
     _call(unit, L.fa_b200_grad_scale, unit.data_ptr(), unit.numel() // n, n, gd.data_ptr(),
           int(bool(per_image)), float(mult), out.data_ptr(), _dev(unit), _stream(unit))
     return out

@@ -40,7 +40,8 @@ int gmsd_backward_impl(const float* x, const float* y, int N, int C, int H, int 
 
 size_t ssim_loss_grad_ws_bytes(int N, int C, int H, int W, int K, int device);
 int ssim_loss_grad_impl(const float* x, const float* y, int N, int C, int H, int W,
-                        const float* taps, int K, double shift, double C1, double C2, void* ws,
+                        const float* taps, int K, double shift, double C1, double C2,
+                        double upstream, void* ws,
                         size_t ws_bytes, double* out_plane_s, double* out_per_image,
                         double* out_total, float* dx, float* dy, int device, cudaStream_t st);
 int grad_scale_impl(const float* in, long long per_image, int n, const double* s,
@@ -373,12 +374,13 @@ FA_B200_API int fa_b200_ssim_loss_grad_workspace_bytes(int n, int c, int h, int 
 
 FA_B200_API int fa_b200_ssim_loss_grad(const float* x, const float* y, int N, int C, int H, int W,
                                        const float* win, int K, double shift, double C1,
-                                       double C2, void* workspace, size_t workspace_bytes,
-                                       double* out_plane_s, double* out_per_image,
-                                       double* out_total, float* dx, float* dy, int device,
-                                       void* stream) {
+                                       double C2, double upstream, void* workspace,
+                                       size_t workspace_bytes, double* out_plane_s,
+                                       double* out_per_image, double* out_total, float* dx,
+                                       float* dy, int device, void* stream) {
   FAB_DEVICE_SCOPE(device);
-  return ssim_loss_grad_impl(x, y, N, C, H, W, win, K, shift, C1, C2, workspace, workspace_bytes,
+  return ssim_loss_grad_impl(x, y, N, C, H, W, win, K, shift, C1, C2, upstream, workspace,
+                             workspace_bytes,
                              out_plane_s, out_per_image, out_total, dx, dy, device,
                              static_cast<cudaStream_t>(stream));
 }

@@ -10,12 +10,15 @@
 namespace fab {
 
 template <bool VEC>
-__global__ void __launch_bounds__(256) grad_scale_kernel(const float* __restrict__ in,
+__global__ void __launch_bounds__(256) grad_scale_kernel(const float* in,
                                                           long long per_image, long long total,
                                                           const double* __restrict__ s,
                                                           int per_image_scale, double mult,
-                                                          float* __restrict__ out) {
+                                                          float* out) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+  const bool inplace = in == out;
+  // in place with a single factor of exactly 1: nothing changes
+  if (inplace && !per_image_scale && (float)(__ldg(s) * mult) == 1.0f) return;
   if constexpr (VEC) {
     const long long n4 = total >> 2, pi4 = per_image >> 2;
     const float4* in4 = reinterpret_cast<const float4*>(in);
@@ -23,6 +26,7 @@ __global__ void __launch_bounds__(256) grad_scale_kernel(const float* __restrict
     const float f0 = (float)(__ldg(s) * mult);
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
       const float f = per_image_scale ? (float)(__ldg(s + i / pi4) * mult) : f0;
+      if (inplace && f == 1.0f) continue;
       float4 v = __ldcs(in4 + i);
       v.x *= f; v.y *= f; v.z *= f; v.w *= f;
       __stcs(out4 + i, v);
@@ -31,6 +35,7 @@ __global__ void __launch_bounds__(256) grad_scale_kernel(const float* __restrict
     const float f0 = (float)(__ldg(s) * mult);
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
       const float f = per_image_scale ? (float)(__ldg(s + i / per_image) * mult) : f0;
+      if (inplace && f == 1.0f) continue;
       out[i] = in[i] * f;
     }
   }

@@ -617,9 +617,10 @@ size_t ssim_loss_grad_ws_bytes(int N, int C, int H, int W, int K, int device) {
 }
 
 int ssim_loss_grad_impl(const float* x, const float* y, int N, int C, int H, int W,
-                        const float* taps, int K, double shift, double C1, double C2, void* ws,
-                        size_t ws_bytes, double* out_plane_s, double* out_per_image,
-                        double* out_total, float* dx, float* dy, int device, cudaStream_t st) {
+                        const float* taps, int K, double shift, double C1, double C2,
+                        double upstream, void* ws, size_t ws_bytes, double* out_plane_s,
+                        double* out_per_image, double* out_total, float* dx, float* dy,
+                        int device, cudaStream_t st) {
   if (!ws) return FA_E_ARG;
   SsimArgs p;
   bool tma = false;
@@ -630,7 +631,7 @@ int ssim_loss_grad_impl(const float* x, const float* y, int N, int C, int H, int
   p.counter = static_cast<unsigned int*>(ws);
   p.part_s = reinterpret_cast<double*>(static_cast<char*>(ws) + FAB_COUNTER_BYTES);
   p.out_plane_s = out_plane_s; p.out_per_image = out_per_image; p.out_total = out_total;
-  p.grad_norm = (float)(1.0 / ((double)p.Hout * p.Wout * p.P));
+  p.grad_norm = (float)(upstream / ((double)p.Hout * p.Wout * p.P));
   return bwd_g<G_SCALAR, true>(p, tma, K, device, st);
 }
 

@@ -344,35 +344,55 @@ class _FusedSSIM(torch.autograd.Function):
 class _SSIMLossGrad(torch.autograd.Function):
     """Differentiable scalar / per-image SSIM computed together with its
     gradient (one launch, no separate forward).  The kernel returns the
-    gradient of the batch-mean SSIM for an upstream gradient of 1; backward
-    only scales it: by ``g`` for the batch mean, by ``g[n] * N`` per image
-    for ``reduction='none'``.  The gradient is computed even if backward is
-    never called, so :func:`set_fused_loss_grad` turns this off for callers
-    that evaluate with gradients enabled but rarely backpropagate."""
+    gradient of the batch-mean SSIM for an upstream gradient of -1, the one a
+    loss ``1 - ssim`` sends; backward rescales that buffer in place by the
+    real upstream gradient (by ``-g`` for the batch mean, by ``-g[n] * N``
+    per image for ``reduction='none'``), which for ``1 - ssim`` is a factor
+    of exactly 1 and costs nothing.  The buffer becomes the input's gradient,
+    so a second backward through the same graph (``retain_graph``) recomputes
+    from the saved inputs.  The gradient is computed even if backward is
+    never called: :func:`set_fused_loss_grad` turns this off for callers that
+    evaluate with gradients enabled but rarely backpropagate."""
 
     @staticmethod
     def forward(ctx, x, y, win, shift, C1, C2, mode, nx, ny):
         total, per_image, dx, dy = backend.ssim_loss_grad(
             x, y, win, shift=shift, C1=C1, C2=C2, need_dx=nx, need_dy=ny,
-            want_per_image=(mode == "none"))
-        ctx.unit = (dx, dy)
+            want_per_image=(mode == "none"), upstream=-1.0)
+        ctx.save_for_backward(x, y)
+        ctx.grads = (dx, dy)
+        ctx.win = win
+        ctx.consts = (shift, C1, C2)
         ctx.mode, ctx.n = mode, x.shape[0]
         return per_image if mode == "none" else total
 
     @staticmethod
     def backward(ctx, g):
         _reject_double_backward()
-        per_image = ctx.mode == "none"
-        mult = float(ctx.n) if per_image else 1.0
-        dx, dy = ctx.unit
         nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        per_image = ctx.mode == "none"
+        if ctx.grads is not None:
+            dx, dy = ctx.grads
+            ctx.grads = None  # handed to autograd below
+            mult = -float(ctx.n) if per_image else -1.0
 
-        def scaled(u):
-            return backend.grad_scale(u, g, per_image=per_image, mult=mult)
+            def scaled(u):
+                return backend.grad_scale(u, g, per_image=per_image, mult=mult, inplace=True)
 
-        return (scaled(dx) if (nx and dx is not None) else None,
-                scaled(dy) if (ny and dy is not None) else None,
-                None, None, None, None, None, None, None)
+            return (scaled(dx) if (nx and dx is not None) else None,
+                    scaled(dy) if (ny and dy is not None) else None,
+                    None, None, None, None, None, None, None)
+        # a second backward through the same graph: recompute
+        x, y = ctx.saved_tensors
+        shift, C1, C2 = ctx.consts
+        kw = dict(shift=shift, C1=C1, C2=C2, need_dx=nx, need_dy=ny)
+        if per_image:
+            c = x.shape[1]
+            gs = (g.to(torch.float32) / c).repeat_interleave(c)
+            dx, dy = backend.ssim_backward(x, y, ctx.win, gs=gs, gcs=torch.zeros_like(gs), **kw)
+        else:
+            dx, dy = backend.ssim_backward(x, y, ctx.win, gscalar=g, **kw)
+        return (dx if nx else None, dy if ny else None, None, None, None, None, None, None, None)
 
 
 _fused_loss_grad = True

@@ -258,8 +258,10 @@ FA_B200_API int fa_b200_ssim_mse(const fa_view* x, const fa_view* y,
  * Since d(mean SSIM)/dx is linear in the upstream scalar, this call returns
  * the SSIM means (as fa_b200_ssim: out_plane_s [N*C], out_per_image [N],
  * out_total [1], each nullable) together with dx / dy = the gradient of the
- * batch-mean SSIM (out_total) for an upstream gradient of 1; the caller
- * multiplies by its real upstream gradient.  Per image n,
+ * batch-mean SSIM (out_total) for the upstream gradient `upstream` (1 for
+ * the unit gradient; -1 gives the gradient of a loss 1 - SSIM directly); the
+ * caller rescales by its real upstream gradient (fa_b200_grad_scale).  Per
+ * image n,
  * d(out_per_image[n])/dx = N * dx restricted to image n.
  * x, y: float32 contiguous [N, C, H, W]; dx / dy nullable (not both);
  * taps_host: host memory.  workspace: device memory of the size
@@ -273,7 +275,8 @@ FA_B200_API int fa_b200_ssim_loss_grad(const float* x, const float* y, int N,
                                        int C, int H, int W,
                                        const float* taps_host, int K,
                                        double shift, double C1, double C2,
-                                       void* workspace, size_t workspace_bytes,
+                                       double upstream, void* workspace,
+                                       size_t workspace_bytes,
                                        double* out_plane_s,
                                        double* out_per_image,
                                        double* out_total, float* dx,
@@ -284,7 +287,8 @@ FA_B200_API int fa_b200_ssim_loss_grad(const float* x, const float* y, int N,
  * Applies the upstream gradient to the unit gradient fa_b200_ssim_loss_grad
  * returns (mult = N for per-image upstream gradients).  No counterpart in
  * the reference, whose backward receives the upstream gradient directly.
- * in and out may alias. */
+ * in and out may alias; in place, samples whose factor is exactly 1 are
+ * left untouched (a single scale of 1 returns at once). */
 FA_B200_API int fa_b200_grad_scale(const float* in, long long per_image, int n,
                                    const double* s, int per_image_scale,
                                    double mult, float* out, int device,

@@ -318,3 +318,26 @@ def test_backward_symmetric_and_asymmetric_windows(taps, fused):
     _torch_ssim_mean(xd, yd, wt, shift, C1, C2).backward()
     for got, ref in ((dx, xd.grad), (dy, yd.grad)):
         torch.testing.assert_close(got.double(), ref, rtol=1e-3, atol=2e-3 * float(ref.abs().max()))
+
+
+@pytest.mark.parametrize("reduction", ["mean", "none"])
+def test_fused_loss_grad_second_backward(reduction):
+    """The first backward hands the fused kernel's buffer to autograd; a second
+    backward through the same graph recomputes and accumulates the same."""
+    g = torch.Generator().manual_seed(5)
+    a = torch.rand((2, 3, 60, 80), generator=g).cuda()
+    b = (a + 0.05 * torch.randn(a.shape, generator=g).cuda()).clamp(0, 1)
+    y = b.clone().requires_grad_(True)
+    v = fa.ssim(a, y, data_range=1.0, reduction=reduction)
+    loss = (1.0 - v).sum()
+    loss.backward(retain_graph=True)
+    first = y.grad.clone()
+    loss.backward()
+    torch.testing.assert_close(y.grad, 2 * first, rtol=1e-5, atol=1e-5 * float(first.abs().max()))
+    fa.set_fused_loss_grad(False)
+    try:
+        y2 = b.clone().requires_grad_(True)
+        (1.0 - fa.ssim(a, y2, data_range=1.0, reduction=reduction)).sum().backward()
+    finally:
+        fa.set_fused_loss_grad(True)
+    torch.testing.assert_close(first, y2.grad, rtol=1e-5, atol=1e-5 * float(first.abs().max()))
