@@ -113,6 +113,8 @@ PROTOTYPES = {
     "fa_b200_grad_scale": [_vp, ctypes.c_longlong, _i, _vp, _i, _d, _vp, _i, _vp],
     "fa_b200_box_downsample": [_pview, _vp, _i, _vp, _i, _vp],
     "fa_b200_box_downsample_backward": [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp],
+    "fa_b200_pixel_loss_grad": [_vp, _vp, _i, _i64, _i, _d, _i, _vp, _sz, _vp, _vp, _vp, _vp,
+                                _i, _vp],
     "fa_b200_pool2": [_pview, _vp, _vp, _i, _vp],
     "fa_b200_pool2_backward": [_vp, _i, _i, _i, _i, _vp, _i, _vp],
 }

@@ -456,6 +456,26 @@ def pool2_backward(g: torch.Tensor, shape) -> torch.Tensor:
 # pixel-loss backward
 # --------------------------------------------------------------------------- #
 
+def pixel_loss_grad(x: torch.Tensor, y: torch.Tensor, *, op: int, param: float,
+                    per_image: bool, need_dx: bool = True, need_dy: bool = True):
+    """A pixel loss and its gradient (for an upstream gradient of 1) from one
+    read; x, y contiguous float32 (N, ...).  Returns (value, dx, dy)."""
+    L = lib()
+    n = x.shape[0]
+    per = x.numel() // n
+    dev = _dev(x)
+    nb = _cached_ws("pix", L.fa_b200_pixel_workspace_bytes, n, dev)
+    ws = workspace(x, nb)
+    out = _f64(x, n) if per_image else _f64(x)
+    dx = torch.empty_like(x) if need_dx else None
+    dy = torch.empty_like(y) if need_dy else None
+    _call(x, L.fa_b200_pixel_loss_grad, x.data_ptr(), y.data_ptr(), n, per, int(op),
+          float(param), int(bool(per_image)), ws.data_ptr(), ws.numel(),
+          _ptr(out) if per_image else None, None if per_image else out.data_ptr(),
+          _ptr(dx), _ptr(dy), dev, _stream(x))
+    return out, dx, dy
+
+
 def pixel_backward(x, y, g, *, op: int, param: float, per_image: bool, luma=None,
                    need_dx: bool = True, need_dy: bool = True):
     """Gradients of a pixel reduction w.r.t. x and y, in the inputs' dtypes."""

@@ -46,6 +46,10 @@ int ssim_loss_grad_impl(const float* x, const float* y, int N, int C, int H, int
                         double* out_total, float* dx, float* dy, int device, cudaStream_t st);
 int grad_scale_impl(const float* in, long long per_image, int n, const double* s,
                     int per_image_scale, double mult, float* out, int device, cudaStream_t st);
+int pixel_loss_grad_impl(const float* x, const float* y, int N, long long per, int op,
+                         double param, int per_image, void* ws, size_t ws_bytes,
+                         double* out_per_image, double* out_total, float* dx, float* dy,
+                         int device, cudaStream_t st);
 int pool2_impl(const View& x, int dtype, const double* luma, float* out, int device,
                cudaStream_t st);
 int box_down_impl(const View& x, int dtype, const double* luma, int f, float* out, int device,
@@ -459,6 +463,17 @@ FA_B200_API int fa_b200_box_downsample_backward(const float* g, int N, int C, in
                                                 int f, float* dx, int device, void* stream) {
   FAB_DEVICE_SCOPE(device);
   return box_down_backward_impl(g, N, C, H, W, f, dx, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_pixel_loss_grad(const float* x, const float* y, int N,
+                                        long long per_image_elems, int op, double param,
+                                        int per_image, void* workspace, size_t workspace_bytes,
+                                        double* out_per_image, double* out_total, float* dx,
+                                        float* dy, int device, void* stream) {
+  FAB_DEVICE_SCOPE(device);
+  return pixel_loss_grad_impl(x, y, N, per_image_elems, op, param, per_image, workspace,
+                              workspace_bytes, out_per_image, out_total, dx, dy, device,
+                              static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

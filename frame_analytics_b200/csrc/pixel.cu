@@ -535,6 +535,108 @@ __global__ void __launch_bounds__(256) pixel_bwd_kernel(PixBwdArgs p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// A pixel loss and its gradient in one read (training with mse / l1 /
+// charbonnier / huber as the loss): contiguous float32 [N, per] only.  Each
+// thread sums its penalties as the forward does (float term, float64 sum) and
+// writes dL/dx = norm * t'(d) (and dL/dy = -dL/dx) for an upstream gradient
+// of 1; norm = 1 / count of the value the gradient is of (the batch mean, or
+// each image's mean).  Block partials and the last-block finaliser are those
+// of the pixel reductions.
+// ---------------------------------------------------------------------------
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(PIX_THREADS, 4) pixel_loss_grad_kernel(PixArgs p, float norm,
+                                                                        float* dx, float* dy) {
+  __shared__ double s_red[32];
+  __shared__ int s_flag;
+  const int img = blockIdx.y;
+  const long long per = (long long)p.c * p.h * p.w;
+  const float* xa = reinterpret_cast<const float*>(p.a) + (long long)img * per;
+  const float* ya = reinterpret_cast<const float*>(p.b) + (long long)img * per;
+  float* gx = dx ? dx + (long long)img * per : nullptr;
+  float* gy = dy ? dy + (long long)img * per : nullptr;
+  const long long t0 = (long long)blockIdx.x * PIX_THREADS + threadIdx.x;
+  const long long step = (long long)p.bpi * PIX_THREADS;
+  double acc = 0.0;
+  auto one = [&](float d, float& g) {
+    if (OP == FA_OP_MSE) acc += (double)(d * d);
+    else acc += (double)pix_term<OP, float>(d, p.pf);
+    g = norm * pix_dterm<OP>(d, p.pf);
+  };
+  if constexpr (VEC) {
+    const long long n4 = per >> 2;
+    for (long long v = t0; v < n4; v += step) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(xa) + v);
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(ya) + v);
+      float4 g;
+      one(a.x - b.x, g.x);
+      one(a.y - b.y, g.y);
+      one(a.z - b.z, g.z);
+      one(a.w - b.w, g.w);
+      if (gx) __stcs(reinterpret_cast<float4*>(gx) + v, g);
+      if (gy) __stcs(reinterpret_cast<float4*>(gy) + v, make_float4(-g.x, -g.y, -g.z, -g.w));
+    }
+  } else {
+    for (long long i = t0; i < per; i += step) {
+      float g;
+      one(__ldg(xa + i) - __ldg(ya + i), g);
+      if (gx) gx[i] = g;
+      if (gy) gy[i] = -g;
+    }
+  }
+  acc = block_sum(acc, s_red);
+  if (threadIdx.x == 0) static_cast<double*>(p.partial)[(long long)img * p.bpi + blockIdx.x] = acc;
+  if (last_block_arrived(p.counter, gridDim.x * gridDim.y, &s_flag))
+    pix_finalize<double>(p, (double)per);
+}
+
+int pixel_loss_grad_impl(const float* x, const float* y, int N, long long per, int op,
+                         double param, int per_image, void* ws, size_t ws_bytes,
+                         double* out_per_image, double* out_total, float* dx, float* dy,
+                         int device, cudaStream_t st) {
+  if (!x || !y || !ws || (!dx && !dy)) return FA_E_ARG;
+  if (N <= 0 || per <= 0) return FA_E_SHAPE;
+  if (op < 0 || op > 3) return FA_E_OP;
+  PixArgs p{};
+  p.a = reinterpret_cast<const char*>(x);
+  p.b = reinterpret_cast<const char*>(y);
+  p.n = N; p.c = 1; p.h = 1; p.w = (int)per;
+  if ((long long)p.w != per) return FA_E_SHAPE;
+  p.sn = per; p.sc = per; p.sh = per;
+  p.flat = 1;
+  p.pf = (float)param;
+  p.pd = param;
+  p.psnr_bias = FA_PSNR_NONE;
+  p.bpi = pix_bpi(N, device);
+  const size_t need = FAB_COUNTER_BYTES + (size_t)N * p.bpi * 8;
+  if (ws_bytes < need) return FA_E_ARG;
+  p.counter = static_cast<unsigned int*>(ws);
+  p.partial = static_cast<char*>(ws) + FAB_COUNTER_BYTES;
+  p.out_per_image = out_per_image;
+  p.out_total = out_total;
+  const float norm = (float)(1.0 / (per_image ? (double)per : (double)per * N));
+  const bool vec = per % 4 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                     reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dy)) & 15u) == 0;
+#define FAB_PLG(OPV)                                                                        \
+  if (vec) {                                                                                \
+    p.bpi = wave_bpi<pixel_loss_grad_kernel<OPV, true>>(p, device);                         \
+    pixel_loss_grad_kernel<OPV, true><<<dim3(p.bpi, N), PIX_THREADS, 0, st>>>(p, norm, dx, dy); \
+  } else {                                                                                  \
+    p.bpi = wave_bpi<pixel_loss_grad_kernel<OPV, false>>(p, device);                        \
+    pixel_loss_grad_kernel<OPV, false><<<dim3(p.bpi, N), PIX_THREADS, 0, st>>>(p, norm, dx, dy); \
+  }
+  switch (op) {
+    case FA_OP_MSE: FAB_PLG(FA_OP_MSE); break;
+    case FA_OP_L1: FAB_PLG(FA_OP_L1); break;
+    case FA_OP_CHARB: FAB_PLG(FA_OP_CHARB); break;
+    default: FAB_PLG(FA_OP_HUBER); break;
+  }
+#undef FAB_PLG
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
 int pixel_backward_impl(const float* x, const float* y, int N, int C, int H, int W,
                         const double* luma, int op, double param, const double* g,
                         int per_image, float* dx, float* dy, int device, cudaStream_t st) {

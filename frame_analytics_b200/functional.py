@@ -184,9 +184,48 @@ class _PixelLoss(torch.autograd.Function):
         return dx, dy, None, None, None, None
 
 
+class _PixelLossGrad(torch.autograd.Function):
+    """A pixel loss computed together with its gradient (one read of x and y;
+    contiguous float32, no luma).  The kernel returns the gradient for an
+    upstream gradient of 1, the one ``loss = fa.mse(...)`` sends; backward
+    rescales that buffer in place (a factor of exactly 1 costs nothing).  A
+    second backward through the same graph recomputes from the saved inputs."""
+
+    @staticmethod
+    def forward(ctx, x, y, op, param, per_image):
+        out, dx, dy = backend.pixel_loss_grad(x, y, op=op, param=param, per_image=per_image,
+                                              need_dx=x.requires_grad, need_dy=y.requires_grad)
+        ctx.save_for_backward(x, y)
+        ctx.grads = (dx, dy)
+        ctx.op, ctx.param, ctx.per_image = op, param, per_image
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        _reject_double_backward()
+        nx, ny = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if ctx.grads is not None:
+            dx, dy = ctx.grads
+            ctx.grads = None  # handed to autograd below
+
+            def scaled(u):
+                return backend.grad_scale(u, g, per_image=ctx.per_image, inplace=True)
+
+            return (scaled(dx) if (nx and dx is not None) else None,
+                    scaled(dy) if (ny and dy is not None) else None, None, None, None)
+        x, y = ctx.saved_tensors
+        dx, dy = backend.pixel_backward(x, y, g, op=ctx.op, param=ctx.param,
+                                        per_image=ctx.per_image, need_dx=nx, need_dy=ny)
+        return dx, dy, None, None, None
+
+
 def _pixel(x4, y4, op, param, per_image, luma_k, psnr_bias=backend.PSNR_NONE):
     backend.require_cuda(x4)
     if _grad_wanted(x4, y4):
+        if (_fused_loss_grad and psnr_bias == backend.PSNR_NONE and luma_k is None
+                and x4.dtype == torch.float32 and y4.dtype == torch.float32
+                and x4.is_contiguous() and y4.is_contiguous()):
+            return _PixelLossGrad.apply(x4, y4, op, param, per_image)
         if psnr_bias != backend.PSNR_NONE:
             m = _PixelLoss.apply(x4, y4, op, param, per_image, luma_k)
             return psnr_bias - 10.0 * torch.log10(m)
@@ -399,8 +438,8 @@ _fused_loss_grad = True
 
 
 def set_fused_loss_grad(enabled: bool) -> None:
-    """Compute the SSIM gradient in the same pass as the value whenever an
-    input requires grad (default on).  Off: the forward computes the value
+    """Compute the SSIM gradient, and that of a float32 pixel loss, in the
+    same pass as the value whenever an input requires grad (default on).  Off: the forward computes the value
     only and the backward recomputes the moments."""
     global _fused_loss_grad
     _fused_loss_grad = bool(enabled)

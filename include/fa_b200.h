@@ -390,6 +390,23 @@ FA_B200_API int fa_b200_pool2_backward(const float* g, int N, int C, int H,
                                        int W, float* dx, int device,
                                        void* stream);
 
+/* A pixel loss (FA_OP_MSE / L1 / CHARB / HUBER) and its gradient from one
+ * read of x and y, for training.  No single counterpart in the reference,
+ * which reduces with fa_cuda_pixel_reduce (fa_cuda.cu:1078-1156) and
+ * differentiates with torch autograd (functional.py:1097-1141), reading the
+ * inputs again.  x, y: contiguous float32 [N, per_image_elems].  Outputs as
+ * fa_b200_pixel_reduce (out_per_image [N] / out_total, nullable) and dx / dy
+ * (nullable, not both) = the gradient, for an upstream gradient of 1, of the
+ * batch mean (per_image = 0) or of each image's mean (per_image = 1).  The
+ * workspace is sized by fa_b200_pixel_workspace_bytes. */
+FA_B200_API int fa_b200_pixel_loss_grad(const float* x, const float* y, int N,
+                                        long long per_image_elems, int op,
+                                        double param, int per_image,
+                                        void* workspace, size_t workspace_bytes,
+                                        double* out_per_image, double* out_total,
+                                        float* dx, float* dy, int device,
+                                        void* stream);
+
 /* Pixel reduction for callers that cannot allocate device memory.  No
  * counterpart in the reference: its reductions always take caller-allocated
  * scratch.  Callers such as host-application plugins that only receive frame

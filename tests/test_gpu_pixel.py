@@ -163,3 +163,48 @@ def test_pixel_loss_gradients(name, param, luma):
     rx, ry = torch.autograd.grad((ref * w).sum(), (xr, yr))
     torch.testing.assert_close(gx, rx, rtol=1e-5, atol=1e-7)
     torch.testing.assert_close(gy, ry, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("op", ["mse", "l1", "charbonnier", "huber"])
+@pytest.mark.parametrize("reduction", ["mean", "none"])
+@pytest.mark.parametrize("shape", [(2, 3, 40, 64), (3, 1, 17, 23)])
+def test_fused_pixel_loss_grad_matches_two_pass(op, reduction, shape):
+    """A float32 pixel loss with gradient from one read equals the reduction
+    followed by the separate backward kernel (vector and scalar paths)."""
+    fn = getattr(fa, op)
+    g = torch.Generator().manual_seed(2)
+    a = torch.rand(shape, generator=g).cuda()
+    b = torch.rand(shape, generator=g).cuda()
+    up = torch.randn(shape[0], generator=g, dtype=torch.float64).cuda() if reduction == "none" else None
+    res = {}
+    for fused in (True, False):
+        fa.set_fused_loss_grad(fused)
+        try:
+            x = a.clone().requires_grad_(True)
+            y = b.clone().requires_grad_(True)
+            v = fn(x, y, reduction=reduction)
+            (v.sum() if up is None else (v * up).sum()).backward()
+            res[fused] = (v.detach(), x.grad, y.grad)
+        finally:
+            fa.set_fused_loss_grad(True)
+    (v1, gx1, gy1), (v0, gx0, gy0) = res[True], res[False]
+    # MSE sums every float term in float64 on both paths; for the other
+    # penalties the forward kernel adds four float terms before going to
+    # float64, the fused one adds each: ~1e-8 relative
+    rtol = 1e-12 if op == "mse" else 1e-7
+    torch.testing.assert_close(v1, v0, rtol=rtol, atol=1e-15)
+    torch.testing.assert_close(v1, fn(a, b, reduction=reduction), rtol=rtol, atol=1e-15)
+    for g1, g0 in ((gx1, gx0), (gy1, gy0)):
+        torch.testing.assert_close(g1, g0, rtol=1e-6, atol=1e-6 * float(g0.abs().max()))
+
+
+def test_fused_pixel_loss_second_backward():
+    g = torch.Generator().manual_seed(3)
+    a = torch.rand((2, 3, 32, 48), generator=g).cuda()
+    y = torch.rand((2, 3, 32, 48), generator=g).cuda().requires_grad_(True)
+    loss = fa.mse(a, y)
+    loss.backward(retain_graph=True)
+    first = y.grad.clone()
+    loss.backward()
+    torch.testing.assert_close(y.grad, 2 * first, rtol=1e-6, atol=1e-12)
+    torch.testing.assert_close(first, 2 * (y.detach() - a) / a.numel(), rtol=1e-5, atol=1e-12)
