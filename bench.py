@@ -539,6 +539,25 @@ def run_ours(args):
             "gmsd_GB/s": 2 * px4 / (g4m / 1e3) / 1e9,
             "both_gpix_s": px4 / ((s4 + g4m) / 1e3) / 1e9}
         del x4, y4
+        # MSE as a training loss on the config-2 frames: one fused read vs the
+        # reduction followed by the separate backward kernel
+        yb = b.detach()
+
+        def mse_step():
+            yr = yb.detach().requires_grad_(True)
+            torch.autograd.grad(fa.mse(a, yr), yr)
+        mse_t = {}
+        for fused in (True, False):
+            fa.set_fused_loss_grad(fused)
+            try:
+                mse_step()
+                mse_t[fused] = timed_stream(mse_step, ev, flush, reps=max(5, args.steps // 2))
+            finally:
+                fa.set_fused_loss_grad(True)
+        extra["mse_loss_fwd_bwd_f32"] = {
+            "workload": "MSE loss fwd+bwd, fp32 8x3x1080x1920, grad w.r.t. b",
+            "fused_ms": mse_t[True], "two_pass_ms": mse_t[False],
+            "fused_GB/s": 12 * px_step / (mse_t[True] / 1e3) / 1e9}
         # config 3: MS-SSIM forward, 5 scales, uint8 input read in place
         ca, cb = u8_pair(PIX_SHAPE, 8.0, 0)
         xm, ym = torch.from_numpy(ca).to(dev), torch.from_numpy(cb).to(dev)
