@@ -369,7 +369,15 @@ def run_ours(args):
     a = a_h.to(dev)
     b = b_h.to(dev)
     b.requires_grad_(True)
-    gathered = torch.empty(world, dtype=torch.float64, device=dev)
+    # the per-step all-gather of the losses runs asynchronously on NCCL's
+    # stream, overlapping the next step's kernels; every handle is waited on
+    # (the current stream waits for the collective) before a timed region ends
+    pending = []
+
+    def drain():
+        for h in pending:
+            h.wait()
+        pending.clear()
 
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
@@ -383,11 +391,14 @@ def run_ours(args):
         if rec is not None:
             rec[2].record()
         if world > 1:
-            dist.all_gather_into_tensor(gathered, loss.detach().reshape(1))
+            gathered = torch.empty(world, dtype=torch.float64, device=dev)
+            pending.append(dist.all_gather_into_tensor(gathered, loss.detach().reshape(1),
+                                                       async_op=True))
         return loss, dy
 
     for _ in range(args.warmup):
         step(a, b)
+    drain()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -398,6 +409,7 @@ def run_ours(args):
         t0.record()
         for i in range(args.steps):
             step(a, b, recs[i])
+        drain()
         t1.record()
         torch.cuda.synchronize()
     if world > 1:
@@ -464,6 +476,7 @@ def run_ours(args):
             loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
             freed[k].record()
             used[k] = True
+        drain()
         if e1 is not None:
             e1.record()
 
