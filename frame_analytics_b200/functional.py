@@ -647,6 +647,55 @@ def _ms_weights(w, device) -> torch.Tensor:
 _ms_weight_cache: dict = {}
 
 
+_ms_stream_cache: dict = {}
+
+
+def _ms_streams(device, k):
+    key = (device.index, k)
+    st = _ms_stream_cache.get(key)
+    if st is None:
+        st = [torch.cuda.Stream(device=device) for _ in range(k)]
+        _ms_stream_cache[key] = st
+    return st
+
+
+def _ms_terms_concurrent(x, y, lk, scales, win, shift, C1, C2):
+    """Per-plane MS-SSIM factors (cs per scale, S at the coarsest), no
+    gradient.  Scale 0 runs on the caller's stream; the pyramid is pooled on
+    a side stream and each coarser scale's SSIM runs on a stream of its own as
+    soon as its level exists, so the small grids of the coarse scales overlap
+    one another and the tail of scale 0.  Every side stream forks from and
+    joins back into the caller's stream (each has its own workspace)."""
+    main = torch.cuda.current_stream(x.device)
+    streams = _ms_streams(x.device, scales)
+    pyr_st, scale_st = streams[0], streams[1:]
+    out = [None] * scales
+
+    def one(i, cx, cy, luma, last):
+        res = backend.ssim_forward(cx, cy, win, shift=shift, C1=C1, C2=C2, luma=luma,
+                                   want_cs=True)
+        return res["plane_s"] if last else res["plane_cs"]
+
+    pyr_st.wait_stream(main)
+    with torch.cuda.stream(pyr_st):
+        cx, cy = x, y
+        for i in range(1, scales):
+            pl = lk if i == 1 else None
+            cx, cy = backend.pool2(cx, luma=pl), backend.pool2(cy, luma=pl)
+            st = scale_st[i - 1]
+            st.wait_stream(pyr_st)
+            with torch.cuda.stream(st):
+                cx.record_stream(st)
+                cy.record_stream(st)
+                t = one(i, cx, cy, None, i == scales - 1)
+                t.record_stream(main)
+                out[i] = t
+    out[0] = one(0, x, y, lk, scales == 1)
+    for st in streams:
+        main.wait_stream(st)
+    return out
+
+
 def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None,
             win_size: int = 11, sigma: float = 1.5, K: Sequence[float] = (0.01, 0.03),
             weights: Optional[Sequence[float]] = None, reduction: str = "mean",
@@ -677,6 +726,12 @@ def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = N
         x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
         lk = None
     n = x4.shape[0]
+    if not grad:
+        terms = _ms_terms_concurrent(x4.detach(), y4.detach(), lk, len(w), win, shift, C1, C2)
+        stacked = torch.stack([t.view(n, -1) for t in terms]).clamp_min(0.0)
+        per_plane = stacked.pow(_ms_weights(w, x4.device)).prod(dim=0)
+        per_image = per_plane.mean(dim=1)
+        return per_image if reduction == "none" else per_image.mean()
     cx, cy = x4, y4
     terms = []
     for i in range(len(w)):

@@ -113,3 +113,16 @@ def test_streaming_metrics_rejects():
         fa.StreamingMetrics((1, 3, 64, 64), metrics=("lpips",), use_cuda_graph=False)
     with pytest.raises(ValueError):
         fa.StreamingMetrics((1, 3, 64, 64), metrics=("nope",), use_cuda_graph=False)
+
+
+def test_streaming_ms_ssim_captures_with_side_streams():
+    """MS-SSIM's coarse scales run on forked side streams; they join back into
+    the capturing stream, so the CUDA graph still captures and replays."""
+    shape = (1, 3, 256, 320)
+    sm = fa.StreamingMetrics(shape, metrics=("ms_ssim", "psnr"))
+    assert sm.graph_captured
+    for seed in range(2):
+        a, b = baseline_pair(shape, 6.0, seed=seed)
+        got = sm.update(a, b)
+        x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        assert abs(got["ms_ssim"] - float(fa.ms_ssim(x, y))) < 1e-12
