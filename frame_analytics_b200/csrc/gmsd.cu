@@ -24,7 +24,7 @@ constexpr int GM_CPT = 2;             // pooled columns per thread
 constexpr int GM_DW = GM_T * GM_CPT;  // pooled columns staged per strip
 constexpr int GM_OW = GM_DW - 4;      // output columns per strip (a multiple of 4 keeps
                                       // every strip's 8-byte uint8 loads aligned)
-constexpr int GM_R = 8;               // output rows per iteration
+constexpr int GM_R = 6;               // output rows per iteration
 constexpr int GM_RING = GM_R + 2;
 
 struct GmsdArgs {
@@ -351,7 +351,7 @@ __device__ __forceinline__ unsigned gm_bytes4(const unsigned char* row, int o) {
 }
 
 template <bool DOWN, bool MAP>
-__global__ void __launch_bounds__(GM_T, 2) gmsd_tma_kernel(const __grid_constant__ GmsdArgs p) {
+__global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant__ GmsdArgs p) {
   using G = GmTma<DOWN>;
   extern __shared__ __align__(128) unsigned char s_gm[];
   unsigned char* rawx = s_gm;
