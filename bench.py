@@ -584,10 +584,10 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and not args.no_extra:
-        gp, dt, thr, nimg = cpu_fwd_bwd_sample(1, min_seconds=10.0)
+        gp, dt, thr, nimg = cpu_fwd_bwd_sample(SHAPE[0], min_seconds=10.0)
         cpu = {"value": gp, "unit": "Gpixel/s", "cores": thr, "kind": "port",
-               "sample": f"{nimg} config-2 images (3x1080x1920 fp32, cycling through the 8) "
-                         f"SSIM fwd+bwd one at a time, C port (oracle/ssim_port.c), "
+               "sample": f"{nimg // SHAPE[0]} passes over the 8 config-2 images "
+                         f"(8x3x1080x1920 fp32) SSIM fwd+bwd, C port (oracle/ssim_port.c), "
                          f"{thr} threads, {dt:.1f} s"}
         rf = cpu_ref_ssim_fwd_sample(thr)
         if rf is not None:
