@@ -20,7 +20,8 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIBDIR = HERE / "_lib"
 LIB = LIBDIR / "libfa_b200.so"
-SOURCES = ["abi.cu", "pixel.cu", "ssim_fwd.cu", "ssim_bwd.cu", "gmsd.cu", "pool.cu", "grad_scale.cu"]
+SOURCES = ["abi.cu", "pixel.cu", "ssim_fwd.cu", "ssim_bwd.cu", "gmsd.cu", "pool.cu", "grad_scale.cu",
+           "ssim_compat.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -30,7 +30,9 @@ _STATUS = {
     5: "invalid argument",
     6: "internal error",
     7: "no CUDA device",
+    8: "a device-side wait timed out; the results of the kernel that waited are invalid",
 }
+FA_E_TIMEOUT = 8
 
 
 class KernelError(RuntimeError):
@@ -117,6 +119,7 @@ PROTOTYPES = {
                                 _i, _vp],
     "fa_b200_pool2": [_pview, _vp, _vp, _i, _vp],
     "fa_b200_pool2_backward": [_vp, _i, _i, _i, _i, _vp, _i, _vp],
+    "fa_b200_wait_selftest": [ctypes.c_ulonglong, _i, _vp],
 }
 _RESTYPE = {"fa_cuda_error_string": ctypes.c_char_p}
 

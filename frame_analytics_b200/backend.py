@@ -12,7 +12,11 @@ native call allocates and the calls stay legal inside CUDA-graph capture
 
 from __future__ import annotations
 
+import contextlib
+import contextvars
 import ctypes
+import functools
+import math
 from typing import Optional, Tuple
 
 import torch
@@ -118,27 +122,49 @@ def _luma_arg(luma) -> Optional[ctypes.Array]:
 # Every kernel's first 256 workspace bytes are completion counters that must
 # be zero on entry and are left zero on exit.  One zero-initialised buffer per
 # (device, stream) therefore serves every call issued in order on that stream;
-# it only ever grows.
+# it only ever grows.  Calls that may overlap on the GPU without being ordered
+# on one stream (CUDA-graph replays of different owners, say) need separate
+# buffers: private_workspaces gives an owner its own table.
 # --------------------------------------------------------------------------- #
 
 _ws: dict = {}
+# A caller that replays its own CUDA graphs (StreamingMetrics) routes its calls
+# to a pool of its own, so graphs and eager calls never share counters.
+_ws_pool: contextvars.ContextVar = contextvars.ContextVar("fa_b200_ws_pool", default=None)
+
+
+@contextlib.contextmanager
+def private_workspaces(pool: dict):
+    """Within this block, every workspace comes from `pool` (keyed by device
+    and stream like the shared one) instead of the process-wide table."""
+    token = _ws_pool.set(pool)
+    try:
+        yield pool
+    finally:
+        _ws_pool.reset(token)
+
+
+def _pool() -> dict:
+    p = _ws_pool.get()
+    return _ws if p is None else p
 
 
 def workspace(t: torch.Tensor, nbytes: int) -> torch.Tensor:
+    pool = _pool()
     key = (_dev(t), _stream(t))
-    buf = _ws.get(key)
+    buf = pool.get(key)
     if buf is None or buf.numel() < nbytes:
         size = max(int(nbytes), 1 << 16)
         if buf is not None:
             size = max(size, 2 * buf.numel())
         buf = torch.zeros(size, dtype=torch.uint8, device=t.device)
-        _ws[key] = buf
+        pool[key] = buf
     return buf
 
 
 def _drop_workspace(t: torch.Tensor) -> None:
     # a failed launch may leave a counter non-zero: never reuse that buffer
-    _ws.pop((_dev(t), _stream(t)), None)
+    _pool().pop((_dev(t), _stream(t)), None)
 
 
 def _call(t: torch.Tensor, fn, *args) -> None:
@@ -215,22 +241,25 @@ class Taps:
         self.arr = (ctypes.c_float * self.k)(*self.values)
 
 
-_taps_cache: dict = {}
+@functools.lru_cache(maxsize=64)
+def gaussian_taps(win_size: int, sigma: float) -> Tuple[float, ...]:
+    """The SSIM window in float64: exp(-t^2 / (2 sigma^2)) at
+    t = -(K-1)/2 .. (K-1)/2, divided by its sum (functional.py:397-420 of the
+    reference)."""
+    half = 0.5 * (win_size - 1)
+    raw = [math.exp(-0.5 * ((i - half) / sigma) ** 2) for i in range(win_size)]
+    total = math.fsum(raw)
+    return tuple(v / total for v in raw)
 
 
+@functools.lru_cache(maxsize=64)
 def host_taps(win_size: int, sigma: float) -> Taps:
-    """Same numbers as functional.gaussian_window_1d(..., dtype=float32):
-    float64 Gaussian, sum-normalised, rounded to float32 (functional.py:397-420)."""
-    key = (int(win_size), float(sigma))
-    t = _taps_cache.get(key)
-    if t is None:
-        r = (win_size - 1) / 2.0
-        c = torch.arange(win_size, dtype=torch.float64) - r
-        g = torch.exp(-(c * c) / (2.0 * sigma * sigma))
-        g = (g / g.sum()).to(torch.float32)
-        t = Taps(g.tolist())
-        _taps_cache[key] = t
-    return t
+    """gaussian_taps rounded to float32: the same numbers as
+    functional.gaussian_window_1d(..., dtype=torch.float32)."""
+    f32 = torch.tensor(gaussian_taps(int(win_size), float(sigma)),
+                       dtype=torch.float64).to(torch.float32)
+    return Taps(f32.tolist())
+
 
 def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                  shift: float, C1: float, C2: float, luma=None,

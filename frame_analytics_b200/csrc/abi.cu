@@ -1,13 +1,14 @@
 // extern "C" boundary of libfa_b200.so.  Every entry point validates its
 // arguments on the host, sets the device, and enqueues on the caller's stream;
 // none allocates and none synchronises.
-#include "common.cuh"
+#include "ssim_common.cuh"  // mbarrier helpers of the wait self-test
 
 #include <algorithm>
-#include <map>
 #include <mutex>
 #include <utility>
 #include <array>
+#include <atomic>
+#include <cstring>
 
 namespace fab {
 
@@ -20,12 +21,12 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
                   int K, double shift, double C1, double C2, float* map_out, void* ws,
                   size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
                   double* out_per_image, double* out_total, int device, cudaStream_t st,
-                  const SqOut* sq = nullptr);
+                  const SqOut* sq = nullptr, const float* wdev = nullptr);
 size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device);
 int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* win,
                   int K, double shift, double C1, double C2, const float* dmap,
                   const float* gscalar, const float* gs, const float* gcs, float* dx, float* dy,
-                  int device, cudaStream_t st);
+                  int device, cudaStream_t st, const float* wdev = nullptr);
 int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, double T, double eps,
               int down, void* ws, size_t ws_bytes, float* map_out, double* out_mean,
               double* out_std, int device, cudaStream_t st);
@@ -90,31 +91,61 @@ static bool view_ok(const fa_view* v) {
 }
 
 
-// The reference-compatible SSIM entry points receive the window as a device
-// pointer, while the kernels take their taps by value.  The taps are read
-// once per (device, pointer, size) with a blocking 44-byte copy and cached;
-// the reference caches its windows for the life of the process
-// (functional.py:397-420), so in practice this happens once.  That first
-// read synchronises, so make the first call outside any stream capture.
-static int host_taps(const float* win_dev, int K, int device, float* out) {
+// The bounded waits' error word.  Pinned, mapped host memory: the kernels
+// store to it without a copy back, and the host reads it without a
+// synchronisation.  It is allocated once per process by the first call that
+// launches a waiting kernel.  If that call happens under stream capture, the
+// thread's capture mode is relaxed for the allocation alone (a host
+// allocation touches no stream).
+static std::atomic<unsigned int*> g_wait_word{nullptr};
+
+unsigned int* wait_error_word() {
+  unsigned int* w = g_wait_word.load(std::memory_order_acquire);
+  if (w) return w;
   static std::mutex mu;
-  static std::map<std::pair<std::pair<int, uintptr_t>, int>, std::array<float, 12>> cache;
-  if (K < 1 || K > 12) return FA_E_WINDOW;
-  const auto key = std::make_pair(std::make_pair(device, reinterpret_cast<uintptr_t>(win_dev)), K);
-  {
-    std::lock_guard<std::mutex> g(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-      for (int j = 0; j < K; ++j) out[j] = it->second[j];
-      return FA_OK;
-    }
-  }
-  std::array<float, 12> t{};
-  FAB_TRY(cudaMemcpy(t.data(), win_dev, sizeof(float) * K, cudaMemcpyDeviceToHost));
   std::lock_guard<std::mutex> g(mu);
-  cache[key] = t;
-  for (int j = 0; j < K; ++j) out[j] = t[j];
-  return FA_OK;
+  w = g_wait_word.load(std::memory_order_acquire);
+  if (w) return w;
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  void* h = nullptr;
+  const cudaError_t e = cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not sticky: the waits then only give up
+    return nullptr;
+  }
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess || d != h) {
+    // every 64-bit CUDA platform has unified addressing; without it the word
+    // stays unused rather than being read through the wrong address
+    cudaGetLastError();
+    cudaFreeHost(h);
+    return nullptr;
+  }
+  std::memset(h, 0, 64);
+  w = static_cast<unsigned int*>(h);
+  g_wait_word.store(w, std::memory_order_release);
+  return w;
+}
+
+int take_wait_error() {
+  unsigned int* w = g_wait_word.load(std::memory_order_acquire);
+  if (!w) return FA_OK;
+  if (__atomic_load_n(w, __ATOMIC_ACQUIRE) == 0u) return FA_OK;
+  const unsigned v = __atomic_exchange_n(w, 0u, __ATOMIC_ACQ_REL);
+  return v ? FA_E_TIMEOUT : FA_OK;
+}
+
+// A wait on an mbarrier phase that nothing completes: no copy is in flight,
+// so the only effect of running out of time is the error word.
+__global__ void wait_selftest_kernel(unsigned* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) unsigned long long bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_async_smem();
+    mbar_wait_slow(smem_u32(&bar), 0u, err, limit_ns);
+  }
 }
 
 }  // namespace fab
@@ -139,6 +170,7 @@ FA_B200_API const char* fa_cuda_error_string(int code) {
     case FA_E_OP: return "unknown pixel op";
     case FA_E_ARG: return "invalid argument";
     case FA_E_NOCUDA: return "no CUDA device";
+    case FA_E_TIMEOUT: return "a device-side wait timed out; the results of the kernel that waited are invalid";
     default: return "internal error";
   }
 }
@@ -170,6 +202,7 @@ FA_B200_API int fa_cuda_pixel_reduce(const void* a, const void* b, int dtype, in
                                      double* out_per_image, double* out_total,
                                      double* out_psnr_per_image, double* out_psnr_total,
                                      int device, void* stream) {
+  FAB_PENDING();
   if (!a || !b || !partial) return FA_E_ARG;
   if (op < 0 || op > 3) return FA_E_OP;
   if (n_images <= 0 || n_per_image <= 0 || bpi <= 0 || n_images > INT32_MAX ||
@@ -202,35 +235,35 @@ FA_B200_API int fa_cuda_ssim(const void* x, const void* y, int dtype, int N, int
                              const float* win, int K, double shift, double C1, double C2,
                              float* map_out, double* partial, int bpp, double* out_per_image,
                              double* out_total, int device, void* stream) {
+  FAB_PENDING();
   if (!x || !y || !win || !partial) return FA_E_ARG;
   if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
   FAB_DEVICE_SCOPE(device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float taps[12];
   if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
-  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
   FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
   View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
-  return ssim_fwd_impl(vx, vy, dtype, nullptr, taps, K, shift, C1, C2, map_out, partial,
+  // the taps stay on the device: the kernel reads `win` itself
+  return ssim_fwd_impl(vx, vy, dtype, nullptr, nullptr, K, shift, C1, C2, map_out, partial,
                        (size_t)N * C * bpp * 8, nullptr, nullptr, out_per_image, out_total,
-                       device, st);
+                       device, st, nullptr, win);
 }
 
 FA_B200_API int fa_cuda_ssim_cs(const void* x, const void* y, int dtype, int N, int C, int H,
                                 int W, const float* win, int K, double shift, double C1,
                                 double C2, double* partial, double* partial_cs, int bpp,
                                 double* out_s, double* out_cs, int device, void* stream) {
+  FAB_PENDING();
   if (!x || !y || !win || !partial || !partial_cs || !out_s || !out_cs) return FA_E_ARG;
   if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
   FAB_DEVICE_SCOPE(device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float taps[12];
   if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
-  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
   FAB_TRY(cudaMemsetAsync(partial, 0, FAB_COUNTER_BYTES, st));
   View vx = contiguous_view(x, N, C, H, W), vy = contiguous_view(y, N, C, H, W);
-  return ssim_fwd_impl(vx, vy, dtype, nullptr, taps, K, shift, C1, C2, nullptr, partial,
-                       (size_t)N * C * bpp * 8, out_s, out_cs, nullptr, nullptr, device, st);
+  return ssim_fwd_impl(vx, vy, dtype, nullptr, nullptr, K, shift, C1, C2, nullptr, partial,
+                       (size_t)N * C * bpp * 8, out_s, out_cs, nullptr, nullptr, device, st,
+                       nullptr, win);
 }
 
 FA_B200_API int fa_cuda_ssim_backward(const float* x, const float* y, const float* dL_dmap,
@@ -238,15 +271,14 @@ FA_B200_API int fa_cuda_ssim_backward(const float* x, const float* y, const floa
                                       int C, int H, int W, double shift, double C1, double C2,
                                       float* aux, float* dx, float* dy, int device,
                                       void* stream) {
+  FAB_PENDING();
   (void)aux;
   if (dL_dmap && grad_scalar) grad_scalar = nullptr;  // the map wins, as in the reference
   if (!win) return FA_E_ARG;
   if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
   FAB_DEVICE_SCOPE(device);
-  float taps[12];
-  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
-  return ssim_bwd_impl(x, y, N, C, H, W, taps, K, shift, C1, C2, dL_dmap, grad_scalar, nullptr,
-                       nullptr, dx, dy, device, static_cast<cudaStream_t>(stream));
+  return ssim_bwd_impl(x, y, N, C, H, W, nullptr, K, shift, C1, C2, dL_dmap, grad_scalar,
+                       nullptr, nullptr, dx, dy, device, static_cast<cudaStream_t>(stream), win);
 }
 
 FA_B200_API int fa_cuda_ssim_cs_backward(const float* x, const float* y, const float* gs,
@@ -254,14 +286,13 @@ FA_B200_API int fa_cuda_ssim_cs_backward(const float* x, const float* y, const f
                                          int H, int W, double shift, double C1, double C2,
                                          float* aux, float* dx, float* dy, int device,
                                          void* stream) {
+  FAB_PENDING();
   (void)aux;
   if (!gs || !gcs || !win) return FA_E_ARG;
   if (K < 3 || K > FA_MAX_WIN || (K & 1) == 0) return FA_E_WINDOW;
   FAB_DEVICE_SCOPE(device);
-  float taps[12];
-  { const int rc = host_taps(win, K, device, taps); if (rc) return rc; }
-  return ssim_bwd_impl(x, y, N, C, H, W, taps, K, shift, C1, C2, nullptr, nullptr, gs, gcs, dx,
-                       dy, device, static_cast<cudaStream_t>(stream));
+  return ssim_bwd_impl(x, y, N, C, H, W, nullptr, K, shift, C1, C2, nullptr, nullptr, gs, gcs,
+                       dx, dy, device, static_cast<cudaStream_t>(stream), win);
 }
 
 FA_B200_API int fa_cuda_gmsd_workspace(int H, int W, int downsample, int* out_bpp) {
@@ -278,6 +309,7 @@ FA_B200_API int fa_cuda_gmsd(const void* x, const void* y, int dtype, int N, int
                              double Tc, double eps, int downsample, double* psum,
                              double* psumsq, int bpp, double* out_mean, double* out_std,
                              int device, void* stream) {
+  FAB_PENDING();
   (void)psumsq;
   if (!x || !y || !psum || !out_mean || !out_std) return FA_E_ARG;
   if (N <= 0 || C <= 0 || H <= 0 || W <= 0 || bpp <= 0) return FA_E_SHAPE;
@@ -308,6 +340,7 @@ FA_B200_API int fa_b200_pixel_reduce(const fa_view* a, const fa_view* b, const d
                                      double* out_total, double* out_psnr_per_image,
                                      double* out_psnr_total, uint64_t* out_isum_per_image,
                                      int device, void* stream) {
+  FAB_PENDING();
   if (!view_ok(a) || !view_ok(b)) return FA_E_ARG;
   if (a->dtype != b->dtype) return FA_E_DTYPE;
   FAB_DEVICE_SCOPE(device);
@@ -332,6 +365,7 @@ FA_B200_API int fa_b200_ssim(const fa_view* x, const fa_view* y, const double* l
                              float* map_out, void* workspace, size_t workspace_bytes,
                              double* out_plane_s, double* out_plane_cs, double* out_per_image,
                              double* out_total, int device, void* stream) {
+  FAB_PENDING();
   if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
   if (x->dtype != y->dtype) return FA_E_DTYPE;
   FAB_DEVICE_SCOPE(device);
@@ -345,6 +379,7 @@ FA_B200_API int fa_b200_ssim_backward(const float* x, const float* y, int N, int
                                       double C2, const float* dL_dmap, const float* g_scalar,
                                       const float* gs, const float* gcs, float* dx, float* dy,
                                       int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return ssim_bwd_impl(x, y, N, C, H, W, win, K, shift, C1, C2, dL_dmap, g_scalar, gs, gcs, dx,
                        dy, device, static_cast<cudaStream_t>(stream));
@@ -357,6 +392,7 @@ FA_B200_API int fa_b200_ssim_mse(const fa_view* x, const fa_view* y, const float
                                  double* out_mse_per_image, double* out_mse_total,
                                  double* out_psnr_per_image, double* out_psnr_total,
                                  uint64_t* out_ssd_per_image, int device, void* stream) {
+  FAB_PENDING();
   if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
   if (x->dtype != y->dtype) return FA_E_DTYPE;
   FAB_DEVICE_SCOPE(device);
@@ -382,6 +418,7 @@ FA_B200_API int fa_b200_ssim_loss_grad(const float* x, const float* y, int N, in
                                        size_t workspace_bytes, double* out_plane_s,
                                        double* out_per_image, double* out_total, float* dx,
                                        float* dy, int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return ssim_loss_grad_impl(x, y, N, C, H, W, win, K, shift, C1, C2, upstream, workspace,
                              workspace_bytes,
@@ -403,6 +440,7 @@ FA_B200_API int fa_b200_gmsd(const fa_view* x, const fa_view* y, const double* l
                              double eps, int downsample, void* workspace,
                              size_t workspace_bytes, float* map_out, double* out_mean,
                              double* out_std, int device, void* stream) {
+  FAB_PENDING();
   if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
   if (x->dtype != y->dtype) return FA_E_DTYPE;
   FAB_DEVICE_SCOPE(device);
@@ -416,6 +454,7 @@ FA_B200_API int fa_b200_gmsd_backward(const float* x, const float* y, int N, int
                                       const double* g_mean, const double* g_std,
                                       const double* mean, const double* std_, float* dx,
                                       float* dy, int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return gmsd_backward_impl(x, y, N, C, H, W, downsample, T, eps, g_mean, g_std, mean, std_, dx,
                             dy, device, static_cast<cudaStream_t>(stream));
@@ -425,6 +464,7 @@ FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N, in
                                        int W, const double* luma, int op, double param,
                                        const double* g, int per_image, float* dx, float* dy,
                                        int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return pixel_backward_impl(x, y, N, C, H, W, luma, op, param, g, per_image, dx, dy, device,
                              static_cast<cudaStream_t>(stream));
@@ -432,6 +472,7 @@ FA_B200_API int fa_b200_pixel_backward(const float* x, const float* y, int N, in
 
 FA_B200_API int fa_b200_pool2(const fa_view* x, const double* luma, float* out, int device,
                               void* stream) {
+  FAB_PENDING();
   if (!view_ok(x) || !out) return FA_E_ARG;
   FAB_DEVICE_SCOPE(device);
   return pool2_impl(to_view(*x), x->dtype, luma, out, device, static_cast<cudaStream_t>(stream));
@@ -439,6 +480,7 @@ FA_B200_API int fa_b200_pool2(const fa_view* x, const double* luma, float* out, 
 
 FA_B200_API int fa_b200_pool2_backward(const float* g, int N, int C, int H, int W, float* dx,
                                        int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return pool2_backward_impl(g, N, C, H, W, dx, device, static_cast<cudaStream_t>(stream));
 }
@@ -446,6 +488,7 @@ FA_B200_API int fa_b200_pool2_backward(const float* g, int N, int C, int H, int 
 FA_B200_API int fa_b200_grad_scale(const float* in, long long per_image, int n, const double* s,
                                    int per_image_scale, double mult, float* out, int device,
                                    void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return grad_scale_impl(in, per_image, n, s, per_image_scale, mult, out, device,
                          static_cast<cudaStream_t>(stream));
@@ -453,6 +496,7 @@ FA_B200_API int fa_b200_grad_scale(const float* in, long long per_image, int n, 
 
 FA_B200_API int fa_b200_box_downsample(const fa_view* x, const double* luma, int f, float* out,
                                        int device, void* stream) {
+  FAB_PENDING();
   if (!view_ok(x) || !out) return FA_E_ARG;
   FAB_DEVICE_SCOPE(device);
   return box_down_impl(to_view(*x), x->dtype, luma, f, out, device,
@@ -461,6 +505,7 @@ FA_B200_API int fa_b200_box_downsample(const fa_view* x, const double* luma, int
 
 FA_B200_API int fa_b200_box_downsample_backward(const float* g, int N, int C, int H, int W,
                                                 int f, float* dx, int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return box_down_backward_impl(g, N, C, H, W, f, dx, device, static_cast<cudaStream_t>(stream));
 }
@@ -470,10 +515,26 @@ FA_B200_API int fa_b200_pixel_loss_grad(const float* x, const float* y, int N,
                                         int per_image, void* workspace, size_t workspace_bytes,
                                         double* out_per_image, double* out_total, float* dx,
                                         float* dy, int device, void* stream) {
+  FAB_PENDING();
   FAB_DEVICE_SCOPE(device);
   return pixel_loss_grad_impl(x, y, N, per_image_elems, op, param, per_image, workspace,
                               workspace_bytes, out_per_image, out_total, dx, dy, device,
                               static_cast<cudaStream_t>(stream));
+}
+
+// Test hook of the bounded waits: one thread waits `limit_ns` for an mbarrier
+// phase that nothing completes, then records the time-out exactly as a
+// staging wait that gave up would.  Nothing is copied and nothing is left in
+// flight.  The next compute call returns FA_E_TIMEOUT.
+FA_B200_API int fa_b200_wait_selftest(unsigned long long limit_ns, int device, void* stream) {
+  FAB_PENDING();
+  FAB_DEVICE_SCOPE(device);
+  unsigned* w = wait_error_word();
+  if (!w) return FA_E_INTERNAL;
+  if (limit_ns > 1000000000ull) return FA_E_ARG;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(w, limit_ns);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
 }
 
 }  // extern "C"

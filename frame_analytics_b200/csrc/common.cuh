@@ -152,6 +152,14 @@ struct DeviceScope {
 
 int sm_count(int device);
 
+// Error word of the kernels' bounded waits: one host-mapped, device-visible
+// word per process, allocated (pinned host memory, 64 bytes) by the first
+// call that launches a waiting kernel; null if that allocation failed.
+unsigned int* wait_error_word();
+// FA_E_TIMEOUT (and the word cleared) if a wait has given up since the last
+// call, else FA_OK.  Never allocates.
+int take_wait_error();
+
 // Host-side request for the squared-difference outputs of the fused SSIM
 // forward (SSIM + MSE/PSNR from one read of the frame pair).
 struct SqOut {
@@ -175,6 +183,12 @@ struct SqOut {
   do {                                                  \
     const cudaError_t e_ = cudaGetLastError();          \
     if (e_ != cudaSuccess) return -static_cast<int>(e_); \
+  } while (0)
+
+// First statement of every compute entry point: report a wait that gave up.
+#define FAB_PENDING()                                          \
+  do {                                                         \
+    if (const int pend_ = ::fab::take_wait_error()) return pend_; \
   } while (0)
 
 #define FAB_DEVICE_SCOPE(DEV)        \

@@ -45,6 +45,7 @@ struct GmsdArgs {
   double* out_mean;
   double* out_std;
   float* map;      // optional [P][Hout][Wout] GMS map
+  unsigned int* err;  // host-mapped error word of the bounded waits
 };
 
 template <typename T, bool LUMA>
@@ -390,7 +391,7 @@ __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant
   double acc = 0.0, acc2 = 0.0;
   for (int rb = 0, it = 0; rb < rows; rb += GM_R, ++it) {
     const int nr = min(GM_R, rows - rb);
-    mbar_wait(&s_bar, it & 1);
+    mbar_wait(&s_bar, it & 1, p.err);
     // pool (or convert) the staged bytes into the ring: exact integer 2x2
     // sums by dp4a (the 1/4 is folded into the Prewitt constant)
     const bool al4 = (sofs & 3) == 0;  // uniform: staged words are aligned
@@ -518,6 +519,7 @@ int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, doubl
   if (x.sn != y.sn || x.sc != y.sc || x.sh != y.sh) return FA_E_SHAPE;
   if (luma && x.c != 3) return FA_E_SHAPE;
   GmsdArgs p{};
+  p.err = wait_error_word();
   if (!gm_dims(x.h, x.w, down, &p.Hd, &p.Wd, &p.Hout, &p.Wout)) return FA_E_SHAPE;
   p.x = static_cast<const char*>(x.data);
   p.y = static_cast<const char*>(y.data);

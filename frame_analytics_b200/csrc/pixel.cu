@@ -727,6 +727,7 @@ extern "C" FA_B200_API int fa_b200_pixel_reduce_noalloc(
     const fa_view* a, const fa_view* b, const double* luma, int op, double param,
     double psnr_bias, double* out_per_image, double* out_total, double* out_psnr_per_image,
     double* out_psnr_total, uint64_t* out_isum_per_image, int device, void* stream) {
+  FAB_PENDING();
   using namespace fab;
   if (!a || !b || !a->data || !b->data) return FA_E_ARG;
   if (a->dtype != b->dtype) return FA_E_DTYPE;

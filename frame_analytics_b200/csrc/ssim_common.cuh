@@ -71,6 +71,8 @@ struct SsimArgs {
   const float* gs;
   const float* gcs;
   float grad_norm;
+  unsigned int* err;  // host-mapped error word of the bounded waits
+  const float* wdev;  // device taps (reference-compatible calls), else null
   float* dx;
   float* dy;
 };
@@ -125,19 +127,55 @@ __device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned
                "r"(bytes)
                : "memory");
 }
-// Bounded wait on a phase: gives up after ~2^24 polls instead of hanging.
-__device__ __forceinline__ void mbar_wait(unsigned long long* bar, unsigned parity) {
-  const unsigned a = smem_u32(bar);
-  for (int i = 0; i < (1 << 24); ++i) {
-    unsigned done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return;
+__device__ __forceinline__ bool mbar_try(unsigned a, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Slow path of a bounded wait: polls until the phase completes, `limit_ns`
+// of wall time passes, or another wait has already failed (the error word is
+// set).  On giving up it records FA_E_TIMEOUT in the error word, which the
+// next call of any entry point turns into its return status, and returns so
+// that the kernel finishes instead of hanging; its outputs are then garbage
+// and reported as such.  `err` is a host-mapped word (it may be null: the
+// wait then only gives up).
+static __device__ __noinline__ void mbar_wait_slow(unsigned a, unsigned parity, unsigned* err,
+                                            unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (unsigned i = 1;; ++i) {
+    if (mbar_try(a, parity)) return;
+    if ((i & 255u) == 0u) {
+      const bool failed = err && *reinterpret_cast<volatile unsigned*>(err) != 0u;
+      if (failed || globaltimer_ns() - t0 > limit_ns) {
+        if (err) {
+          *reinterpret_cast<volatile unsigned*>(err) = (unsigned)FA_E_TIMEOUT;
+          __threadfence_system();
+        }
+        return;
+      }
+    }
   }
+}
+// Bounded wait on a phase: a few fast polls, then the timed slow path (two
+// seconds: a row copy takes microseconds).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ void mbar_wait(unsigned long long* bar, unsigned parity,
+                                          unsigned* err) {
+  const unsigned a = smem_u32(bar);
+#pragma unroll 1
+  for (int i = 0; i < 32; ++i)
+    if (mbar_try(a, parity)) return;
+  mbar_wait_slow(a, parity, err, kWaitLimitNs);
 }
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -531,6 +569,20 @@ static __device__ __noinline__ void ssim_fwd_finalize(const SsimArgs& p, int bpp
   }
   t = block_sum(t, s_red);
   if (threadIdx.x == 0 && p.out_total) *p.out_total = t / (npix * p.Cm * (double)p.N);
+}
+
+// The Gaussian taps of the reference-compatible entry points arrive as a
+// device pointer (`wdev`): every thread reads them (a broadcast from L1/L2)
+// into a private copy of the arguments, so no host copy of the window, and
+// no synchronisation, is needed.
+template <int KW>
+__device__ __forceinline__ void load_device_taps(SsimArgs& q) {
+#pragma unroll
+  for (int j = 0; j < KW; ++j) {
+    const float w = __ldg(q.wdev + j);
+    q.w[j] = w;
+    q.w2[j] = make_float2(w, w);
+  }
 }
 
 }  // namespace fab

@@ -1,331 +1,15 @@
-// SSIM forward on sm_100a: per-plane SSIM and cs means, the SSIM map, per
-// image and batch means -- one launch.  Replaces the reference's
-// ssim_fused_kernel REDUCE/MAP/CS modes + finalize (fa_cuda.cu:389-637,
-// 182-234, host 1167-1283).  Layout notes: ssim_common.cuh.
-#include <type_traits>
-
-#include "ssim_common.cuh"
+// SSIM forward on sm_100a, host side: plans, TMA maps and dispatch.
+// Replaces the reference's host path of ssim_fused_kernel
+// (fa_cuda.cu:1167-1283).  Kernel: ssim_fwd.cuh.
+#include "ssim_fwd.cuh"
 
 namespace fab {
 
-// Squared-difference accumulator: exact for uint8, double otherwise (float
-// terms for f16/bf16/f32 as the pixel reductions form them, double for f64).
-template <typename T>
-using SqAcc = typename std::conditional<std::is_same<T, unsigned char>::value ||
-                                            std::is_same<T, unsigned short>::value,
-                                        unsigned long long, double>::type;
-
-// stage_convert plus the squared differences of the staged elements this
-// block owns: global rows [rlo, rhi) and columns [clo, chi).  Element (r, i)
-// of the staged rows is global row grow0 + r, column gcol0 + i.  Rows and
-// columns outside the image arrive as zeros in both inputs and add nothing.
-template <typename T, int KW>
-__device__ __forceinline__ void stage_convert_sq(const SsimArgs& p, const T* rawx, const T* rawy,
-                                                 float* sx, float* sy, int grow0, int gcol0,
-                                                 int rlo, int rhi, int clo, int chi,
-                                                 SqAcc<T>& acc) {
-  using R = Raw<T, KW>;
-  constexpr int N4 = KW * R::RP / 4;
-  constexpr int R4 = R::RP / 4;
-  unsigned isum = 0;  // uint8: at most a few words per thread per batch
-  for (int i = threadIdx.x; i < N4; i += Geo<KW>::NT) {
-    const int r = i / R4, c4 = i - r * R4;
-    if (4 * c4 >= R::FP) continue;
-    const int o4 = (r * R::FP) / 4 + c4;
-    const int gr = grow0 + r, gc = gcol0 + 4 * c4;
-    const bool row_own = gr >= rlo && gr < rhi;
-    float4 a, b;
-    if constexpr (std::is_same<T, float>::value) {
-      a = reinterpret_cast<const float4*>(rawx)[i];
-      b = reinterpret_cast<const float4*>(rawy)[i];
-      if (row_own) {
-        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (gc + j >= clo && gc + j < chi) {
-            const float d = av[j] - bv[j];
-            acc += (double)(d * d);
-          }
-      }
-    } else if constexpr (std::is_same<T, unsigned char>::value) {
-      const unsigned u = reinterpret_cast<const unsigned*>(rawx)[i];
-      const unsigned v = reinterpret_cast<const unsigned*>(rawy)[i];
-      if (row_own && gc + 3 >= clo && gc < chi) {
-        unsigned d = __vabsdiffu4(u, v);
-        if (gc < clo || gc + 3 >= chi) {  // a word across an ownership edge
-          unsigned mask = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (gc + j >= clo && gc + j < chi) mask |= 0xffu << (8 * j);
-          d &= mask;
-        }
-        isum = __dp4a(d, d, isum);
-      }
-      a = make_float4((float)(u & 0xff), (float)((u >> 8) & 0xff), (float)((u >> 16) & 0xff),
-                      (float)(u >> 24));
-      b = make_float4((float)(v & 0xff), (float)((v >> 8) & 0xff), (float)((v >> 16) & 0xff),
-                      (float)(v >> 24));
-    } else {
-      const T* ex = rawx + 4 * i;
-      const T* ey = rawy + 4 * i;
-      a = make_float4(Ld<T>::f(ex[0]), Ld<T>::f(ex[1]), Ld<T>::f(ex[2]), Ld<T>::f(ex[3]));
-      b = make_float4(Ld<T>::f(ey[0]), Ld<T>::f(ey[1]), Ld<T>::f(ey[2]), Ld<T>::f(ey[3]));
-      if (row_own) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (gc + j >= clo && gc + j < chi) {
-            if constexpr (std::is_same<T, double>::value) {
-              const double d = ex[j] - ey[j];
-              acc += d * d;
-            } else if constexpr (std::is_same<T, unsigned short>::value) {
-              const long long d = (long long)ex[j] - (long long)ey[j];
-              acc += (unsigned long long)(d * d);
-            } else {
-              const float d = Ld<T>::f(ex[j]) - Ld<T>::f(ey[j]);
-              acc += (double)(d * d);
-            }
-          }
-      }
-    }
-    a.x -= p.shift; a.y -= p.shift; a.z -= p.shift; a.w -= p.shift;
-    b.x -= p.shift; b.y -= p.shift; b.z -= p.shift; b.w -= p.shift;
-    reinterpret_cast<float4*>(sx)[o4] = a;
-    reinterpret_cast<float4*>(sy)[o4] = b;
-  }
-  if constexpr (std::is_same<T, unsigned char>::value) acc += isum;
-}
-
-// Register-path staging written straight to shared memory, element by
-// element (no staging arrays stay live): LUMA projects RGB first; SQ also
-// sums the owned squared differences of the unshifted values.
-template <typename T, bool LUMA, bool SQ, int KW>
-__device__ __forceinline__ void stage_direct(const SsimArgs& p, long long base, int row0,
-                                             int col0, float* sx, float* sy, int rlo, int rhi,
-                                             int clo, int chi, SqAcc<T>& acc) {
-  using G = Geo<KW>;
-  constexpr int FP = Raw<T, KW>::FP;
-  const T* X = reinterpret_cast<const T*>(p.x);
-  const T* Y = reinterpret_cast<const T*>(p.y);
-#pragma unroll 4
-  for (int e = 0; e < G::NE; ++e) {
-    const int idx = threadIdx.x + e * G::NT;
-    if (idx >= KW * G::SW) break;
-    const int r = idx / G::SW;
-    const int c = idx - r * G::SW;
-    const int gr = row0 + r, gc = col0 + c;
-    float a = 0.f, b = 0.f;
-    if (gr >= 0 && gr < p.H && gc >= 0 && gc < p.W) {
-      const long long o = base + (long long)gr * p.sh + gc;
-      if constexpr (LUMA) {
-        a = fmaf(p.lk0, Ld<T>::f(ldro(X + o)),
-                 fmaf(p.lk1, Ld<T>::f(ldro(X + o + p.sc)),
-                      fmaf(p.lk2, Ld<T>::f(ldro(X + o + 2 * p.sc)), p.lk3)));
-        b = fmaf(p.lk0, Ld<T>::f(ldro(Y + o)),
-                 fmaf(p.lk1, Ld<T>::f(ldro(Y + o + p.sc)),
-                      fmaf(p.lk2, Ld<T>::f(ldro(Y + o + 2 * p.sc)), p.lk3)));
-      } else {
-        const T ra = ldro(X + o), rb = ldro(Y + o);
-        a = Ld<T>::f(ra);
-        b = Ld<T>::f(rb);
-        if constexpr (SQ) {
-          if (gr >= rlo && gr < rhi && gc >= clo && gc < chi) {
-            if constexpr (std::is_same<T, unsigned char>::value ||
-                          std::is_same<T, unsigned short>::value) {
-              const long long d = (long long)ra - (long long)rb;
-              acc += (unsigned long long)(d * d);
-            } else if constexpr (std::is_same<T, double>::value) {
-              const double d = ra - rb;
-              acc += d * d;
-            } else {
-              const float d = a - b;
-              acc += (double)(d * d);
-            }
-          }
-        }
-      }
-      a -= p.shift;
-      b -= p.shift;
-    }
-    sx[r * FP + c] = a;
-    sy[r * FP + c] = b;
-  }
-}
-
-// Last block, after the SSIM finaliser: per-plane squared-difference sums in a
-// fixed order, then per-image and batch MSE and PSNR (bias - 10 log10 mse).
-template <typename A>
-static __device__ __noinline__ void sq_finalize(const SsimArgs& p, int bpp) {
-  __shared__ A s_red[32];
-  A* part = static_cast<A*>(p.part_sq);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int nw = blockDim.x >> 5;
-  for (int pl = wid; pl < p.P; pl += nw) {
-    A s = 0;
-    for (int i = lane; i < bpp; i += 32) s += part[(long long)pl * bpp + i];
-    s = warp_sum(s);
-    if (lane == 0) part[(long long)pl * bpp] = s;
-  }
-  __syncthreads();
-  __threadfence_block();
-  const double per_img = (double)p.C * p.H * p.W;
-  A t = 0;
-  for (int n = threadIdx.x; n < p.N; n += blockDim.x) {
-    A s = 0;
-    for (int c = 0; c < p.C; ++c) s += part[(long long)(n * p.C + c) * bpp];
-    const double mse = (double)s / per_img;
-    if (p.out_mse_per_image) p.out_mse_per_image[n] = mse;
-    if (p.out_psnr_per_image) p.out_psnr_per_image[n] = p.psnr_bias - 10.0 * log10(mse);
-    if constexpr (std::is_same<A, unsigned long long>::value)
-      if (p.out_ssd_per_image) p.out_ssd_per_image[n] = s;
-    t += s;
-  }
-  t = block_sum(t, s_red);
-  if (threadIdx.x == 0) {
-    const double mse = (double)t / (per_img * p.N);
-    if (p.out_mse_total) *p.out_mse_total = mse;
-    if (p.out_psnr_total) *p.out_psnr_total = p.psnr_bias - 10.0 * log10(mse);
-  }
-}
-
-template <typename T, int KW, bool CS, int STAGE, bool SQ = false>
-__global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_constant__ SsimArgs p) {
-  using G = Geo<KW>;
-  using R = Raw<T, KW>;
-  constexpr bool TMA = (STAGE == STAGE_TMA);
-  extern __shared__ __align__(128) float4 smem4[];
-  float4* sH = smem4;                                        // [KW][NT]
-  float* sX = reinterpret_cast<float*>(smem4 + KW * G::NT);  // [KW][FP]
-  float* sY = sX + KW * R::FP;
-  T* rawX = R::kInPlace ? reinterpret_cast<T*>(sX)
-                        : reinterpret_cast<T*>(reinterpret_cast<char*>(sX) + R::kFloatBytes);
-  T* rawY = R::kInPlace ? reinterpret_cast<T*>(sY) : rawX + KW * R::RP;
-  __shared__ double s_red[32];
-  __shared__ int s_flag;
-  __shared__ __align__(8) unsigned long long s_bar;
-
-  const int t = threadIdx.x;
-  const int lane = t & 31, warp = t >> 5;
-  const int plane = blockIdx.z;
-  const int pn = plane / p.Cm, pc = plane - pn * p.Cm;
-  const long long base = (long long)pn * p.sn + (long long)pc * p.sc;
-  const int c0 = blockIdx.x * G::NT;
-  const int r0 = blockIdx.y * p.RH;
-  const int rows = min(p.RH, p.Hout - r0);
-  const int col = c0 + t;
-  const bool col_ok = col < p.Wout;
-  const int iters = (rows + KW - 1 + KW - 1) / KW;
-  float* map = p.map_out ? p.map_out + (long long)plane * p.Hout * p.Wout : nullptr;
-  // TMA x coordinate of the strip, rounded down to 16 bytes, and the offset of
-  // column c0 inside the staged rows
-  const int xm = c0 + p.tma_d;
-  const int x0 = TMA ? (xm / R::XA) * R::XA : 0;
-  const int sofs = TMA ? xm - x0 : 0;
-
-  if constexpr (TMA) {
-    if (t == 0) mbar_init(&s_bar, 1);
-    fence_async_smem();
-    __syncthreads();
-    stage_tma<T, KW>(p, pn, pc, r0, x0, rawX, rawY, &s_bar);
-  }
-
-  float4 ring[KW];
-#pragma unroll
-  for (int k = 0; k < KW; ++k) ring[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  double acc_s = 0.0, acc_cs = 0.0;
-  // SQ: input pixels this block owns for the squared-difference sums (the
-  // last strip / chunk also owns the K-1 columns / rows past the map)
-  SqAcc<T> acc_sq = 0;
-  const int sq_chi = (blockIdx.x == gridDim.x - 1) ? p.W : c0 + G::NT;
-  const int sq_rhi = (blockIdx.y == gridDim.y - 1) ? p.H : r0 + rows;
-
-  for (int m = 0; m < iters; ++m) {
-    if constexpr (!TMA) {
-      // direct staging: nothing stays live across the compute (the block's
-      // second resident copy hides the load latency); the previous batch's
-      // horizontal pass ended at a barrier
-      stage_direct<T, STAGE == STAGE_LUMA, SQ, KW>(p, base, r0 + m * KW, c0, sX, sY, r0, sq_rhi,
-                                                   c0, sq_chi, acc_sq);
-    }
-    if constexpr (TMA) {
-      mbar_wait(&s_bar, m & 1);
-      if constexpr (SQ)
-        stage_convert_sq<T, KW>(p, rawX, rawY, sX, sY, r0 + m * KW, x0 - p.tma_d, r0, sq_rhi, c0,
-                                sq_chi, acc_sq);
-      else
-        stage_convert<T, KW>(p, rawX, rawY, sX, sY);
-    }
-    __syncthreads();
-    // horizontal: warp k -> staged row k, lane -> columns [lane*KW, lane*KW+KW)
-    {
-      const float* rx = sX + warp * R::FP + sofs + lane * KW;
-      const float* ry = sY + warp * R::FP + sofs + lane * KW;
-      float4* out = sH + warp * G::NT + lane * KW;
-      hblur4<KW, TMA>(p, rx, ry, out);  // TMA staging implies symmetric taps
-    }
-    __syncthreads();
-    const bool more = (m + 1 < iters);
-    if constexpr (TMA) {
-      if (more) stage_tma<T, KW>(p, pn, pc, r0 + (m + 1) * KW, x0, rawX, rawY, &s_bar);
-    }
-    // vertical + epilogue; interior batches (every slot a map row of this
-    // chunk) skip the per-row tests
-    float fs = 0.f, fcs = 0.f;
-    auto rows_step = [&](auto chk) {
-      constexpr bool CHK = decltype(chk)::value;
-#pragma unroll
-      for (int k = 0; k < KW; ++k) {
-        ring[k] = sH[k * G::NT + t];
-        const int o = m * KW + k - (KW - 1);
-        if (col_ok && (!CHK || (o >= 0 && o < rows))) {
-          const Moments mo = moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
-          // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
-          // cs = A2 / B2 = A2 B1 / (B1 B2)
-          const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
-          const float S = mo.A1 * mo.A2 * inv;
-          if (CS) fcs += mo.A2 * mo.B1 * inv;
-          fs += S;
-          if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
-        }
-      }
-    };
-    const int o_first = m * KW - (KW - 1);
-    if (o_first >= 0 && o_first + KW - 1 < rows) rows_step(std::false_type{});
-    else rows_step(std::true_type{});
-    acc_s += (double)fs;
-    acc_cs += (double)fcs;
-  }
-
-  const int bpp = p.strips * p.chunks;
-  const long long pidx = (long long)plane * bpp + blockIdx.y * p.strips + blockIdx.x;
-  acc_s = block_sum(acc_s, s_red);
-  if (t == 0) p.part_s[pidx] = acc_s;
-  if (CS) {
-    acc_cs = block_sum(acc_cs, s_red);
-    if (t == 0) p.part_cs[pidx] = acc_cs;
-  }
-  if constexpr (SQ) {
-    __shared__ SqAcc<T> s_red_q[32];
-    acc_sq = block_sum(acc_sq, s_red_q);
-    if (t == 0) static_cast<SqAcc<T>*>(p.part_sq)[pidx] = acc_sq;
-  }
-  if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag)) {
-    ssim_fwd_finalize(p, bpp);
-    if constexpr (SQ) {
-      __syncthreads();
-      sq_finalize<SqAcc<T>>(p, bpp);
-    }
-  }
-}
+int fwd_dw_dispatch(const SsimArgs& p, int dtype, bool cs, int K, int device, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-
-template <typename T, int KW, int STAGE>
-static constexpr size_t fwd_smem() {
-  return sizeof(float4) * KW * Geo<KW>::NT + Raw<T, KW>::kFloatBytes +
-         (STAGE == STAGE_TMA ? Raw<T, KW>::kRawBytes : 0);
-}
 
 static SsimPlan fwd_plan(int Hout, int Wout, int K, int planes, int device) {
   const int nt = 32 * K;
@@ -336,18 +20,6 @@ size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device) {
   const SsimPlan pl = fwd_plan(Hout, Wout, K, planes, device);
   // partial sums: SSIM, cs and squared differences (8 bytes each per block)
   return FAB_COUNTER_BYTES + 3 * sizeof(double) * (size_t)planes * pl.strips * pl.chunks;
-}
-
-template <typename T, int KW, bool CS, int STAGE, bool SQ = false>
-static int launch_fwd(const SsimArgs& p, int device, cudaStream_t st) {
-  auto kern = ssim_fwd_kernel<T, KW, CS, STAGE, SQ>;
-  const size_t sm = fwd_smem<T, KW, STAGE>();
-  static bool done[64] = {false};
-  FAB_TRY(ensure_smem(kern, sm, device, done));
-  dim3 grid(p.strips, p.chunks, p.P);
-  kern<<<grid, 32 * KW, sm, st>>>(p);
-  FAB_LAUNCH_CHECK();
-  return FA_OK;
 }
 
 template <typename T, bool CS, int STAGE>
@@ -476,8 +148,9 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
                   int K, double shift, double C1, double C2, float* map_out, void* ws,
                   size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
                   double* out_per_image, double* out_total, int device, cudaStream_t st,
-                  const SqOut* sq) {
-  if (!x.data || !y.data || !taps || !ws) return FA_E_ARG;
+                  const SqOut* sq, const float* wdev) {
+  if (!x.data || !y.data || (!taps && !wdev) || !ws) return FA_E_ARG;
+  if (wdev && (sq || luma)) return FA_E_ARG;
   if (sq && (luma || out_plane_cs)) return FA_E_ARG;
   if (x.n <= 0 || x.c <= 0 || x.h <= 0 || x.w <= 0) return FA_E_SHAPE;
   if (x.n != y.n || x.c != y.c || x.h != y.h || x.w != y.w) return FA_E_SHAPE;
@@ -487,6 +160,7 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
   const int Hout = x.h - K + 1, Wout = x.w - K + 1;
   if (Hout <= 0 || Wout <= 0) return FA_E_SHAPE;
   SsimArgs p{};
+  p.err = wait_error_word();
   p.x = static_cast<const char*>(x.data);
   p.y = static_cast<const char*>(y.data);
   p.sn = x.sn; p.sc = x.sc; p.sh = x.sh;
@@ -499,10 +173,13 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
   if (luma) {
     p.lk0 = (float)luma[0]; p.lk1 = (float)luma[1]; p.lk2 = (float)luma[2]; p.lk3 = (float)luma[3];
   }
-  for (int j = 0; j < K; ++j) {
-    p.w[j] = taps[j];
-    p.w2[j] = make_float2(taps[j], taps[j]);
+  if (taps) {
+    for (int j = 0; j < K; ++j) {
+      p.w[j] = taps[j];
+      p.w2[j] = make_float2(taps[j], taps[j]);
+    }
   }
+  p.wdev = wdev;
   const SsimPlan pl = fwd_plan(Hout, Wout, K, p.P, device);
   p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
   const size_t nb = (size_t)p.P * pl.strips * pl.chunks;
@@ -525,6 +202,7 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
   const bool cs = out_plane_cs != nullptr;
   if (dtype < 0 || dtype > 5) return FA_E_DTYPE;
   int stage = luma ? STAGE_LUMA : STAGE_GENERIC;
+  if (wdev) return fwd_dw_dispatch(p, dtype, cs, K, device, st);
   bool sym = true;  // the TMA kernels read only the first (K+1)/2 taps
   for (int j = 0; j < K; ++j) sym = sym && taps[j] == taps[K - 1 - j];
   if (!luma && sym) {

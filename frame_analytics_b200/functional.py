@@ -44,68 +44,66 @@ def set_compile_enabled(flag: bool) -> None:
 # input handling (functional.py:141-271)
 # --------------------------------------------------------------------------- #
 
+# Peak value of integer sample types; every floating type is taken as [0, 1].
+_INT_PEAK = {torch.uint8: 255.0, torch.int16: 65535.0, torch.int32: 65535.0}
+if getattr(torch, "uint16", None) is not None:
+    _INT_PEAK[torch.uint16] = 65535.0
+
+
 def _infer_data_range(t: torch.Tensor) -> float:
-    if t.dtype == torch.uint8:
-        return 255.0
-    if t.dtype in (torch.int16, torch.int32):
-        return 65535.0
-    if getattr(torch, "uint16", None) is not None and t.dtype == torch.uint16:
-        return 65535.0
-    return 1.0
+    return _INT_PEAK.get(t.dtype, 1.0)
 
 
 def _as_nchw(t: torch.Tensor) -> torch.Tensor:
-    if t.ndim == 2:
-        return t.unsqueeze(0).unsqueeze(0)
-    if t.ndim == 3:
-        return t.unsqueeze(0)
-    if t.ndim == 4:
-        return t
-    raise ValueError(f"expected 2/3/4-D tensor, got shape {tuple(t.shape)}")
+    """(H,W) / (C,H,W) / (N,C,H,W) as a 4-D view with leading unit axes."""
+    if not 2 <= t.ndim <= 4:
+        raise ValueError(f"images must have 2, 3 or 4 dimensions (H,W / C,H,W / "
+                         f"N,C,H,W); this one has shape {tuple(t.shape)}")
+    return t.view((1,) * (4 - t.ndim) + tuple(t.shape)) if t.ndim < 4 else t
 
 
 def _check_pair(x: torch.Tensor, y: torch.Tensor):
-    if x.shape != y.shape:
-        raise ValueError(f"shape mismatch: {tuple(x.shape)} vs {tuple(y.shape)}")
-    if x.device != y.device:
-        raise ValueError(f"device mismatch: {x.device} vs {y.device}")
+    for what, u, v in (("shape", tuple(x.shape), tuple(y.shape)),
+                       ("device", x.device, y.device)):
+        if u != v:
+            raise ValueError(f"the two images differ in {what}: {u} and {v}")
     return _as_nchw(x), _as_nchw(y)
 
 
 def _resolve_luma(luma) -> Optional[str]:
-    if luma is None or luma is False:
-        return None
-    if luma is True:
-        return "bt601"
-    if isinstance(luma, str):
-        if luma not in LUMA_COEFFS:
-            raise ValueError(f"unknown luma mode {luma!r}; "
-                             f"expected one of {sorted(LUMA_COEFFS)}")
+    """None/False -> no projection, True -> bt601, a name -> that convention."""
+    if isinstance(luma, bool) or luma is None:
+        return "bt601" if luma else None
+    if not isinstance(luma, str):
+        raise TypeError(f"luma is None, a bool or a convention name, "
+                        f"not {type(luma).__name__}")
+    if luma in LUMA_COEFFS:
         return luma
-    raise TypeError(f"luma must be None, a bool or a string, got {type(luma).__name__}")
+    raise ValueError(f"luma convention {luma!r} is not one of {sorted(LUMA_COEFFS)}")
 
 
 def _crop_border(t: torch.Tensor, b: int) -> torch.Tensor:
-    if not b:
-        return t
+    """Drop `b` pixels on every side, as a view (the kernels take strides)."""
     if b < 0:
-        raise ValueError(f"crop_border must be >= 0, got {b}")
-    h, w = t.shape[-2], t.shape[-1]
-    if h <= 2 * b or w <= 2 * b:
-        raise ValueError(f"crop_border={b} removes the whole {h}x{w} image")
-    return t[..., b:h - b, b:w - b]
+        raise ValueError(f"crop_border cannot be negative ({b})")
+    if b == 0:
+        return t
+    h, w = t.shape[-2:]
+    if min(h, w) <= 2 * b:
+        raise ValueError(f"crop_border={b} leaves nothing of a {h}x{w} image")
+    return t.narrow(-2, b, h - 2 * b).narrow(-1, b, w - 2 * b)
 
 
 def _prep(x, y, luma, crop_border, data_range):
-    """Shape check, border crop (a view), luma resolution -> (x4, y4, L, mode)."""
+    """Validate a pair and return (x4, y4, L, luma mode): 4-D views with the
+    border already cropped; L is `data_range` or the dtype's peak."""
     x4, y4 = _check_pair(x, y)
-    L = float(data_range) if data_range is not None else _infer_data_range(x4)
     mode = _resolve_luma(luma)
-    x4 = _crop_border(x4, crop_border)
-    y4 = _crop_border(y4, crop_border)
     if mode is not None and x4.shape[1] != 3:
-        raise ValueError(f"luma needs a 3-channel image, got {x4.shape[1]} channels")
-    return x4, y4, L, mode
+        raise ValueError(f"a luma projection needs RGB input (3 channels), "
+                         f"not {x4.shape[1]}")
+    L = _infer_data_range(x4) if data_range is None else float(data_range)
+    return _crop_border(x4, crop_border), _crop_border(y4, crop_border), L, mode
 
 
 def _luma_k(mode: Optional[str], L: float):
@@ -306,19 +304,14 @@ _window_cache: dict = {}
 
 def gaussian_window_1d(win_size: int = 11, sigma: float = 1.5, *, device=None,
                        dtype=torch.float32) -> torch.Tensor:
-    """Sum-normalised 1-D Gaussian (functional.py:397-420); the 2-D window is
-    its outer product.  Cached per (size, sigma, device, dtype)."""
-    key = (win_size, sigma, str(device), dtype)
-    w = _window_cache.get(key)
-    if w is not None:
-        return w
-    r = (win_size - 1) / 2.0
-    coords = torch.arange(win_size, dtype=torch.float64) - r
-    g = torch.exp(-(coords * coords) / (2.0 * sigma * sigma))
-    g = g / g.sum()
-    w = g.to(device=device, dtype=dtype)
-    _window_cache[key] = w
-    return w
+    """The separable SSIM window (functional.py:397-420 of the reference): a
+    1-D Gaussian normalised to sum 1; the 2-D window is its outer product.
+    One tensor per (size, sigma, device, dtype) is kept."""
+    key = (win_size, float(sigma), str(device), dtype)
+    if key not in _window_cache:
+        _window_cache[key] = torch.tensor(backend.gaussian_taps(int(win_size), float(sigma)),
+                                          dtype=torch.float64).to(device=device, dtype=dtype)
+    return _window_cache[key]
 
 
 def _reject_double_backward() -> None:
@@ -636,12 +629,12 @@ class _Pool2Fn(torch.autograd.Function):
 
 
 def _ms_weights(w, device) -> torch.Tensor:
-    key = (w, str(device))
-    t = _ms_weight_cache.get(key)
-    if t is None:
-        t = torch.tensor(w, dtype=torch.float64, device=device).view(-1, 1, 1)
-        _ms_weight_cache[key] = t
-    return t
+    """Per-scale exponents as a (scales, 1, 1) float64 tensor on `device`."""
+    key = (tuple(float(v) for v in w), str(device))
+    if key not in _ms_weight_cache:
+        _ms_weight_cache[key] = torch.as_tensor(key[0], dtype=torch.float64,
+                                                device=device).reshape(len(key[0]), 1, 1)
+    return _ms_weight_cache[key]
 
 
 _ms_weight_cache: dict = {}

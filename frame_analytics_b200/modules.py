@@ -4,11 +4,13 @@ conventions (frame_analytics/modules.py:42-241): SSIM/MSSSIM loss is
 
 from __future__ import annotations
 
+import math
 from typing import Optional, Sequence
 
 import torch
 from torch import nn
 
+from . import backend
 from .functional import (MS_SSIM_WEIGHTS, charbonnier, gms, gmsd, huber, l1, ms_ssim,
                          mse, psnr, ssim)
 
@@ -155,16 +157,43 @@ class Huber(_PixelLoss):
         self.extra = {"delta": float(delta)}
 
 
+class _Slot:
+    """One pair of device frames with its own staging, events and graph."""
+
+    __slots__ = ("ref", "dist", "host", "uploaded", "scored", "graph", "out")
+
+    def __init__(self, shape, dtype, device, pinned: bool):
+        self.ref = torch.zeros(shape, dtype=dtype, device=device)
+        self.dist = torch.zeros(shape, dtype=dtype, device=device)
+        self.host = None
+        if pinned:
+            try:
+                self.host = (torch.empty(shape, dtype=dtype, pin_memory=True),
+                             torch.empty(shape, dtype=dtype, pin_memory=True))
+            except RuntimeError:  # no pinned memory available: pageable copies
+                self.host = None
+        self.uploaded = torch.cuda.Event()
+        self.scored = torch.cuda.Event()
+        self.graph = None
+        self.out = None
+
+
 class StreamingMetrics:
-    """Score a stream of frame pairs of one fixed shape (modules.py:308-451 of
-    the reference): the metrics are computed into static device buffers, by
-    one CUDA-graph replay per pair when capture succeeds.
+    """Score a stream of frame pairs of one fixed shape (the reference's
+    streaming scorer, modules.py:308-451).
+
+    Two frame slots alternate.  Pair k is uploaded on a copy stream into slot
+    k % 2 while pair k-1 may still be scored on the scoring stream, so with
+    ``update(..., as_float=False)`` uploads overlap scoring.  Each slot has
+    its own CUDA graph (one replay per pair when capture succeeds, eager calls
+    otherwise), and the instance owns its kernel scratch
+    (``backend.private_workspaces``): several instances may replay at the
+    same time on different streams.
 
     ``metrics`` defaults to ``("mse", "psnr", "ssim")``, which
     :func:`frame_analytics_b200.metrics` computes in a single launch and one
-    read of the pair.  Host frames are staged through pinned buffers.  The
-    reference's ``lpips`` and ``ssimulacra2`` are outside this package and
-    raise ``NotImplementedError``."""
+    read of the pair.  The reference's ``lpips`` and ``ssimulacra2`` are
+    outside this package and raise ``NotImplementedError``."""
 
     _KNOWN = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber")
     _ELSEWHERE = ("lpips", "ssimulacra2")
@@ -179,71 +208,102 @@ class StreamingMetrics:
         self.dtype = dtype
         self.shape = tuple(shape)
         self.metrics = tuple(metrics)
-        other = [m for m in self.metrics if m in self._ELSEWHERE]
-        if other:
-            raise NotImplementedError(f"{other} are not part of frame_analytics_b200")
+        elsewhere = [m for m in self.metrics if m in self._ELSEWHERE]
+        if elsewhere:
+            raise NotImplementedError(f"{elsewhere} are not part of frame_analytics_b200")
         unknown = [m for m in self.metrics if m not in self._KNOWN]
         if unknown:
             raise ValueError(f"unknown metric(s) {unknown}; expected any of {list(self._KNOWN)}")
-        self.ref = torch.zeros(self.shape, dtype=dtype, device=self.device)
-        self.dist = torch.zeros(self.shape, dtype=dtype, device=self.device)
-        self._L = float(data_range) if data_range is not None else _infer_data_range(self.ref)
-        self._host = None
-        if pinned_staging:
-            self._host = (torch.empty(self.shape, dtype=dtype, pin_memory=True),
-                          torch.empty(self.shape, dtype=dtype, pin_memory=True))
-        self._graph = None
-        self._static_out = None
-        if use_cuda_graph:
-            self._try_capture()
+        self._scratch: dict = {}
+        self._copy = torch.cuda.Stream(device=self.device)
+        self._work = torch.cuda.Stream(device=self.device)
+        with torch.cuda.device(self.device):
+            self._slots = [_Slot(self.shape, dtype, self.device, pinned_staging) for _ in range(2)]
+        self._L = (float(data_range) if data_range is not None
+                   else _infer_data_range(self._slots[0].ref))
+        self._turn = 0
+        if use_cuda_graph and not all(self._record(s) for s in self._slots):
+            for s in self._slots:  # all or nothing: graph replay is an optimisation
+                s.graph = s.out = None
 
-    def _compute(self):
+    # -- scoring ---------------------------------------------------------- #
+
+    def _score(self, slot: _Slot) -> dict:
         from .functional import metrics as _metrics
-        return _metrics(self.ref, self.dist, self.metrics, data_range=self._L)
+        with backend.private_workspaces(self._scratch):
+            return _metrics(slot.ref, slot.dist, self.metrics, data_range=self._L)
 
-    def _try_capture(self):
+    def _record(self, slot: _Slot) -> bool:
+        """Capture the slot's scoring into a graph on the scoring stream.  The
+        eager passes first set the kernels' one-time attributes and allocate
+        (zeroed) scratch outside the capture."""
         try:
-            side = torch.cuda.Stream(device=self.device)
-            side.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(side):
-                for _ in range(3):  # kernels' one-time attributes, workspaces
-                    self._compute()
-            torch.cuda.current_stream(self.device).wait_stream(side)
-            torch.cuda.synchronize(self.device)
+            self._work.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self._work):
+                self._score(slot)
+                self._score(slot)
+            self._work.synchronize()
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self._static_out = self._compute()
-            self._graph = g
-        except Exception:  # capture is an optimisation: fall back to eager calls
-            self._graph = None
-            self._static_out = None
+            with torch.cuda.graph(g, stream=self._work):
+                out = self._score(slot)
+            slot.graph, slot.out = g, out
+            return True
+        except Exception:
+            slot.graph = slot.out = None
+            return False
 
-    def _stage(self, buf: torch.Tensor, src, slot: int) -> None:
-        if not torch.is_tensor(src):
-            src = torch.from_numpy(src)
-        if tuple(src.shape) != self.shape:
-            src = src.reshape(self.shape)
-        if src.is_cuda:
-            buf.copy_(src, non_blocking=True)
-        elif self._host is not None:
-            self._host[slot].copy_(src)
-            buf.copy_(self._host[slot], non_blocking=True)
+    # -- staging ---------------------------------------------------------- #
+
+    def _as_frame(self, src) -> torch.Tensor:
+        t = src if torch.is_tensor(src) else torch.from_numpy(src)
+        if tuple(t.shape) != self.shape:
+            if t.numel() != math.prod(self.shape):
+                raise ValueError(f"frame of shape {tuple(t.shape)} does not fit {self.shape}")
+            t = t.reshape(self.shape)
+        return t
+
+    def _upload(self, dst: torch.Tensor, src, pinned: Optional[torch.Tensor]) -> None:
+        """Enqueue src -> dst on the copy stream (the caller holds it current)."""
+        t = self._as_frame(src)
+        if t.is_cuda:
+            dst.copy_(t, non_blocking=True)
+            t.record_stream(self._copy)  # keep the source alive until the copy ran
+        elif pinned is not None:
+            pinned.copy_(t)  # host memcpy; the slot's previous upload has finished
+            dst.copy_(pinned, non_blocking=True)
         else:
-            buf.copy_(src)
+            dst.copy_(t)
 
     def update(self, ref, dist, *, as_float: bool = True):
-        """Score one frame pair; returns a dict metric -> value."""
-        self._stage(self.ref, ref, 0)
-        self._stage(self.dist, dist, 1)
-        if self._graph is not None:
-            self._graph.replay()
-            out = self._static_out
-        else:
-            out = self._compute()
+        """Score one frame pair; returns a dict metric -> value (Python floats,
+        or 0-d / per-image device tensors with ``as_float=False``)."""
+        slot = self._slots[self._turn]
+        self._turn ^= 1
+        slot.scored.synchronize()  # this slot's previous pair is done with its buffers
+        caller = torch.cuda.current_stream(self.device)
+        self._copy.wait_stream(caller)  # device frames written on the caller's stream
+        with torch.cuda.stream(self._copy):
+            self._upload(slot.ref, ref, slot.host[0] if slot.host else None)
+            self._upload(slot.dist, dist, slot.host[1] if slot.host else None)
+            slot.uploaded.record(self._copy)
+        self._work.wait_event(slot.uploaded)
+        with torch.cuda.stream(self._work):
+            if slot.graph is not None:
+                slot.graph.replay()
+                res = slot.out
+            else:
+                res = self._score(slot)
+            if not as_float:
+                res = {k: v.clone() for k, v in res.items()}
+            slot.scored.record(self._work)
         if as_float:
-            return {k: float(v) for k, v in out.items()}
-        return {k: v.clone() for k, v in out.items()}
+            slot.scored.synchronize()
+            return {k: float(v) for k, v in res.items()}
+        caller.wait_stream(self._work)
+        for v in res.values():
+            v.record_stream(caller)
+        return res
 
     @property
     def graph_captured(self) -> bool:
-        return self._graph is not None
+        return all(s.graph is not None for s in self._slots)

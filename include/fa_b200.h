@@ -81,6 +81,12 @@ extern "C" {
 #define FA_E_ARG 5
 #define FA_E_INTERNAL 6
 #define FA_E_NOCUDA 7
+/* Extension, no counterpart in the reference: a bounded device-side wait (a
+ * TMA row copy that never completed) gave up.  Kernels run asynchronously, so
+ * the code is returned by the first compute call made after the failing
+ * kernel has finished; that call enqueues nothing.  The failing kernel's
+ * outputs are garbage. */
+#define FA_E_TIMEOUT 8
 
 /* "not an MSE reduction, skip the dB conversion" (fa_abi.h:67) */
 #define FA_PSNR_NONE (-1.0e300)
@@ -426,6 +432,14 @@ FA_B200_API int fa_b200_pixel_reduce_noalloc(
     double param, double psnr_bias, double* out_per_image, double* out_total,
     double* out_psnr_per_image, double* out_psnr_total,
     uint64_t* out_isum_per_image, int device, void* stream);
+
+/* No counterpart in the reference: test hook of the bounded device-side
+ * waits.  Launches one thread that waits `limit_ns` (at most 1 s) for an
+ * mbarrier phase that nothing completes and then records FA_E_TIMEOUT the
+ * way a staging wait that gave up does; nothing is copied, so nothing is left
+ * in flight.  Returns FA_OK; the next compute call after the kernel has
+ * finished returns FA_E_TIMEOUT. */
+FA_B200_API int fa_b200_wait_selftest(unsigned long long limit_ns, int device, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

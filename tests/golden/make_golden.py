@@ -17,13 +17,26 @@ from __future__ import annotations
 import ctypes
 import importlib.util
 import sys
+import json
+import os
 from pathlib import Path
 
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+
+
+def _reference_path() -> Path:
+    """argv[1], else $FA_REFERENCE, else BASELINE.json's reference_path."""
+    if len(sys.argv) > 1:
+        return Path(sys.argv[1])
+    if os.environ.get("FA_REFERENCE"):
+        return Path(os.environ["FA_REFERENCE"])
+    return Path(json.loads((REPO / "BASELINE.json").read_text())["reference_path"])
+
+
+REF = _reference_path()
 
 
 def _load(name, path):

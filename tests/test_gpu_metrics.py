@@ -126,3 +126,35 @@ def test_streaming_ms_ssim_captures_with_side_streams():
         got = sm.update(a, b)
         x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
         assert abs(got["ms_ssim"] - float(fa.ms_ssim(x, y))) < 1e-12
+
+
+def test_streaming_instances_replay_concurrently_on_two_streams():
+    """Each StreamingMetrics owns its scratch and streams: two instances whose
+    graph replays overlap on the GPU both return the single-call values."""
+    shape = (2, 3, 128, 160)
+    sms = [fa.StreamingMetrics(shape, metrics=("mse", "psnr", "ssim", "ms_ssim")) for _ in range(2)]
+    assert all(s.graph_captured for s in sms)
+    pairs = [baseline_pair(shape, 6.0, seed=10 + i) for i in range(6)]
+    dev = [(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()) for a, b in pairs]
+    torch.cuda.synchronize()
+    outs = []
+    for i in range(0, 6, 2):  # both instances queued before either result is read
+        outs.append(sms[0].update(*dev[i], as_float=False))
+        outs.append(sms[1].update(*dev[i + 1], as_float=False))
+    torch.cuda.synchronize()
+    for (x, y), got in zip(dev, outs):
+        assert float(got["mse"]) == float(fa.mse(x, y))
+        assert float(got["ssim"]) == float(fa.ssim(x, y))
+        assert abs(float(got["ms_ssim"]) - float(fa.ms_ssim(x, y))) < 1e-12
+
+
+def test_streaming_overlapped_updates_keep_results_apart():
+    """Back-to-back device-result updates alternate slots; every returned
+    tensor holds its own pair's values."""
+    shape = (1, 3, 96, 128)
+    sm = fa.StreamingMetrics(shape)
+    pairs = [baseline_pair(shape, 4.0 + i, seed=20 + i) for i in range(5)]
+    res = [sm.update(a, b, as_float=False) for a, b in pairs]
+    for (a, b), got in zip(pairs, res):
+        x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        assert float(got["psnr"]) == float(fa.psnr(x, y))
