@@ -348,6 +348,128 @@ def run_only(args):
                       "GB/s": {k: nbytes / (v / 1e3) / 1e9 for k, v in res.items()}}))
 
 
+def bind_to_gpu_numa_node(dev_index: int):
+    """Pin this rank's threads to the CPUs nearest its GPU (sysfs local_cpulist
+    of the GPU's PCI function), so pinned host buffers allocated afterwards
+    land on that NUMA node.  Returns the CPU list used, or None."""
+    try:
+        pr = torch.cuda.get_device_properties(dev_index)
+        bus = f"{getattr(pr, 'pci_domain_id', 0):04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        txt = Path(f"/sys/bus/pci/devices/{bus}/local_cpulist").read_text().strip()
+        cpus = set()
+        for part in txt.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus and len(cpus) < os.cpu_count():
+            os.sched_setaffinity(0, cpus)
+            return txt
+    except Exception:
+        pass
+    return None
+
+
+CFG4_SHAPE = (64, 3, 2160, 3840)
+
+
+def cfg4_images(lo: int, hi: int, dev):
+    """Config-4 images [lo, hi) of the fixed 64-image batch: a ~ U{0..255},
+    b = clip(a + round(N(0, 8^2))), generated on the device per image from a
+    seed of its own, so every rank count sees the same bytes per image."""
+    n = hi - lo
+    x = torch.empty((n,) + CFG4_SHAPE[1:], dtype=torch.uint8, device=dev)
+    y = torch.empty_like(x)
+    for j in range(n):
+        g = torch.Generator(device=dev).manual_seed(40_000 + lo + j)
+        a = torch.randint(0, 256, CFG4_SHAPE[1:], generator=g, device=dev, dtype=torch.int16)
+        b = (a + torch.randn(a.shape, generator=g, device=dev).mul_(8.0).round_().to(torch.int16))
+        x[j] = a.to(torch.uint8)
+        y[j] = b.clamp_(0, 255).to(torch.uint8)
+    return x, y
+
+
+def cfg4_sweep(args, world: int, rank: int, dev, hbm: float):
+    """Config 4 as BASELINE.json states it: a FIXED 64x3x2160x3840 uint8 batch,
+    SSIM + GMSD with reduction='none', sharded over the ranks (strong
+    scaling).  Each step scores the local shard with one fused launch (SSIM and
+    GMSD from one read) and all-gathers the per-image values with one NCCL
+    collective.  Time = max over ranks of the device time of K steps."""
+    import torch.distributed as dist
+
+    import frame_analytics_b200 as fa
+    from frame_analytics_b200.distributed import ShardedMetrics, shard_bounds
+
+    n = CFG4_SHAPE[0]
+    lo, hi = shard_bounds(n, rank, world)
+    x, y = cfg4_images(lo, hi, dev)
+    names = ("ssim", "gmsd")
+    sharded = ShardedMetrics(names) if world > 1 else None
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step():
+        if sharded is not None:
+            return sharded(x, y, n)
+        r = fa.metrics(x, y, names, reduction="none")
+        return {k: r[k].to(torch.float64) for k in names}
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = ev(), ev()
+    t0.record()
+    for _ in range(args.steps):
+        out = step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    # the kernels alone on this shard (no gather), and the single-pass variant
+    k0, k1, s0, s1 = ev(), ev(), ev(), ev()
+    k0.record()
+    for _ in range(args.steps):
+        fa.metrics(x, y, names, reduction="none")
+    k1.record()
+    s0.record()
+    for _ in range(args.steps):
+        fa.metrics(x, y, names, reduction="none", fuse_gmsd=True)
+    s1.record()
+    torch.cuda.synchronize()
+    kern_ms = k0.elapsed_time(k1) / args.steps
+    sep_ms = s0.elapsed_time(s1) / args.steps
+    t = torch.tensor([ms, kern_ms, sep_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kern_ms, sep_ms = (float(v) for v in t)
+    diff = None
+    if rank == 0:
+        # the gathered values against one GPU scoring the whole batch
+        del x, y
+        torch.cuda.empty_cache()
+        xa, ya = cfg4_images(0, n, dev)
+        ref = fa.metrics(xa, ya, names, reduction="none")
+        diff = max(float((out[k] - ref[k].to(torch.float64)).abs().max()) for k in names)
+        del xa, ya
+    px = int(np.prod(CFG4_SHAPE))
+    per_gpu_px = (hi - lo) * int(np.prod(CFG4_SHAPE[1:]))
+    res = {
+        "workload": "cfg4: SSIM + GMSD reduction='none', fixed uint8 64x3x2160x3840 batch "
+                    "sharded over the ranks (strong scaling); the SSIM and GMSD kernels per "
+                    "shard and one NCCL all-gather of both metrics' per-image values per step",
+        "images_total": n, "images_per_rank_max": -(-n // world), "ms_per_step": ms,
+        "Gpixel/s": px / (ms / 1e3) / 1e9,
+        # SURVEY's per-pass algorithmic bytes (2 B per pixel pair, two metric passes)
+        "GB/s_algorithmic_two_passes": 4 * px / (ms / 1e3) / 1e9,
+        "hbm_frac_per_gpu_two_passes": 4 * per_gpu_px / (kern_ms / 1e3) / 1e9 / hbm,
+        "kernels_ms_per_rank": kern_ms, "single_pass_fused_ms_per_rank": sep_ms,
+        "gather_and_host_ms": ms - kern_ms,
+        "max_abs_diff_vs_single_gpu": diff,
+    }
+    del out
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -362,6 +484,7 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     backend.lib()  # fail loudly now if the kernels are missing
+    numa_cpus = bind_to_gpu_numa_node(local)
 
     hbm, hbm_kind = peaks()
     a_h, b_h = cfg2_inputs(seed=rank)
@@ -430,7 +553,10 @@ def run_ours(args):
     # 1 - ssim) inside the forward, and the in-place upstream-gradient rescale
     # in the backward (a factor of exactly 1 here: it returns at once; other
     # upstream gradients read and write d/db, 8 B/px).
-    fwd_bytes, bwd_bytes = 12 * px_step, 8 * px_step
+    # Algorithmic bytes (the survey's per-unit count for config 2): forward
+    # 2 x 4 B read, backward 2 x 4 B read + 4 B write = 20 B per pixel.  The
+    # fused kernel needs only 12 B (one read of a and b, one write of d/db).
+    fwd_bytes, bwd_bytes = 20 * px_step, 8 * px_step
     dom_ms, dom_bytes, dom_name = (fwd_ms, fwd_bytes, "ssim_loss_grad") if fwd_ms >= bwd_ms else \
         (bwd_ms, bwd_bytes, "grad_scale")
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
@@ -481,6 +607,7 @@ def run_ours(args):
             e1.record()
 
     e2e_value = None
+    h2d = {}
     if e2e_steps:
         e2e_run(2)
         torch.cuda.synchronize()
@@ -493,6 +620,53 @@ def run_ours(args):
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
         e2e_value = px_step * e2e_steps * world / (float(e_ms) / 1e3) / 1e9
+        # what the uploads achieved, and the raw pinned host->device rate of
+        # the same 398 MB with every rank copying at once (the e2e ceiling)
+        mine = 2 * 4 * px_step * e2e_steps / (e0.elapsed_time(e1) / 1e3) / 1e9
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        r0, r1 = ev(), ev()
+        with torch.cuda.stream(cstream):
+            r0.record(cstream)
+            for _ in range(3):
+                slots[0][0].copy_(a_h, non_blocking=True)
+                slots[0][1].copy_(b_h, non_blocking=True)
+            r1.record(cstream)
+        torch.cuda.synchronize()
+        raw = 3 * 2 * 4 * px_step / (r0.elapsed_time(r1) / 1e3) / 1e9
+        v = torch.tensor([mine, raw], dtype=torch.float64, device=dev)
+        if world > 1:
+            allv = torch.empty(world * 2, dtype=torch.float64, device=dev)
+            dist.all_gather_into_tensor(allv, v)
+            v = allv
+        v = v.view(-1, 2).cpu().tolist()
+        h2d = {"e2e_h2d_GBps_per_rank": [r[0] for r in v],
+               "raw_pinned_h2d_GBps_per_rank": [r[1] for r in v],
+               "numa_cpus": numa_cpus}
+
+    # config 4 at this rank count (every rank), and config-1 PSNR on every rank
+    cfg4 = None if args.no_extra else cfg4_sweep(args, world, rank, dev, hbm)
+    psnr_ranks = None
+    if not args.no_extra:
+        ua1, ub1 = u8_pair(PIX_SHAPE, 5.0, 0)
+        xu1, yu1 = torch.from_numpy(ua1).to(dev), torch.from_numpy(ub1).to(dev)
+        fl1 = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+        for _ in range(3):
+            fa.psnr(xu1, yu1)
+        if world > 1:
+            dist.barrier()
+        pm1 = timed_stream(lambda: fa.psnr(xu1, yu1), ev, fl1, reps=max(10, args.steps))
+        gbs = torch.tensor([2 * xu1.numel() / (pm1 / 1e3) / 1e9], dtype=torch.float64, device=dev)
+        if world > 1:
+            allg = torch.empty(world, dtype=torch.float64, device=dev)
+            dist.all_gather_into_tensor(allg, gbs)
+            gbs = allg
+        psnr_ranks = {"workload": "cfg1 PSNR uint8 8x3x1080x1920 on every rank at once, "
+                                  "L2 flushed by a 256 MB read",
+                      "GB/s_per_rank": gbs.cpu().tolist(),
+                      "hbm_frac_per_rank": [g / hbm for g in gbs.cpu().tolist()]}
+        del xu1, yu1, fl1
 
     # extra legs (rank-local, reported by rank 0): uint8 PSNR and SSIM forward
     extra = {}
@@ -544,13 +718,16 @@ def run_ours(args):
             fa.ssim(x4, y4, reduction="none"), fa.gmsd(x4, y4, reduction="none")
         s4 = timed_stream(lambda: fa.ssim(x4, y4, reduction="none"), ev, flush, reps=3)
         g4m = timed_stream(lambda: fa.gmsd(x4, y4, reduction="none"), ev, flush, reps=3)
+        f4m = timed_stream(lambda: fa.metrics(x4, y4, ("ssim", "gmsd"), reduction="none",
+                                              fuse_gmsd=True), ev, flush, reps=3)
         px4 = x4.numel()
         extra["cfg4_shard_ssim_gmsd_u8"] = {
             "workload": "config-4 shard: SSIM + GMSD reduction='none', uint8 8x3x2160x3840",
             "ssim_ms": s4, "gmsd_ms": g4m, "ssim_gpix_s": px4 / (s4 / 1e3) / 1e9,
             "gmsd_gpix_s": px4 / (g4m / 1e3) / 1e9,
             "gmsd_GB/s": 2 * px4 / (g4m / 1e3) / 1e9,
-            "both_gpix_s": px4 / ((s4 + g4m) / 1e3) / 1e9}
+            "both_gpix_s": px4 / ((s4 + g4m) / 1e3) / 1e9,
+            "fused_ssim_gmsd_ms": f4m, "fused_gpix_s": px4 / (f4m / 1e3) / 1e9}
         del x4, y4
         # MSE as a training loss on the config-2 frames: one fused read vs the
         # reduction followed by the separate backward kernel
@@ -613,6 +790,7 @@ def run_ours(args):
                      "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": traffic, "peak_source": hbm_kind,
                      "kernel_ms": dom_ms, "algorithmic_bytes": dom_bytes,
+                     "fused_minimum_bytes": 12 * px_step if dom_name == "ssim_loss_grad" else None,
                      "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                      "fp32_peak_tflops_at_clock": fp32_peak_tflops(sm_mhz),
                      # the kernel's binding roof is the FP32 pipes, not HBM:
@@ -628,7 +806,9 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "Gpixel/s", "overlap": "double-buffered uploads",
                 "h2d_bytes_per_step": 2 * 4 * px_step, "d2h_bytes_per_step": 8,
-                "steps": e2e_steps},
+                "steps": e2e_steps, **h2d},
+        "cfg4": cfg4,
+        "psnr_u8_all_ranks": psnr_ranks,
         "gpu_launches": 2 * args.steps,
         "clocks": clocks,
         "extra": extra,

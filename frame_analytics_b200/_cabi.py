@@ -120,6 +120,9 @@ PROTOTYPES = {
     "fa_b200_pool2": [_pview, _vp, _vp, _i, _vp],
     "fa_b200_pool2_backward": [_vp, _i, _i, _i, _i, _vp, _i, _vp],
     "fa_b200_wait_selftest": [ctypes.c_ulonglong, _i, _vp],
+    "fa_b200_ssim_gmsd_fusable": [_pview, _pview, _i, _i, _vp],
+    "fa_b200_ssim_gmsd": [_pview, _pview, _vp, _i, _d, _d, _d, _d, _d, _d, _vp, _sz,
+                          _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
 }
 _RESTYPE = {"fa_cuda_error_string": ctypes.c_char_p}
 

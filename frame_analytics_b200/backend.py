@@ -323,6 +323,53 @@ def ssim_mse(x: torch.Tensor, y: torch.Tensor, win: Taps, *, shift: float, C1: f
     return res
 
 
+def ssim_gmsd_fusable(x: torch.Tensor, y: torch.Tensor, k: int) -> bool:
+    """Whether ssim_gmsd serves this pair (see fa_b200_ssim_gmsd_fusable)."""
+    L = lib()
+    if kernel_dtype(x).dtype not in (torch.uint8, torch.float32):
+        return False
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    ok = ctypes.c_int(0)
+    _cabi.check(L.fa_b200_ssim_gmsd_fusable(ctypes.byref(vx), ctypes.byref(vy), int(k),
+                                            _dev(x), ctypes.byref(ok)))
+    return bool(ok.value)
+
+
+def ssim_gmsd(x: torch.Tensor, y: torch.Tensor, win: Taps, *, shift: float, C1: float,
+              C2: float, T: float, eps: float, psnr_bias: float, per_image: bool,
+              want_mse: bool) -> dict:
+    """SSIM and GMSD / GMS (2x2 pool) of one pair from ONE read (one launch),
+    plus MSE / PSNR when ``want_mse``.  SSIM / MSE / PSNR are (N,) when
+    ``per_image`` else 0-d; GMS and GMSD are always per image (N,)."""
+    L = lib()
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    k = win.k
+    dev = _dev(x)
+    nb = _cached_ws("ssim", L.fa_b200_ssim_workspace_bytes, vx.n, vx.c, vx.h, vx.w, k, dev)
+    ws = workspace(x, nb)
+    shape = (vx.n,) if per_image else ()
+    res = {"ssim": _f64(x, *shape), "gms": _f64(x, vx.n), "gmsd": _f64(x, vx.n)}
+    if want_mse:
+        res["mse"], res["psnr"] = _f64(x, *shape), _f64(x, *shape)
+        res["ssd"] = (torch.empty(vx.n, dtype=torch.int64, device=x.device)
+                      if x.dtype == torch.uint8 else None)
+    pi = (lambda t: t) if per_image else (lambda t: None)
+    tot = (lambda t: None) if per_image else (lambda t: t)
+    m, p_ = res.get("mse"), res.get("psnr")
+    _call(x, L.fa_b200_ssim_gmsd, ctypes.byref(vx), ctypes.byref(vy), win.arr, k,
+          float(shift), float(C1), float(C2), float(T), float(eps), float(psnr_bias),
+          ws.data_ptr(), ws.numel(), None, _ptr(pi(res["ssim"])), _ptr(tot(res["ssim"])),
+          _ptr(res["gms"]), _ptr(res["gmsd"]),
+          _ptr(pi(m) if m is not None else None), _ptr(tot(m) if m is not None else None),
+          _ptr(pi(p_) if p_ is not None else None), _ptr(tot(p_) if p_ is not None else None),
+          _ptr(res.get("ssd")), dev, _stream(x))
+    return res
+
+
 def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                   shift: float, C1: float, C2: float,
                   dmap: Optional[torch.Tensor] = None,

@@ -21,7 +21,9 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
                   int K, double shift, double C1, double C2, float* map_out, void* ws,
                   size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
                   double* out_per_image, double* out_total, int device, cudaStream_t st,
-                  const SqOut* sq = nullptr, const float* wdev = nullptr);
+                  const SqOut* sq = nullptr, const float* wdev = nullptr,
+                  const GmOut* gm = nullptr);
+bool ssim_gmsd_fusable(const View& x, const View& y, int dtype, int K, int device);
 size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device);
 int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* win,
                   int K, double shift, double C1, double C2, const float* dmap,
@@ -401,6 +403,41 @@ FA_B200_API int fa_b200_ssim_mse(const fa_view* x, const fa_view* y, const float
   return ssim_fwd_impl(to_view(*x), to_view(*y), x->dtype, nullptr, win, K, shift, C1, C2,
                        nullptr, workspace, workspace_bytes, out_plane_s, nullptr, out_per_image,
                        out_total, device, static_cast<cudaStream_t>(stream), &sq);
+}
+
+FA_B200_API int fa_b200_ssim_gmsd_fusable(const fa_view* x, const fa_view* y, int K,
+                                          int device, int* out_ok) {
+  if (!out_ok) return FA_E_ARG;
+  *out_ok = 0;
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  *out_ok = ssim_gmsd_fusable(to_view(*x), to_view(*y), x->dtype, K, device) ? 1 : 0;
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_ssim_gmsd(const fa_view* x, const fa_view* y, const float* win, int K,
+                                  double shift, double C1, double C2, double gmsd_T,
+                                  double gmsd_eps, double psnr_bias, void* workspace,
+                                  size_t workspace_bytes, double* out_plane_s,
+                                  double* out_per_image, double* out_total,
+                                  double* out_gms_per_image, double* out_gmsd_per_image,
+                                  double* out_mse_per_image, double* out_mse_total,
+                                  double* out_psnr_per_image, double* out_psnr_total,
+                                  uint64_t* out_ssd_per_image, int device, void* stream) {
+  FAB_PENDING();
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  const SqOut sq{psnr_bias, out_mse_per_image, out_mse_total, out_psnr_per_image,
+                 out_psnr_total, reinterpret_cast<unsigned long long*>(out_ssd_per_image)};
+  const bool want_sq = out_mse_per_image || out_mse_total || out_psnr_per_image ||
+                       out_psnr_total || out_ssd_per_image;
+  const GmOut gm{gmsd_T, gmsd_eps, out_gms_per_image, out_gmsd_per_image};
+  return ssim_fwd_impl(to_view(*x), to_view(*y), x->dtype, nullptr, win, K, shift, C1, C2,
+                       nullptr, workspace, workspace_bytes, out_plane_s, nullptr, out_per_image,
+                       out_total, device, static_cast<cudaStream_t>(stream),
+                       want_sq ? &sq : nullptr, nullptr, &gm);
 }
 
 FA_B200_API int fa_b200_ssim_loss_grad_workspace_bytes(int n, int c, int h, int w, int K,

@@ -171,6 +171,13 @@ struct SqOut {
   unsigned long long* ssd_per_image;  // uint8 input only
 };
 
+// Host-side request for GMSD from the SSIM forward's staged rows.
+struct GmOut {
+  double T, eps;             // GMSD threshold and epsilon in the metric's units
+  double* gms_per_image;     // [N] mean of q over the image's planes
+  double* gmsd_per_image;    // [N] population std of q
+};
+
 }  // namespace fab
 
 #define FAB_TRY(EXPR)                                   \

@@ -458,8 +458,9 @@ static GmPlan gm_plan(int Hout, int Wout, int planes, int device) {
   GmPlan g;
   g.strips = (Wout + GM_OW - 1) / GM_OW;
   const int sms = sm_count(device);
-  // about two waves of 4 resident blocks per SM, each streaming many rows
-  long long want = (8LL * sms + (long long)g.strips * planes - 1) / ((long long)g.strips * planes);
+  // two full waves of the 3 blocks per SM gmsd_tma_kernel keeps resident,
+  // each block streaming many rows
+  long long want = (6LL * sms + (long long)g.strips * planes - 1) / ((long long)g.strips * planes);
   if (want < 1) want = 1;
   long long maxc = (Hout + GM_R - 1) / GM_R;
   if (want > maxc) want = maxc;

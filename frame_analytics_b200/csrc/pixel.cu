@@ -697,25 +697,49 @@ int pixel_backward_impl(const float* x, const float* y, int N, int C, int H, int
 //     (cudaGetSymbolAddress, with that device current) and caches it; make
 //     that first call before any stream capture.
 // ---------------------------------------------------------------------------
+#include <cuda.h>
+
 #include <mutex>
 
 namespace fab {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[FA_B200_NOALLOC_SCRATCH_BYTES];
 
-// Device address of g_noalloc_scratch on `device`, looked up once per device.
+// Device address of g_noalloc_scratch in the current context of `device`.
 // In host code the symbol itself is only a host-side stand-in, never a
-// device pointer, so the address must come from the runtime.
+// device pointer, so the address must come from the runtime.  It is looked
+// up once per (device, context): a context created anew (after
+// cudaDeviceReset, or another context made current) gets its own lookup
+// instead of a stale address.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
 static int noalloc_scratch(int device, void** out) {
   constexpr int MAXD = 64;
   static std::mutex mu;
   static void* addr[MAXD] = {nullptr};
+  static CUcontext ctx[MAXD] = {nullptr};
   if (device < 0 || device >= MAXD) return FA_E_ARG;
+  const CUcontext cur = current_context();  // the device is current here
   std::lock_guard<std::mutex> g(mu);
-  if (!addr[device]) {
+  if (!addr[device] || ctx[device] != cur) {
     void* p = nullptr;
-    FAB_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));  // the device is current here
+    FAB_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     addr[device] = p;
+    ctx[device] = cur;
   }
   *out = addr[device];
   return FA_OK;

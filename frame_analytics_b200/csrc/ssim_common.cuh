@@ -73,6 +73,12 @@ struct SsimArgs {
   float grad_norm;
   unsigned int* err;  // host-mapped error word of the bounded waits
   const float* wdev;  // device taps (reference-compatible calls), else null
+  // fused GMSD (2x2 pool, Prewitt, pooled over the image's planes)
+  float gT, geps;     // threshold and epsilon in the metric's units
+  int gHo, gWo;       // GMS map size, (H/2 - 2) x (W/2 - 2)
+  double* part_g;     // [P][bpp] (sum d, sum d^2), d = q - 1
+  double* out_gms_per_image;
+  double* out_gmsd_per_image;
   float* dx;
   float* dy;
 };

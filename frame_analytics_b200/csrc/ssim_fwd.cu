@@ -18,8 +18,8 @@ static SsimPlan fwd_plan(int Hout, int Wout, int K, int planes, int device) {
 
 size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device) {
   const SsimPlan pl = fwd_plan(Hout, Wout, K, planes, device);
-  // partial sums: SSIM, cs and squared differences (8 bytes each per block)
-  return FAB_COUNTER_BYTES + 3 * sizeof(double) * (size_t)planes * pl.strips * pl.chunks;
+  // partial sums: SSIM, cs, squared differences and the GMSD pair (8 bytes each per block)
+  return FAB_COUNTER_BYTES + 5 * sizeof(double) * (size_t)planes * pl.strips * pl.chunks;
 }
 
 template <typename T, bool CS, int STAGE>
@@ -148,8 +148,9 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
                   int K, double shift, double C1, double C2, float* map_out, void* ws,
                   size_t ws_bytes, double* out_plane_s, double* out_plane_cs,
                   double* out_per_image, double* out_total, int device, cudaStream_t st,
-                  const SqOut* sq, const float* wdev) {
+                  const SqOut* sq, const float* wdev, const GmOut* gm) {
   if (!x.data || !y.data || (!taps && !wdev) || !ws) return FA_E_ARG;
+  if (gm && (wdev || luma || out_plane_cs || map_out)) return FA_E_ARG;
   if (wdev && (sq || luma)) return FA_E_ARG;
   if (sq && (luma || out_plane_cs)) return FA_E_ARG;
   if (x.n <= 0 || x.c <= 0 || x.h <= 0 || x.w <= 0) return FA_E_SHAPE;
@@ -183,7 +184,8 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
   const SsimPlan pl = fwd_plan(Hout, Wout, K, p.P, device);
   p.strips = pl.strips; p.chunks = pl.chunks; p.RH = pl.RH;
   const size_t nb = (size_t)p.P * pl.strips * pl.chunks;
-  if (ws_bytes < FAB_COUNTER_BYTES + (sq ? 3 : 2) * sizeof(double) * nb) return FA_E_ARG;
+  if (ws_bytes < FAB_COUNTER_BYTES + (gm ? 5 : (sq ? 3 : 2)) * sizeof(double) * nb)
+    return FA_E_ARG;
   p.counter = static_cast<unsigned int*>(ws);
   p.part_s = reinterpret_cast<double*>(static_cast<char*>(ws) + FAB_COUNTER_BYTES);
   p.part_cs = out_plane_cs ? p.part_s + nb : nullptr;
@@ -195,6 +197,17 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
     p.out_psnr_per_image = sq->psnr_per_image;
     p.out_psnr_total = sq->psnr_total;
     p.out_ssd_per_image = (dtype == FA_U8 || dtype == FA_U16) ? sq->ssd_per_image : nullptr;
+  }
+  if (gm) {
+    p.part_g = p.part_s + 3 * nb;
+    p.gT = (float)gm->T;
+    p.geps = (float)gm->eps;
+    p.gHo = x.h / 2 - 2;
+    p.gWo = x.w / 2 - 2;
+    p.out_gms_per_image = gm->gms_per_image;
+    p.out_gmsd_per_image = gm->gmsd_per_image;
+    if (p.gHo <= 0 || p.gWo <= 0 || K != 11 || p.gWo > pl.strips * (Geo<11>::NT / 2))
+      return FA_E_SHAPE;
   }
   p.map_out = map_out;
   p.out_plane_s = out_plane_s; p.out_plane_cs = out_plane_cs;
@@ -214,6 +227,16 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
       p.tma_d = dx;
     }
   }
+  if (gm) {
+    if (stage != STAGE_TMA) return FA_E_SHAPE;
+    if (dtype == FA_U8)
+      return sq ? launch_fwd<unsigned char, 11, false, STAGE_TMA, true, false, true>(p, device, st)
+                : launch_fwd<unsigned char, 11, false, STAGE_TMA, false, false, true>(p, device, st);
+    if (dtype == FA_F32)
+      return sq ? launch_fwd<float, 11, false, STAGE_TMA, true, false, true>(p, device, st)
+                : launch_fwd<float, 11, false, STAGE_TMA, false, false, true>(p, device, st);
+    return FA_E_DTYPE;
+  }
   switch (dtype) {
     case FA_U8: return fwd_dispatch<unsigned char>(p, stage, cs, K, device, st);
     case FA_F16: return fwd_dispatch<f16_t>(p, stage, cs, K, device, st);
@@ -222,6 +245,21 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
     case FA_U16: return fwd_dispatch<unsigned short>(p, stage, cs, K, device, st);
     default: return fwd_dispatch<double>(p, stage, cs, K, device, st);
   }
+}
+
+// Whether ssim_fwd_impl can add GMSD (2x2 pool) to this pair's SSIM pass: an
+// 11-tap symmetric window, uint8 or float32 rows a TMA map can describe, and
+// a GMS map no wider than the strips' owned columns.
+bool ssim_gmsd_fusable(const View& x, const View& y, int dtype, int K, int device) {
+  if (K != 11 || (dtype != FA_U8 && dtype != FA_F32)) return false;
+  if (x.h < 11 || x.w < 11 || x.h / 2 - 2 <= 0 || x.w / 2 - 2 <= 0) return false;
+  if (x.sn != y.sn || x.sc != y.sc || x.sh != y.sh) return false;
+  const SsimPlan pl = fwd_plan(x.h - 10, x.w - 10, 11, x.n * x.c, device);
+  if (x.w / 2 - 2 > pl.strips * (Geo<11>::NT / 2)) return false;
+  CUtensorMap mx, my;
+  const int bw = box_width_k(11, dtype);
+  int dx = 0, dy = 0;
+  return make_row_map(&mx, x, dtype, bw, &dx) && make_row_map(&my, y, dtype, bw, &dy) && dx == dy;
 }
 
 }  // namespace fab

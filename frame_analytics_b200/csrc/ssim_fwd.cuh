@@ -190,7 +190,106 @@ static __device__ __noinline__ void sq_finalize(const SsimArgs& p, int bpp) {
   }
 }
 
-template <typename T, int KW, bool CS, int STAGE, bool SQ>
+// Last block: per-image GMS mean and GMSD (population std of q over the map
+// positions of all the image's planes) from the per-block (sum d, sum d^2).
+static __device__ __noinline__ void gm_fused_finalize(const SsimArgs& p, int bpp) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const double npix = (double)p.gHo * p.gWo * p.Cm;
+  for (int n = wid; n < p.N; n += nw) {
+    double s = 0.0, s2 = 0.0;
+    for (int c = 0; c < p.Cm; ++c) {
+      const double* row = p.part_g + 2 * (long long)(n * p.Cm + c) * bpp;
+      for (int i = lane; i < bpp; i += 32) {
+        s += row[2 * i];
+        s2 += row[2 * i + 1];
+      }
+    }
+    s = warp_sum(s);
+    s2 = warp_sum(s2);
+    if (lane == 0) {
+      const double md = s / npix;
+      const double var = s2 / npix - md * md;
+      if (p.out_gms_per_image) p.out_gms_per_image[n] = 1.0 + md;
+      if (p.out_gmsd_per_image) p.out_gmsd_per_image[n] = sqrt(var > 0.0 ? var : 0.0);
+    }
+  }
+}
+
+// Fused GMSD state of one thread.  Thread pair (2c, 2c+1) owns GMS map column
+// j0 + c of its block, the even thread for x, the odd one for y, so all the
+// block's warps share the work evenly.  Staged rows are visited in order; an
+// even row's horizontal pair sums wait in e, an odd row completes a pooled
+// row P, whose column difference D = P0 - P2 and 3-sum R = P0 + P1 + P2 enter
+// a 3-row window kept as running sums: gx = D0 + D1 + D2 = d12 + D with
+// d12 = D1 + D2 of the previous window, gy = R0 - R2.  Both are 3 x 4 times
+// the pooled Prewitt responses (hence the 1/144); the pair exchanges them
+// with one shuffle each and the even thread forms the map value.
+struct GmState {
+  float e0, e1, e2;
+  float d2, d12;  // newest D, and D1 + D2
+  float r1, r2;   // the two newest R
+  float fs, fs2;
+};
+
+// One staged row (global input row r, this thread's six inputs at s[0..5]).
+// Control flow is uniform across the block, so every lane reaches the
+// shuffles.
+__device__ __forceinline__ void gm_row(const SsimArgs& p, const float* s, int r, int rlo, int rhi,
+                                       bool col_ok, GmState& g) {
+  constexpr float K144 = 1.0f / 144.0f;
+  if (r < rlo || r > rhi) return;
+  const float h0 = s[0] + s[1], h1 = s[2] + s[3], h2 = s[4] + s[5];
+  if ((r & 1) == 0) {
+    g.e0 = h0; g.e1 = h1; g.e2 = h2;
+    return;
+  }
+  const float P0 = g.e0 + h0, P1 = g.e1 + h1, P2 = g.e2 + h2;
+  const float D = P0 - P2, R = P0 + P1 + P2;
+  const float gx = g.d12 + D, gy = g.r1 - R;
+  g.d12 = g.d2 + D;
+  g.d2 = D;
+  g.r1 = g.r2;
+  g.r2 = R;
+  if (r - rlo < 5) return;  // fewer than three pooled rows so far
+  const float ox = __shfl_xor_sync(0xffffffffu, gx, 1);
+  const float oy = __shfl_xor_sync(0xffffffffu, gy, 1);
+  if (col_ok && (threadIdx.x & 1) == 0) {
+    // the map value exactly as the GMSD kernel forms it (gmsd.cu)
+    const float G1 = fmaf(fmaf(gx, gx, gy * gy), K144, p.geps);
+    const float G2 = fmaf(fmaf(ox, ox, oy * oy), K144, p.geps);
+    const float dG = fmaf(gx - ox, gx + ox, (gy - oy) * (gy + oy)) * K144;
+    const float S = G1 + G2;
+    const float G12 = G1 * G2;
+    const float d = -__fdividef(dG * dG, (S + 2.f * G12 * rsqrtf(G12)) * (S + p.gT));
+    g.fs += d;
+    g.fs2 = fmaf(d, d, g.fs2);
+  }
+}
+
+// The rows of one staged batch.  When every row lies inside the block's
+// GMSD range with three pooled rows already in the window (the common case),
+// each row is passed as the stand-in index 6 + its parity: in range, past the
+// first five rows, and compile-time once the loop unrolls, so the batch
+// becomes straight-line code.
+template <int KW, int FP>
+__device__ __forceinline__ void gm_batch(const SsimArgs& p, const float* s, int row0, int rlo,
+                                         int rhi, bool col_ok, GmState& g) {
+  if (row0 - rlo >= 5 && row0 + KW - 1 <= rhi) {
+    if (row0 & 1) {
+#pragma unroll
+      for (int k = 0; k < KW; ++k) gm_row(p, s + k * FP, 6 + ((k + 1) & 1), 0, 1 << 30, col_ok, g);
+    } else {
+#pragma unroll
+      for (int k = 0; k < KW; ++k) gm_row(p, s + k * FP, 6 + (k & 1), 0, 1 << 30, col_ok, g);
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int k = 0; k < KW; ++k) gm_row(p, s + k * FP, row0 + k, rlo, rhi, col_ok, g);
+}
+
+template <typename T, int KW, bool CS, int STAGE, bool SQ, bool GM = false>
 __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
   using G = Geo<KW>;
   using R = Raw<T, KW>;
@@ -240,6 +339,19 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
   SqAcc<T> acc_sq = 0;
   const int sq_chi = (blockIdx.x == gridDim.x - 1) ? p.W : c0 + G::NT;
   const int sq_rhi = (blockIdx.y == gridDim.y - 1) ? p.H : r0 + rows;
+  // GM: this block's GMS map rows are those i with 2i in [r0, r0 + rows) (the
+  // last chunk: all from there on), which need input rows [2 i_lo, 2 i_hi + 5]
+  GmState gst{};
+  int g_rlo = 0, g_rhi = -1;
+  bool g_col = false;
+  if constexpr (GM) {
+    const int i_lo = (r0 + 1) >> 1;
+    const int i_end = (blockIdx.y == gridDim.y - 1) ? p.gHo : (r0 + rows + 1) >> 1;
+    g_rlo = 2 * i_lo;
+    g_rhi = i_end > i_lo ? 2 * (i_end - 1) + 5 : -1;
+    g_col = (c0 >> 1) + (t >> 1) < p.gWo;
+  }
+  const float* gm_in = ((t & 1) ? sY : sX) + sofs + 2 * (t >> 1);
 
   for (int m = 0; m < iters; ++m) {
     if constexpr (!TMA) {
@@ -265,6 +377,9 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
       float4* out = sH + warp * G::NT + lane * KW;
       hblur4<KW, TMA>(p, rx, ry, out);  // TMA staging implies symmetric taps
     }
+    // GM: the staged rows through the GMSD state; the next batch's copy and
+    // convert rewrite sX / sY only after the barrier below
+    if constexpr (GM) gm_batch<KW, R::FP>(p, gm_in, r0 + m * KW, g_rlo, g_rhi, g_col, gst);
     __syncthreads();
     const bool more = (m + 1 < iters);
     if constexpr (TMA) {
@@ -311,7 +426,22 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
     acc_sq = block_sum(acc_sq, s_red_q);
     if (t == 0) static_cast<SqAcc<T>*>(p.part_sq)[pidx] = acc_sq;
   }
+  if constexpr (GM) {
+    // a thread's column sums stay in float (a few hundred small terms, kept
+    // there to stay within 80 registers); the block sums are double
+    double acc_g = block_sum((double)gst.fs, s_red);
+    double acc_g2 = block_sum((double)gst.fs2, s_red);
+    // part_g is only 8-byte aligned (it follows 3 x nb doubles): two stores
+    if (t == 0) {
+      p.part_g[2 * pidx] = acc_g;
+      p.part_g[2 * pidx + 1] = acc_g2;
+    }
+  }
   if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag)) {
+    if constexpr (GM) {
+      gm_fused_finalize(p, bpp);
+      __syncthreads();
+    }
     ssim_fwd_finalize(p, bpp);
     if constexpr (SQ) {
       __syncthreads();
@@ -333,15 +463,28 @@ __global__ void __launch_bounds__(32 * KW, 2) ssim_fwd_kernel(const __grid_const
   }
 }
 
+// SSIM with GMSD of the same pair from the same staged rows
+// (ssim_gmsd_fusable).  Two blocks per SM as the plain kernel; the GMSD state
+// needs 88 registers a thread instead of 80 (88 x 352 x 2 fits an SM).
+template <typename T, int KW, bool SQ>
+__global__ void __launch_bounds__(32 * KW, 2) ssim_gmsd_kernel(const __grid_constant__ SsimArgs p) {
+  ssim_fwd_body<T, KW, false, STAGE_TMA, SQ, true>(p);
+}
+
 template <typename T, int KW, int STAGE>
 static constexpr size_t fwd_smem() {
   return sizeof(float4) * KW * Geo<KW>::NT + Raw<T, KW>::kFloatBytes +
          (STAGE == STAGE_TMA ? Raw<T, KW>::kRawBytes : 0);
 }
 
-template <typename T, int KW, bool CS, int STAGE, bool SQ = false, bool DW = false>
+template <typename T, int KW, bool CS, int STAGE, bool SQ = false, bool DW = false,
+          bool GM = false>
 static int launch_fwd(const SsimArgs& p, int device, cudaStream_t st) {
-  auto kern = ssim_fwd_kernel<T, KW, CS, STAGE, SQ, DW>;
+  static_assert(!GM || (STAGE == STAGE_TMA && !CS && !DW), "GMSD rides on the TMA forward");
+  auto kern = [] {
+    if constexpr (GM) return ssim_gmsd_kernel<T, KW, SQ>;
+    else return ssim_fwd_kernel<T, KW, CS, STAGE, SQ, DW>;
+  }();
   const size_t sm = fwd_smem<T, KW, STAGE>();
   static bool done[64] = {false};
   FAB_TRY(ensure_smem(kern, sm, device, done));

@@ -91,18 +91,54 @@ def sharded_mse(x_local: torch.Tensor, y_local: torch.Tensor, n: int,
 class ShardedMetrics:
     """Score a batch sharded over ranks and return whole-batch per-image results.
 
-    ``metrics`` maps a name to a callable ``f(x, y) -> (n_local,)`` (e.g.
-    ``lambda x, y: fa.ssim(x, y, reduction='none')``).  Each rank passes its
-    own shard; the result holds every image's value on every rank.
+    ``metrics`` is either a mapping name -> callable ``f(x, y) -> (n_local,)``
+    (e.g. ``lambda x, y: fa.ssim(x, y, reduction='none')``), one collective
+    per name, or a sequence of metric names for
+    :func:`frame_analytics_b200.metrics`: then the names are scored together
+    (SSIM with GMSD / MSE / PSNR from one read of the shard, one launch) and
+    their per-image values travel in ONE all-gather.  Each rank passes its own
+    shard; the result holds every image's value on every rank.
     """
 
-    def __init__(self, metrics: Dict[str, Callable], group=None):
-        self.metrics = dict(metrics)
+    def __init__(self, metrics, group=None, **kw):
         self.group = group
+        self.kw = kw
+        if isinstance(metrics, dict):
+            self.metrics, self.names = dict(metrics), None
+        else:
+            self.metrics, self.names = None, tuple(metrics)
 
     def __call__(self, x_local: torch.Tensor, y_local: torch.Tensor, n: int) -> Dict[str, torch.Tensor]:
-        return {name: gather_per_image(fn(x_local, y_local).reshape(-1), n, self.group)
-                for name, fn in self.metrics.items()}
+        if self.metrics is not None:
+            return {name: gather_per_image(fn(x_local, y_local).reshape(-1), n, self.group)
+                    for name, fn in self.metrics.items()}
+        from .functional import metrics as _metrics
+        res = _metrics(x_local, y_local, self.names, reduction="none", **self.kw)
+        return gather_stacked([res[k].reshape(-1).to(torch.float64) for k in self.names],
+                              self.names, n, self.group)
+
+
+def gather_stacked(values: Sequence[torch.Tensor], names: Sequence[str], n: int,
+                   group=None) -> Dict[str, torch.Tensor]:
+    """All-gather several per-image float64 vectors of this rank's shard with
+    one collective: they are stacked as (k, n_local) and gathered image-major,
+    so the (n_local, k) rows travel together."""
+    stacked = torch.stack(list(values), dim=1).contiguous()  # (n_local, k)
+    k = stacked.shape[1]
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    lo, hi = shard_bounds(n, rank, world)
+    if stacked.shape[0] != hi - lo:
+        raise ValueError(f"rank {rank} holds images [{lo}, {hi}) but scored {stacked.shape[0]}")
+    width = max(shard_bounds(n, r, world)[1] - shard_bounds(n, r, world)[0] for r in range(world))
+    buf = torch.zeros((width, k), dtype=stacked.dtype, device=stacked.device)
+    buf[: hi - lo] = stacked
+    out = torch.empty((world * width, k), dtype=stacked.dtype, device=stacked.device)
+    dist.all_gather_into_tensor(out, buf, group=group)
+    rows = [out[r * width: r * width + (shard_bounds(n, r, world)[1] - shard_bounds(n, r, world)[0])]
+            for r in range(world)]
+    full = torch.cat(rows)
+    return {name: full[:, i].contiguous() for i, name in enumerate(names)}
 
 
 def default_metrics(names: Sequence[str] = ("ssim", "gmsd"), **kw) -> Dict[str, Callable]:

@@ -222,6 +222,7 @@ class StreamingMetrics:
         self._L = (float(data_range) if data_range is not None
                    else _infer_data_range(self._slots[0].ref))
         self._turn = 0
+        self.capture_error: Optional[str] = None  # why graph capture was given up, if it was
         if use_cuda_graph and not all(self._record(s) for s in self._slots):
             for s in self._slots:  # all or nothing: graph replay is an optimisation
                 s.graph = s.out = None
@@ -248,8 +249,9 @@ class StreamingMetrics:
                 out = self._score(slot)
             slot.graph, slot.out = g, out
             return True
-        except Exception:
+        except Exception as exc:
             slot.graph = slot.out = None
+            self.capture_error = f"{type(exc).__name__}: {exc}"
             return False
 
     # -- staging ---------------------------------------------------------- #

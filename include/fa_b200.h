@@ -257,6 +257,35 @@ FA_B200_API int fa_b200_ssim_mse(const fa_view* x, const fa_view* y,
                                  uint64_t* out_ssd_per_image, int device,
                                  void* stream);
 
+/* No single counterpart in the reference: the SSIM and GMSD of config 4
+ * (and optionally MSE / PSNR) from ONE read of the frame pair.  The
+ * reference's StreamingMetrics scores them with separate kernels
+ * (modules.py:373-402; SSIM fa_cuda.cu:1167-1223, GMSD fa_cuda.cu:1426-1466),
+ * reading every frame twice.  Here the SSIM kernel's staged rows also feed a
+ * 2x2-pooled Prewitt pass.  GMSD semantics are fa_b200_gmsd's with
+ * downsample=1: q over the (H/2-2) x (W/2-2) map of every plane, pooled over
+ * the image's planes; out_gms_per_image = mean q, out_gmsd_per_image = its
+ * population std.  SSIM and MSE / PSNR outputs as fa_b200_ssim_mse; the
+ * MSE / PSNR pass runs only when one of its outputs is non-NULL.  Every
+ * output is nullable.  Serves the pairs fa_b200_ssim_gmsd_fusable accepts
+ * (11-tap symmetric window, uint8 or float32, rows a TMA map can describe);
+ * others return FA_E_SHAPE.  Workspace: fa_b200_ssim_workspace_bytes. */
+FA_B200_API int fa_b200_ssim_gmsd_fusable(const fa_view* x, const fa_view* y, int K,
+                                          int device, int* out_ok);
+FA_B200_API int fa_b200_ssim_gmsd(const fa_view* x, const fa_view* y,
+                                  const float* taps_host, int K, double shift,
+                                  double C1, double C2, double gmsd_T,
+                                  double gmsd_eps, double psnr_bias,
+                                  void* workspace, size_t workspace_bytes,
+                                  double* out_plane_s, double* out_per_image,
+                                  double* out_total, double* out_gms_per_image,
+                                  double* out_gmsd_per_image,
+                                  double* out_mse_per_image, double* out_mse_total,
+                                  double* out_psnr_per_image,
+                                  double* out_psnr_total,
+                                  uint64_t* out_ssd_per_image, int device,
+                                  void* stream);
+
 /* SSIM loss value and gradient in one pass (training steps).  No single
  * counterpart in the reference: it runs its forward (fa_cuda_ssim,
  * fa_cuda.cu:1167-1283) and later its backward (fa_cuda_ssim_backward,
@@ -423,7 +452,8 @@ FA_B200_API int fa_b200_pixel_loss_grad(const float* x, const float* y, int N,
  * fa_b200_pixel_reduce minus the workspace.  Batches of more than
  * FA_B200_NOALLOC_MAX_IMAGES images return FA_E_SHAPE.  All calls on a
  * device share the array: calls that may overlap on the GPU race, so
- * serialise them.  The first call on a device looks up the array's address;
+ * serialise them.  The first call on a device (and the first in each new context of it, e.g.
+ * after cudaDeviceReset) looks up the array's address;
  * make it before any stream capture. */
 #define FA_B200_NOALLOC_SCRATCH_BYTES (64 * 1024)
 #define FA_B200_NOALLOC_MAX_IMAGES 4096

@@ -14,7 +14,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from frame_analytics_b200.distributed import (batch_mean, exact_mse_from_ssd, gather_per_image,
-                                              shard_bounds)
+                                              gather_stacked, shard_bounds)
 
 
 def _port():
@@ -46,6 +46,12 @@ def _worker(rank, world, port, n, mode, q):
         if mode == "die" and rank == 1:
             raise SystemExit(3)  # leaves before the gather, with nothing in flight
         full = gather_per_image(local, n)
+        if mode == "stacked":
+            res = gather_stacked([local, -local, local * local], ("a", "b", "c"), n)
+            q.put((rank, "ok", [res[k].tolist() for k in ("a", "b", "c")], None))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         if mode == "ssd":
             # integer sums near 2^53 / n: the exact path must not round them
             ssd = (torch.arange(lo, hi, dtype=torch.int64) * 1_000_003 + (1 << 40))
@@ -104,3 +110,12 @@ def test_exact_mse_gathers_integer_sums(world, n):
         assert status == "ok", out
         assert per == [v / 6220800 for v in ssd]
         assert total == float(sum(ssd)) / float(6220800 * n)
+
+
+@pytest.mark.parametrize("world,n", [(2, 5), (3, 7)])
+def test_stacked_gather_moves_several_metrics_in_one_collective(world, n):
+    out = _run(world, n, "stacked")
+    want = [i * 1.5 + 0.25 for i in range(n)]
+    for rank, status, (a, b, c), _ in out:
+        assert status == "ok", out
+        assert a == want and b == [-v for v in want] and c == [v * v for v in want]

@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 import torch
 
+import fa_oracle as O
 from conftest import baseline_pair
 
 import frame_analytics_b200 as fa
@@ -95,7 +96,7 @@ def test_streaming_metrics(use_graph):
     shape = (1, 3, 120, 160)
     sm = fa.StreamingMetrics(shape, metrics=("mse", "psnr", "ssim", "gmsd"),
                              use_cuda_graph=use_graph)
-    assert sm.graph_captured == use_graph
+    assert sm.graph_captured == use_graph, sm.capture_error
     for seed in range(3):
         a, b = baseline_pair(shape, 6.0, seed=seed)
         got = sm.update(a, b)  # host numpy frames through pinned staging
@@ -131,9 +132,9 @@ def test_streaming_ms_ssim_captures_with_side_streams():
 def test_streaming_instances_replay_concurrently_on_two_streams():
     """Each StreamingMetrics owns its scratch and streams: two instances whose
     graph replays overlap on the GPU both return the single-call values."""
-    shape = (2, 3, 128, 160)
+    shape = (2, 3, 192, 200)
     sms = [fa.StreamingMetrics(shape, metrics=("mse", "psnr", "ssim", "ms_ssim")) for _ in range(2)]
-    assert all(s.graph_captured for s in sms)
+    assert all(s.graph_captured for s in sms), [s.capture_error for s in sms]
     pairs = [baseline_pair(shape, 6.0, seed=10 + i) for i in range(6)]
     dev = [(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()) for a, b in pairs]
     torch.cuda.synchronize()
@@ -158,3 +159,45 @@ def test_streaming_overlapped_updates_keep_results_apart():
     for (a, b), got in zip(pairs, res):
         x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
         assert float(got["psnr"]) == float(fa.psnr(x, y))
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 64, 96), (1, 1, 37, 53), (3, 2, 131, 717),
+                                   (1, 1, 400, 1067), (1, 3, 2160, 3840)])
+@pytest.mark.parametrize("dt", [torch.uint8, torch.float32])
+def test_fused_ssim_gmsd_matches_separate_calls(shape, dt):
+    """SSIM + GMSD (+ MSE / PSNR) from one launch equal the separate calls
+    (GMSD within 5e-6, SSIM within 1e-7, MSE exact for uint8) and the oracle."""
+    from frame_analytics_b200 import backend
+    a, b = baseline_pair(shape, 9.0, seed=sum(shape))
+    x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    L = 255.0
+    if dt == torch.float32:
+        x, y, L = x.float() / 255.0, y.float() / 255.0, 1.0
+    # rows a TMA map describes (16-byte strides) fuse
+    assert backend.ssim_gmsd_fusable(x, y, 11) == (shape[-1] * x.element_size() % 16 == 0)
+    for names in (("ssim", "gmsd", "gms"), ("mse", "psnr", "ssim", "gmsd")):
+        for red in ("none", "mean"):
+            got = fa.metrics(x, y, names, reduction=red, data_range=L, fuse_gmsd=True)
+            for n in names:
+                kw = {} if n == "mse" else {"data_range": L}
+                want = getattr(fa, n)(x, y, reduction=red, **kw)
+                tol = 0 if (n == "mse" and dt == torch.uint8) else (1e-7 if n == "ssim" else 5e-6)
+                assert float((got[n] - want).abs().max()) <= tol, (n, red)
+    if shape[-1] <= 1067:
+        m, s = O.gmsd(a, b, eps=(1e-6 * 255.0) ** 2)
+        got = fa.metrics(x, y, ("ssim", "gmsd", "gms"), reduction="none", data_range=L,
+                         fuse_gmsd=True)
+        np.testing.assert_allclose(got["gmsd"].cpu().numpy(), s, atol=5e-6)
+        np.testing.assert_allclose(got["gms"].cpu().numpy(), m, atol=5e-6)
+
+
+def test_fused_ssim_gmsd_falls_back_where_it_cannot_fuse():
+    """A width whose GMS map overhangs the SSIM strips (W = 362), and a uint16
+    pair, are served by separate launches with the same results."""
+    from frame_analytics_b200 import backend
+    a, b = baseline_pair((1, 2, 70, 362), 9.0, seed=1)
+    x, y = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    assert not backend.ssim_gmsd_fusable(x, y, 11)
+    got = fa.metrics(x, y, ("ssim", "gmsd"), reduction="none", fuse_gmsd=True)
+    assert torch.equal(got["gmsd"], fa.gmsd(x, y, reduction="none"))
+    assert torch.equal(got["ssim"], fa.ssim(x, y, reduction="none"))
