@@ -340,10 +340,13 @@ def run_only(args):
             ts.append(timed_call(lambda: fn(xu, yu), ev))
         res[mode] = statistics.median(ts)
     nbytes = 2 * ua.size
-    # calibration: torch's own copy kernel moving the same number of bytes
-    src = torch.empty(nbytes // 2, dtype=torch.uint8, device="cuda")
-    dst = torch.empty_like(src)
-    res["torch_copy_same_bytes"] = timed_stream(lambda: dst.copy_(src), ev, flush)
+    # calibration at the same size: (a) the fixed cost of one timed launch
+    # (a one-thread kernel that returns at once, between the same events and
+    # flushes), (b) torch's own reduction reading the same number of bytes
+    # (one buffer of both frames, viewed as int64): one read-only launch
+    res["launch_floor"] = timed_stream(lambda: torch.cuda._sleep(0), ev, flush)
+    both = torch.cat([xu.view(-1), yu.view(-1)]).view(torch.int64)
+    res["torch_sum_same_bytes"] = timed_stream(lambda: both.sum(), ev, flush)
     print(json.dumps({"only": args.only, "ms": res,
                       "GB/s": {k: nbytes / (v / 1e3) / 1e9 for k, v in res.items()}}))
 

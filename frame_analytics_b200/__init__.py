@@ -29,6 +29,7 @@ from .functional import (  # noqa: F401
     set_fused_loss_grad,
     ssim,
 )
+from . import planes  # noqa: F401
 from .modules import (GMSD, L1, MSE, MSSSIM, PSNR, SSIM, Charbonnier, Huber,  # noqa: F401
                       StreamingMetrics)
 

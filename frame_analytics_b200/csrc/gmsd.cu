@@ -215,6 +215,66 @@ __device__ __forceinline__ void gm_rows_packed(const GmsdArgs& p, const float2* 
   }
 }
 
+// Prewitt window of the uint8 TMA kernel carried across iterations: per
+// output column, (x, y) pairs of the newest column difference D, of D1 + D2
+// (the two newest), and of the two newest 3-sums R.  gx = D0 + D1 + D2 and
+// gy = R0 - R2 then need one add each, and no pooled row is pooled or read
+// twice (the ring holds only new rows after the first iteration).
+struct GmWin {
+  float2 d2[GM_CPT], d12[GM_CPT], r1[GM_CPT], r2[GM_CPT];
+};
+
+// Ring rows 0..n-1 hold pooled rows g0 .. g0+n-1 of the block (g counted from
+// the block's first pooled row); a map row is emitted from pooled row g >= 2
+// (map row r0 + g - 2).
+template <bool MAP, bool DOWN>
+__device__ __forceinline__ void gm_rows_window(const GmsdArgs& p, const float2* ring, int pitch,
+                                               int n, int g0, int t, int dc0, int plane, int r0,
+                                               GmWin& w, float& fs, float& fs2) {
+  static_assert(GM_CPT == 2, "two output columns per thread");
+  constexpr float K = DOWN ? 1.0f / 144.0f : 1.0f / 9.0f;
+  const int c0t = t * GM_CPT;
+  const int ncol = min(min(GM_OW, p.Wout - dc0) - c0t, GM_CPT);
+  const float2 kk = make_float2(K, K), ee = make_float2(p.eps, p.eps);
+  const float2 m1 = make_float2(-1.f, -1.f);
+#pragma unroll
+  for (int q = 0; q < GM_R + 2; ++q) {
+    if (q < n) {
+      const float2* rowp = ring + q * pitch;
+      const float4 A = *reinterpret_cast<const float4*>(rowp + c0t);
+      const float4 B = *reinterpret_cast<const float4*>(rowp + c0t + 2);
+      const float2 P0 = make_float2(A.x, A.y), P1 = make_float2(A.z, A.w);
+      const float2 P2 = make_float2(B.x, B.y), P3 = make_float2(B.z, B.w);
+      const float2 s12 = __fadd2_rn(P1, P2);
+      const float2 D[GM_CPT] = {__ffma2_rn(P2, m1, P0), __ffma2_rn(P3, m1, P1)};
+      const float2 R[GM_CPT] = {__fadd2_rn(P0, s12), __fadd2_rn(s12, P3)};
+      const bool emit = g0 + q >= 2;
+#pragma unroll
+      for (int i = 0; i < GM_CPT; ++i) {
+        const float2 gx = __fadd2_rn(w.d12[i], D[i]);
+        const float2 gy = __ffma2_rn(R[i], m1, w.r1[i]);
+        w.d12[i] = __fadd2_rn(w.d2[i], D[i]);
+        w.d2[i] = D[i];
+        w.r1[i] = w.r2[i];
+        w.r2[i] = R[i];
+        if (emit && i < ncol) {
+          const float2 G = __ffma2_rn(__ffma2_rn(gx, gx, __fmul2_rn(gy, gy)), kk, ee);
+          // G1 - G2 from differences and sums of the gradients: no cancellation
+          const float dG = fmaf(gx.x - gx.y, gx.x + gx.y, (gy.x - gy.y) * (gy.x + gy.y)) * K;
+          const float S = G.x + G.y;
+          const float G12 = G.x * G.y;
+          const float d = -__fdividef(dG * dG, (S + 2.f * G12 * rsqrtf(G12)) * (S + p.T));
+          fs += d;
+          fs2 = fmaf(d, d, fs2);
+          if constexpr (MAP)
+            p.map[((long long)plane * p.Hout + (r0 + g0 + q - 2)) * p.Wout + dc0 + c0t + i] =
+                1.0f + d;
+        }
+      }
+    }
+  }
+}
+
 __device__ void gmsd_finalize(const GmsdArgs& p, int bpp) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nw = blockDim.x >> 5;
@@ -324,12 +384,13 @@ __global__ void __launch_bounds__(GM_T, 2) gmsd_kernel(GmsdArgs p) {
 
 
 // ---------------------------------------------------------------------------
-// uint8 kernel with TMA staging.  Each iteration of GM_R output rows needs
-// GM_R + 2 pooled rows, i.e. 2 * (GM_R + 2) input rows with the 2x2 pool.  They
-// arrive as one-row TMA boxes (GMT_BOX bytes, x rounded down to 16 bytes),
-// issued by all threads; the block pools them from shared memory into the
-// float ring, issues the next iteration's copies, then computes.  No thread
-// waits on a global load.
+// uint8 kernel with TMA staging.  The first iteration stages GM_R + 2 pooled
+// rows (2 * (GM_R + 2) input rows with the 2x2 pool), every later one the next
+// GM_R: the Prewitt window is carried in registers (GmWin), so no input row
+// is copied, pooled or differenced twice.  Rows arrive as one-row TMA boxes
+// (GMT_BOX bytes, x rounded down to 16 bytes), issued by all threads; the
+// block pools them from shared memory into the float ring, issues the next
+// iteration's copies, then computes.  No thread waits on a global load.
 // ---------------------------------------------------------------------------
 constexpr int GMT_BOX = 256;
 
@@ -371,13 +432,25 @@ __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant
   const int xin = (DOWN ? 2 * dc0 : dc0) + p.tma_d;
   const int x0 = (xin / 16) * 16, sofs = xin - x0;
 
-  auto issue = [&](int rb) {
-    if (t == 0) mbar_expect_tx(&s_bar, G::TX);
+  // The block needs pooled rows [r0, r0 + rows + 2).  Iteration 0 stages
+  // GM_R + 2 of them, every later one the next GM_R; the Prewitt window
+  // carries the two rows before each iteration's first in registers.
+  constexpr int PR = DOWN ? 2 : 1;  // input rows per pooled row
+  const int np_total = rows + 2;
+  auto first_of = [&](int it) { return it == 0 ? 0 : 2 + it * GM_R; };
+  auto count_of = [&](int it) {
+    const int f = first_of(it);
+    return min(it == 0 ? GM_R + 2 : GM_R, np_total - f);
+  };
+  auto issue = [&](int it) {
+    const int f = first_of(it), n = count_of(it);
+    const int rin = PR * n;
+    if (t == 0) mbar_expect_tx(&s_bar, 2u * rin * G::IW);
     fence_async_smem();
-    for (int i = t; i < 2 * G::RIN * G::NB; i += GM_T) {
-      const int img = i / (G::RIN * G::NB), rem = i - img * (G::RIN * G::NB);
+    for (int i = t; i < 2 * rin * G::NB; i += GM_T) {
+      const int img = i / (rin * G::NB), rem = i - img * (rin * G::NB);
       const int row = rem / G::NB, box = rem - row * G::NB;
-      const int in_row = DOWN ? 2 * (r0 + rb) + row : (r0 + rb) + row;
+      const int in_row = PR * (r0 + f) + row;
       unsigned char* dst = (img ? rawy : rawx) + row * G::IW + box * GMT_BOX;
       tma_row(dst, img ? &p.tmy : &p.tmx, x0 + box * GMT_BOX, in_row, pc, pn, &s_bar);
     }
@@ -388,16 +461,17 @@ __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant
   __syncthreads();
   issue(0);
 
+  GmWin win{};
   double acc = 0.0, acc2 = 0.0;
-  for (int rb = 0, it = 0; rb < rows; rb += GM_R, ++it) {
-    const int nr = min(GM_R, rows - rb);
+  for (int it = 0; first_of(it) < np_total; ++it) {
+    const int g0 = first_of(it), n = count_of(it);
     mbar_wait(&s_bar, it & 1, p.err);
     // pool (or convert) the staged bytes into the ring: exact integer 2x2
     // sums by dp4a (the 1/4 is folded into the Prewitt constant)
     const bool al4 = (sofs & 3) == 0;  // uniform: staged words are aligned
 #pragma unroll
     for (int q = 0; q < GM_R + 2; ++q) {
-      if (q < nr + 2) {
+      if (q < n) {
         float4 v;
         if (DOWN) {
           const int o = sofs + 4 * t;
@@ -430,9 +504,9 @@ __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant
       }
     }
     __syncthreads();
-    if (rb + GM_R < rows) issue(rb + GM_R);  // the staging buffer is free again
+    if (first_of(it + 1) < np_total) issue(it + 1);  // the staging buffer is free again
     float fs = 0.f, fs2 = 0.f;
-    gm_rows_packed<MAP, DOWN>(p, ring, G::RP, nr, t, dc0, plane, r0 + rb, fs, fs2);
+    gm_rows_window<MAP, DOWN>(p, ring, G::RP, n, g0, t, dc0, plane, r0, win, fs, fs2);
     acc += (double)fs;
     acc2 += (double)fs2;
     __syncthreads();  // the ring is rewritten next iteration

@@ -202,6 +202,63 @@ __device__ __forceinline__ void reduce_run(const T* pa, const T* pb, long long l
   }
 }
 
+// reduce_run for the contiguous-image kernel, with one contiguous span of the
+// run's 16-byte vectors per block (block `blk` of `nblk`, thread `t` of
+// PIX_THREADS): every step reads PIX_UNROLL x 4 KB of each operand as one
+// coalesced sweep, and each block streams its own DRAM pages instead of
+// striding the whole image.  Block 0 also takes the unaligned head and tail.
+template <typename T, int OP>
+__device__ __forceinline__ void reduce_span(const T* pa, const T* pb, long long len, int blk,
+                                            int nblk, int t,
+                                            typename PixTraits<T, OP>::Acc& acc,
+                                            const float* lut, float pf, double pd) {
+  constexpr int E = 16 / sizeof(T);
+  constexpr int STEP = PIX_UNROLL * PIX_THREADS;
+  const uintptr_t ua = reinterpret_cast<uintptr_t>(pa);
+  const uintptr_t ub = reinterpret_cast<uintptr_t>(pb);
+  if (((ua ^ ub) & 15u) != 0) {
+    reduce_run<T, OP>(pa, pb, len, (long long)blk * PIX_THREADS + t,
+                      (long long)nblk * PIX_THREADS, acc, lut, pf, pd);
+    return;
+  }
+  long long head = (long long)(((16u - (ua & 15u)) & 15u) / sizeof(T));
+  if (head > len) head = len;
+  const long long nv = (len - head) / E;
+  const long long tail0 = head + nv * E;
+  if (blk == 0) {
+    if (t < head) accum_one<T, OP>(ldro(pa + t), ldro(pb + t), acc, lut, pf, pd);
+    if (tail0 + t < len) accum_one<T, OP>(ldro(pa + tail0 + t), ldro(pb + tail0 + t), acc, lut, pf, pd);
+  }
+  // spans are whole steps, so only the last block's last step is ragged
+  const long long per = (nv + (long long)nblk * STEP - 1) / ((long long)nblk * STEP) * STEP;
+  const long long lo = (long long)blk * per;
+  const long long hi = lo + per < nv ? lo + per : nv;
+  const uint4* va = reinterpret_cast<const uint4*>(pa + head);
+  const uint4* vb = reinterpret_cast<const uint4*>(pb + head);
+  for (long long v0 = lo; v0 < hi; v0 += STEP) {
+    uint4 xa[PIX_UNROLL], xb[PIX_UNROLL];
+    if (v0 + STEP <= hi) {
+#pragma unroll
+      for (int u = 0; u < PIX_UNROLL; ++u) {
+        xa[u] = __ldg(va + v0 + u * PIX_THREADS + t);
+        xb[u] = __ldg(vb + v0 + u * PIX_THREADS + t);
+      }
+#pragma unroll
+      for (int u = 0; u < PIX_UNROLL; ++u) accum_vec<T, OP>(xa[u], xb[u], acc, lut, pf, pd);
+    } else {
+#pragma unroll
+      for (int u = 0; u < PIX_UNROLL; ++u) {
+        const long long v = v0 + u * PIX_THREADS + t;
+        xa[u] = v < hi ? __ldg(va + v) : make_uint4(0, 0, 0, 0);
+        xb[u] = v < hi ? __ldg(vb + v) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < PIX_UNROLL; ++u)
+        if (v0 + u * PIX_THREADS + t < hi) accum_vec<T, OP>(xa[u], xb[u], acc, lut, pf, pd);
+    }
+  }
+}
+
 // Luma rows: dY = k0*dR + k1*dG + k2*dB in float64 (the luma offset cancels).
 template <typename T, int OP>
 __device__ __forceinline__ void reduce_luma_row(const T* ra, const T* rb, long long sc,
@@ -283,15 +340,19 @@ __device__ __forceinline__ void fill_lut(float* lut, float pf) {
 template <typename Acc>
 __device__ void pix_finalize(const PixArgs& p, double n_per_image) {
   __shared__ Acc s_red[32];
-  const Acc* part = static_cast<const Acc*>(p.partial);
+  __shared__ Acc s_img[64];  // per-image sums of small batches stay on chip
+  Acc* part = static_cast<Acc*>(p.partial);
+  const bool on_chip = p.n <= 64;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  // 1. per-image sums, one warp per image; stash them in slot 0 of the row
+  // 1. per-image sums, one warp per image; kept in shared memory (small
+  //    batches) or in slot 0 of the image's partials row
   for (int img = wid; img < p.n; img += PIX_WARPS) {
     Acc s = 0;
     for (int i = lane; i < p.bpi; i += 32) s += part[(long long)img * p.bpi + i];
     s = warp_sum(s);
     if (lane == 0) {
-      const_cast<Acc*>(part)[(long long)img * p.bpi] = s;
+      if (on_chip) s_img[img] = s;
+      else part[(long long)img * p.bpi] = s;
       const double v = (double)s / n_per_image;
       if (p.out_per_image) p.out_per_image[img] = v;
       if (p.psnr_bias != FA_PSNR_NONE && p.out_psnr_per_image)
@@ -300,10 +361,11 @@ __device__ void pix_finalize(const PixArgs& p, double n_per_image) {
     }
   }
   __syncthreads();
-  __threadfence_block();
+  if (!on_chip) __threadfence_block();
   // 2. batch total over the per-image sums, fixed order
   Acc t = 0;
-  for (int img = threadIdx.x; img < p.n; img += blockDim.x) t += part[(long long)img * p.bpi];
+  for (int img = threadIdx.x; img < p.n; img += blockDim.x)
+    t += on_chip ? s_img[img] : part[(long long)img * p.bpi];
   t = block_sum(t, s_red);
   if (threadIdx.x == 0) {
     const double v = (double)t / (n_per_image * (double)p.n);
@@ -313,7 +375,8 @@ __device__ void pix_finalize(const PixArgs& p, double n_per_image) {
   }
 }
 
-// Contiguous images: block (bx, img) strides over image img's c*h*w elements.
+// Contiguous images: block (bx, img) streams span bx of image img's c*h*w
+// elements.
 template <typename T, int OP>
 __global__ void __launch_bounds__(PIX_THREADS, 6) pixel_flat_kernel(PixArgs p) {
   using Tr = PixTraits<T, OP>;
@@ -328,8 +391,7 @@ __global__ void __launch_bounds__(PIX_THREADS, 6) pixel_flat_kernel(PixArgs p) {
   const T* pa = reinterpret_cast<const T*>(p.a) + (long long)img * p.sn;
   const T* pb = reinterpret_cast<const T*>(p.b) + (long long)img * p.sn;
   Acc acc = 0;
-  reduce_run<T, OP>(pa, pb, per, (long long)blockIdx.x * PIX_THREADS + threadIdx.x,
-                    (long long)p.bpi * PIX_THREADS, acc, s_lut, p.pf, p.pd);
+  reduce_span<T, OP>(pa, pb, per, blockIdx.x, p.bpi, threadIdx.x, acc, s_lut, p.pf, p.pd);
   acc = block_sum(acc, s_red);
   if (threadIdx.x == 0) static_cast<Acc*>(p.partial)[(long long)img * p.bpi + blockIdx.x] = acc;
   if (last_block_arrived(p.counter, gridDim.x * gridDim.y, &s_flag))
