@@ -230,15 +230,18 @@ def pixel(x: torch.Tensor, y: torch.Tensor, *, op: int, param: float = 0.0,
 # --------------------------------------------------------------------------- #
 
 class Taps:
-    """The 1-D Gaussian window as host float32 taps: the kernels take them by
-    value in their launch parameters, so no device window is read."""
+    """The 1-D Gaussian window as host taps: float32 for the float32 kernels
+    (they take them by value in their launch parameters, so no device window
+    is read) and float64 for the float64 kernels."""
 
-    __slots__ = ("k", "arr", "values")
+    __slots__ = ("k", "arr", "values", "arr64")
 
-    def __init__(self, values):
+    def __init__(self, values, values64=None):
         self.values = tuple(float(v) for v in values)
         self.k = len(self.values)
         self.arr = (ctypes.c_float * self.k)(*self.values)
+        v64 = self.values if values64 is None else tuple(float(v) for v in values64)
+        self.arr64 = (ctypes.c_double * self.k)(*v64)
 
 
 @functools.lru_cache(maxsize=64)
@@ -256,9 +259,9 @@ def gaussian_taps(win_size: int, sigma: float) -> Tuple[float, ...]:
 def host_taps(win_size: int, sigma: float) -> Taps:
     """gaussian_taps rounded to float32: the same numbers as
     functional.gaussian_window_1d(..., dtype=torch.float32)."""
-    f32 = torch.tensor(gaussian_taps(int(win_size), float(sigma)),
-                       dtype=torch.float64).to(torch.float32)
-    return Taps(f32.tolist())
+    g = gaussian_taps(int(win_size), float(sigma))
+    f32 = torch.tensor(g, dtype=torch.float64).to(torch.float32)
+    return Taps(f32.tolist(), g)
 
 
 def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
@@ -267,9 +270,14 @@ def ssim_forward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                  want_cs: bool = False, want_per_image: bool = False,
                  want_total: bool = False) -> dict:
     """Fused SSIM forward, one launch.  ``win`` holds the window taps.
-    Returns a dict with the requested outputs."""
+    Returns a dict with the requested outputs.  float64 frames go to the
+    float64 kernels (everything, the map included, in double)."""
     L = lib()
     x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    if x.dtype == torch.float64:
+        return _ssim64_forward(x, y, win, C1=C1, C2=C2, luma=luma, want_map=want_map,
+                               want_plane=want_plane or want_cs, want_cs=want_cs,
+                               want_per_image=want_per_image, want_total=want_total)
     vx, x = as_view(x)
     vy, y = as_view(y)
     k = win.k
@@ -377,8 +385,12 @@ def ssim_backward(x: torch.Tensor, y: torch.Tensor, win: Taps, *,
                   gs: Optional[torch.Tensor] = None,
                   gcs: Optional[torch.Tensor] = None,
                   need_dx: bool = True, need_dy: bool = True):
-    """Fused SSIM backward (no scratch).  x, y: float32 (N,C,H,W)."""
+    """Fused SSIM backward (no scratch).  x, y: float32 (N,C,H,W); float64
+    frames take the float64 kernels (scratch: four coefficient planes)."""
     L = lib()
+    if x.dtype == torch.float64:
+        return _ssim64_backward(x, y, win, C1=C1, C2=C2, dmap=dmap, gscalar=gscalar, gs=gs,
+                                gcs=gcs, need_dx=need_dx, need_dy=need_dy)
     x = x.detach().to(torch.float32).contiguous()
     y = y.detach().to(torch.float32).contiguous()
     n, c, h, w = x.shape
@@ -443,12 +455,107 @@ def grad_scale(unit: torch.Tensor, g: torch.Tensor, *, per_image: bool,
 # GMSD
 # --------------------------------------------------------------------------- #
 
+# --------------------------------------------------------------------------- #
+# float64 frames
+# --------------------------------------------------------------------------- #
+
+def _ssim64_forward(x, y, win: Taps, *, C1, C2, luma, want_map, want_plane, want_cs,
+                    want_per_image, want_total) -> dict:
+    L = lib()
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    k = win.k
+    cm = 1 if luma is not None else vx.c
+    hout, wout = vx.h - k + 1, vx.w - k + 1
+    if hout <= 0 or wout <= 0:
+        raise ValueError(f"image {(vx.h, vx.w)} smaller than window {k}x{k}")
+    nb = _cached_ws("ssim64", L.fa_b200_ssim64_workspace_bytes, vx.n, vx.c, vx.h, vx.w, k,
+                    int(luma is not None))
+    ws = workspace(x, nb)
+    res = {"map": _f64(x, vx.n, cm, hout, wout) if want_map else None,
+           "plane_s": _f64(x, vx.n * cm) if want_plane else None,
+           "plane_cs": _f64(x, vx.n * cm) if want_cs else None,
+           "per_image": _f64(x, vx.n) if want_per_image else None,
+           "total": _f64(x) if want_total else None}
+    _call(x, L.fa_b200_ssim64, ctypes.byref(vx), ctypes.byref(vy), _luma_arg(luma), win.arr64,
+          k, float(C1), float(C2), ws.data_ptr(), ws.numel(), _ptr(res["map"]),
+          _ptr(res["plane_s"]), _ptr(res["plane_cs"]), _ptr(res["per_image"]),
+          _ptr(res["total"]), _dev(x), _stream(x))
+    return res
+
+
+def _ssim64_backward(x, y, win: Taps, *, C1, C2, dmap, gscalar, gs, gcs, need_dx, need_dy):
+    L = lib()
+    x = x.detach().contiguous()
+    y = y.detach().contiguous()
+    n, c, h, w = x.shape
+    k = win.k
+    coef = torch.empty((4, n * c, h - k + 1, w - k + 1), dtype=torch.float64, device=x.device)
+    dx = torch.empty_like(x) if need_dx else None
+    dy = torch.empty_like(y) if need_dy else None
+
+    def d64(t, flat=True):
+        if t is None:
+            return None
+        t = t.detach().to(torch.float64)
+        return (t.reshape(-1) if flat else t).contiguous()
+
+    _call(x, L.fa_b200_ssim64_backward, x.data_ptr(), y.data_ptr(), n, c, h, w, win.arr64, k,
+          float(C1), float(C2), _ptr(d64(dmap)), _ptr(d64(gscalar)), _ptr(d64(gs)),
+          _ptr(d64(gcs)), coef.data_ptr(), _ptr(dx), _ptr(dy), _dev(x), _stream(x))
+    return dx, dy
+
+
+def _gmsd64(x, y, *, T, eps, downsample, luma, want_map):
+    L = lib()
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    cm = 1 if luma is not None else vx.c
+    nb = _cached_ws("gmsd64", L.fa_b200_gmsd64_workspace_bytes, vx.n, vx.c, vx.h, vx.w,
+                    int(bool(downsample)), int(luma is not None), _dev(x))
+    ws = workspace(x, nb)
+    mean, std = _f64(x, vx.n), _f64(x, vx.n)
+    qmap = None
+    if want_map:
+        hd = vx.h // 2 if downsample else vx.h
+        wd = vx.w // 2 if downsample else vx.w
+        qmap = _f64(x, vx.n, cm, hd - 2, wd - 2)
+    _call(x, L.fa_b200_gmsd64, ctypes.byref(vx), ctypes.byref(vy), _luma_arg(luma), float(T),
+          float(eps), int(bool(downsample)), ws.data_ptr(), ws.numel(), _ptr(qmap),
+          mean.data_ptr(), std.data_ptr(), _dev(x), _stream(x))
+    return (mean, std, qmap) if want_map else (mean, std)
+
+
+def _gmsd64_backward(x, y, *, T, eps, downsample, mean, std, g_mean, g_std, need_dx, need_dy):
+    L = lib()
+    x = x.detach().contiguous()
+    y = y.detach().contiguous()
+    n, c, h, w = x.shape
+    hd, wd = (h // 2, w // 2) if downsample else (h, w)
+    coef = torch.empty((4, n * c, hd - 2, wd - 2), dtype=torch.float64, device=x.device)
+    dx = torch.empty_like(x) if need_dx else None
+    dy = torch.empty_like(y) if need_dy else None
+    zero = torch.zeros(n, dtype=torch.float64, device=x.device)
+
+    def d64(t):
+        return zero if t is None else t.detach().to(torch.float64).reshape(-1).contiguous()
+
+    _call(x, L.fa_b200_gmsd64_backward, x.data_ptr(), y.data_ptr(), n, c, h, w,
+          int(bool(downsample)), float(T), float(eps), d64(g_mean).data_ptr(),
+          d64(g_std).data_ptr(), d64(mean).data_ptr(), d64(std).data_ptr(), coef.data_ptr(),
+          _ptr(dx), _ptr(dy), _dev(x), _stream(x))
+    return dx, dy
+
+
 def gmsd(x: torch.Tensor, y: torch.Tensor, *, T: float, eps: float,
          downsample: bool, luma=None, want_map: bool = False):
     """``(gms_mean, gmsd)`` per image, float64, one launch (plus the float32
-    GMS map when ``want_map``)."""
+    GMS map when ``want_map``; float64 frames: the float64 kernels, float64
+    map)."""
     L = lib()
     x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    if x.dtype == torch.float64:
+        return _gmsd64(x, y, T=T, eps=eps, downsample=downsample, luma=luma, want_map=want_map)
     vx, x = as_view(x)
     vy, y = as_view(y)
     cm = 1 if luma is not None else vx.c
@@ -472,7 +579,7 @@ def gmsd(x: torch.Tensor, y: torch.Tensor, *, T: float, eps: float,
 
 
 def gms_map(x, y, *, T: float, eps: float, downsample: bool, luma=None) -> torch.Tensor:
-    """The (N, C', H'-2, W'-2) float32 GMS map."""
+    """The (N, C', H'-2, W'-2) GMS map (float32; float64 for float64 frames)."""
     return gmsd(x, y, T=T, eps=eps, downsample=downsample, luma=luma, want_map=True)[2]
 
 
@@ -482,8 +589,18 @@ def gms_map(x, y, *, T: float, eps: float, downsample: bool, luma=None) -> torch
 
 def pool2(x: torch.Tensor, luma=None) -> torch.Tensor:
     """2x2 mean pool to float32 (``F.avg_pool2d(x.float(), 2)``), one read of
-    ``x`` in its own dtype and strides; ``luma`` projects RGB first."""
+    ``x`` in its own dtype and strides; ``luma`` projects RGB first.  float64
+    planes pool to float64 (no luma: project first)."""
     L = lib()
+    if x.dtype == torch.float64:
+        if luma is not None:
+            raise ValueError("float64 pooling takes luma planes, not RGB")
+        x = x.contiguous()
+        n, c, h, w = x.shape
+        out = torch.empty((n, c, h // 2, w // 2), dtype=torch.float64, device=x.device)
+        _call(x, L.fa_b200_pool64, x.data_ptr(), n * c, h, w, out.data_ptr(), _dev(x),
+              _stream(x))
+        return out
     vx, x = as_view(kernel_dtype(x))
     cm = 1 if luma is not None else vx.c
     out = torch.empty((vx.n, cm, vx.h // 2, vx.w // 2), dtype=torch.float32, device=x.device)
@@ -518,8 +635,16 @@ def box_downsample_backward(g: torch.Tensor, shape, f: int) -> torch.Tensor:
 
 
 def pool2_backward(g: torch.Tensor, shape) -> torch.Tensor:
-    """Adjoint of :func:`pool2` for a float32 input of ``shape``."""
+    """Adjoint of :func:`pool2` for an input of ``shape`` (float32, or
+    float64 when ``g`` is float64)."""
     L = lib()
+    if g.dtype == torch.float64:
+        g = g.detach().contiguous()
+        n, c, h, w = shape
+        dx = torch.empty((n, c, h, w), dtype=torch.float64, device=g.device)
+        _call(g, L.fa_b200_pool64_backward, g.data_ptr(), n * c, h, w, dx.data_ptr(), _dev(g),
+              _stream(g))
+        return dx
     g = g.detach().to(torch.float32).contiguous()
     n, c, h, w = shape
     dx = torch.empty((n, c, h, w), dtype=torch.float32, device=g.device)
@@ -572,6 +697,9 @@ def gmsd_backward(x, y, *, T: float, eps: float, downsample: bool, mean, std,
                   g_mean=None, g_std=None, need_dx: bool = True, need_dy: bool = True):
     """Gradients of the per-image GMS (mean) and GMSD (std) w.r.t. x and y."""
     L = lib()
+    if x.dtype == torch.float64:
+        return _gmsd64_backward(x, y, T=T, eps=eps, downsample=downsample, mean=mean, std=std,
+                                g_mean=g_mean, g_std=g_std, need_dx=need_dx, need_dy=need_dy)
     xf = x.detach().to(torch.float32).contiguous()
     yf = y.detach().to(torch.float32).contiguous()
     n, c, h, w = xf.shape

@@ -24,6 +24,27 @@ int ssim_fwd_impl(const View& x, const View& y, int dtype, const double* luma, c
                   const SqOut* sq = nullptr, const float* wdev = nullptr,
                   const GmOut* gm = nullptr);
 bool ssim_gmsd_fusable(const View& x, const View& y, int dtype, int K, int device);
+size_t ssim64_ws_bytes(int planes, int h, int w, int K);
+int ssim64_fwd_impl(const View& x, const View& y, int dtype, const double* luma,
+                    const double* taps, int K, double C1, double C2, void* ws, size_t ws_bytes,
+                    double* map, double* out_plane_s, double* out_plane_cs,
+                    double* out_per_image, double* out_total, cudaStream_t st);
+int ssim64_bwd_impl(const double* x, const double* y, int N, int C, int H, int W,
+                    const double* taps, int K, double C1, double C2, const double* dmap,
+                    const double* gscalar, const double* gs, const double* gcs, double* coef,
+                    double* dx, double* dy, cudaStream_t st);
+int pool64_impl(const double* in, int NC, int H, int W, double* out, int device,
+                cudaStream_t st);
+int pool64_bwd_impl(const double* g, int NC, int H, int W, double* dx, int device,
+                    cudaStream_t st);
+size_t gmsd64_ws_bytes(int planes, int h, int w, int down, int device);
+int gmsd64_impl(const View& x, const View& y, int dtype, const double* luma, double T,
+                double eps, int down, void* ws, size_t ws_bytes, double* map,
+                double* out_mean, double* out_std, int device, cudaStream_t st);
+int gmsd64_bwd_impl(const double* x, const double* y, int N, int C, int H, int W, int down,
+                    double T, double eps, const double* gm, const double* gsd, const double* mu,
+                    const double* sd, double* coef, double* dx, double* dy, int device,
+                    cudaStream_t st);
 size_t ssim_ws_bytes(int planes, int Hout, int Wout, int K, int device);
 int ssim_bwd_impl(const float* x, const float* y, int N, int C, int H, int W, const float* win,
                   int K, double shift, double C1, double C2, const float* dmap,
@@ -557,6 +578,94 @@ FA_B200_API int fa_b200_pixel_loss_grad(const float* x, const float* y, int N,
   return pixel_loss_grad_impl(x, y, N, per_image_elems, op, param, per_image, workspace,
                               workspace_bytes, out_per_image, out_total, dx, dy, device,
                               static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// float64 block
+// ---------------------------------------------------------------------------
+
+FA_B200_API int fa_b200_ssim64_workspace_bytes(int n, int c, int h, int w, int K, int luma,
+                                               size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (n <= 0 || c <= 0 || h < K || w < K) return FA_E_SHAPE;
+  *out_bytes = ssim64_ws_bytes(n * (luma ? 1 : c), h, w, K);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_ssim64(const fa_view* x, const fa_view* y, const double* luma,
+                               const double* taps_host, int K, double C1, double C2,
+                               void* workspace, size_t workspace_bytes, double* map_out,
+                               double* out_plane_s, double* out_plane_cs, double* out_per_image,
+                               double* out_total, int device, void* stream) {
+  FAB_PENDING();
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (workspace) FAB_TRY(cudaMemsetAsync(workspace, 0, FAB_COUNTER_BYTES, st));
+  return ssim64_fwd_impl(to_view(*x), to_view(*y), x->dtype, luma, taps_host, K, C1, C2,
+                         workspace, workspace_bytes, map_out, out_plane_s, out_plane_cs,
+                         out_per_image, out_total, st);
+}
+
+FA_B200_API int fa_b200_ssim64_backward(const double* x, const double* y, int N, int C, int H,
+                                        int W, const double* taps_host, int K, double C1,
+                                        double C2, const double* dL_dmap,
+                                        const double* grad_scalar, const double* gs,
+                                        const double* gcs, double* coef, double* dx,
+                                        double* dy, int device, void* stream) {
+  FAB_PENDING();
+  FAB_DEVICE_SCOPE(device);
+  return ssim64_bwd_impl(x, y, N, C, H, W, taps_host, K, C1, C2, dL_dmap, grad_scalar, gs, gcs,
+                         coef, dx, dy, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_pool64(const double* in, int NC, int H, int W, double* out, int device,
+                               void* stream) {
+  FAB_PENDING();
+  FAB_DEVICE_SCOPE(device);
+  return pool64_impl(in, NC, H, W, out, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_pool64_backward(const double* g, int NC, int H, int W, double* dx,
+                                        int device, void* stream) {
+  FAB_PENDING();
+  FAB_DEVICE_SCOPE(device);
+  return pool64_bwd_impl(g, NC, H, W, dx, device, static_cast<cudaStream_t>(stream));
+}
+
+FA_B200_API int fa_b200_gmsd64_workspace_bytes(int n, int c, int h, int w, int downsample,
+                                               int luma, int device, size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return FA_E_SHAPE;
+  FAB_DEVICE_SCOPE(device);
+  *out_bytes = gmsd64_ws_bytes(n * (luma ? 1 : c), h, w, downsample, device);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_gmsd64(const fa_view* x, const fa_view* y, const double* luma, double T,
+                               double eps, int downsample, void* workspace,
+                               size_t workspace_bytes, double* map_out, double* out_mean,
+                               double* out_std, int device, void* stream) {
+  FAB_PENDING();
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (workspace) FAB_TRY(cudaMemsetAsync(workspace, 0, FAB_COUNTER_BYTES, st));
+  return gmsd64_impl(to_view(*x), to_view(*y), x->dtype, luma, T, eps, downsample, workspace,
+                     workspace_bytes, map_out, out_mean, out_std, device, st);
+}
+
+FA_B200_API int fa_b200_gmsd64_backward(const double* x, const double* y, int N, int C, int H,
+                                        int W, int downsample, double T, double eps,
+                                        const double* g_mean, const double* g_std,
+                                        const double* mean, const double* std_, double* coef,
+                                        double* dx, double* dy, int device, void* stream) {
+  FAB_PENDING();
+  FAB_DEVICE_SCOPE(device);
+  return gmsd64_bwd_impl(x, y, N, C, H, W, downsample, T, eps, g_mean, g_std, mean, std_, coef,
+                         dx, dy, device, static_cast<cudaStream_t>(stream));
 }
 
 // Test hook of the bounded waits: one thread waits `limit_ns` for an mbarrier

@@ -367,7 +367,8 @@ class _FusedSSIM(torch.autograd.Function):
             dx, dy = backend.ssim_backward(x, y, win, gscalar=g, **kw)
         else:
             n, c = x.shape[0], x.shape[1]
-            gs = (g.to(torch.float32) / c).repeat_interleave(c)
+            gdt = torch.float64 if x.dtype == torch.float64 else torch.float32
+            gs = (g.to(gdt) / c).repeat_interleave(c)
             dx, dy = backend.ssim_backward(x, y, win, gs=gs, gcs=torch.zeros_like(gs), **kw)
         return (dx.to(x.dtype) if nx else None, dy.to(y.dtype) if ny else None,
                 None, None, None, None, None)
@@ -497,14 +498,16 @@ def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None
     win = _kernel_window(win_size, sigma, x4.device)
 
     if grad:
-        # the fused backward reads float32 planes: luma/crop/cast are applied
-        # with differentiable torch ops first
+        # the fused backward reads float32 planes (float64 frames: float64
+        # planes and the float64 kernels): luma/crop/cast are applied with
+        # differentiable torch ops first
         if lk is not None:
             x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
-        xf = x4 if x4.dtype == torch.float32 else x4.to(torch.float32)
-        yf = y4 if y4.dtype == torch.float32 else y4.to(torch.float32)
+        cdt = torch.float64 if x4.dtype == torch.float64 else torch.float32
+        xf = x4 if x4.dtype == cdt else x4.to(cdt)
+        yf = y4 if y4.dtype == cdt else y4.to(cdt)
         m = "map" if return_map else reduction
-        if _fused_loss_grad and m != "map":
+        if _fused_loss_grad and m != "map" and cdt == torch.float32:
             return _SSIMLossGrad.apply(xf.contiguous(), yf.contiguous(), win, shift, C1, C2, m,
                                        xf.requires_grad, yf.requires_grad)
         return _FusedSSIM.apply(xf.contiguous(), yf.contiguous(), win, shift, C1, C2, m)
@@ -557,9 +560,10 @@ def metrics(x: torch.Tensor, y: torch.Tensor, names: Sequence[str] = ("mse", "ps
     backend.require_cuda(x4)
     out = {}
     no_grad = not _grad_wanted(x4, y4)
+    f32_ssim = x4.dtype != torch.float64  # float64 SSIM has kernels of its own
     want_gm = [n for n in ("gms", "gmsd") if n in names]
     want_sq = "mse" in names or "psnr" in names
-    if fuse_gmsd and "ssim" in names and want_gm and no_grad and win_size == 11 and \
+    if fuse_gmsd and f32_ssim and "ssim" in names and want_gm and no_grad and win_size == 11 and \
             backend.ssim_gmsd_fusable(x4, y4, win_size):
         K1, K2 = float(K[0]), float(K[1])
         res = backend.ssim_gmsd(x4.detach(), y4.detach(), _kernel_window(win_size, sigma, x4.device),
@@ -572,7 +576,7 @@ def metrics(x: torch.Tensor, y: torch.Tensor, names: Sequence[str] = ("mse", "ps
                 out[n] = res[n]
         for n in want_gm:
             out[n] = res[n] if reduction == "none" else res[n].mean()
-    fused = "ssim" in names and "ssim" not in out and want_sq and no_grad and \
+    fused = f32_ssim and "ssim" in names and "ssim" not in out and want_sq and no_grad and \
         min(x4.shape[-2:]) >= win_size
     if fused:
         K1, K2 = float(K[0]), float(K[1])
@@ -628,7 +632,7 @@ class _FusedSSIMCS(torch.autograd.Function):
         if not (nx or ny):
             return (None,) * 6
         if g_s is None:
-            g_s = torch.zeros(x.shape[0] * x.shape[1], dtype=torch.float32, device=x.device)
+            g_s = torch.zeros(x.shape[0] * x.shape[1], dtype=x.dtype, device=x.device)
         if g_cs is None:
             g_cs = torch.zeros_like(g_s)
         dx, dy = backend.ssim_backward(x, y, win, shift=shift, C1=C1, C2=C2,
@@ -737,7 +741,9 @@ def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = N
     win = _kernel_window(win_size, sigma, x4.device)
     lk = _luma_k(mode, L)
     grad = _grad_wanted(x4, y4)
-    if lk is not None and grad:
+    f64 = x4.dtype == torch.float64
+    if lk is not None and (grad or f64):
+        # (float64 pooling reads luma planes)
         x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
         lk = None
     n = x4.shape[0]
@@ -761,8 +767,9 @@ def ms_ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = N
                 pl = lk if i == 1 else None
                 cx, cy = backend.pool2(cx, luma=pl), backend.pool2(cy, luma=pl)
         if grad:
-            xf = cx.to(torch.float32).contiguous()
-            yf = cy.to(torch.float32).contiguous()
+            cdt = torch.float64 if f64 else torch.float32
+            xf = cx.to(cdt).contiguous()
+            yf = cy.to(cdt).contiguous()
             s, cs = _FusedSSIMCS.apply(xf, yf, win, shift, C1, C2)
         else:
             res = backend.ssim_forward(cx.detach(), cy.detach(), win, shift=shift, C1=C1,
@@ -826,8 +833,9 @@ def _gmsd_common(x, y, data_range, T, eps, downsample, luma, crop_border, reduct
         # differentiable torch ops first
         if lk is not None:
             x4, y4 = rgb_to_luma(x4, mode, data_range=L), rgb_to_luma(y4, mode, data_range=L)
-        xf = x4.to(torch.float32).contiguous()
-        yf = y4.to(torch.float32).contiguous()
+        cdt = torch.float64 if x4.dtype == torch.float64 else torch.float32
+        xf = x4.to(cdt).contiguous()
+        yf = y4.to(cdt).contiguous()
         return None, _GmsdFn.apply(xf, yf, Tv, ev, bool(downsample))
     return None, backend.gmsd(x4.detach(), y4.detach(), T=Tv, eps=ev,
                               downsample=downsample, luma=lk)

@@ -463,6 +463,59 @@ FA_B200_API int fa_b200_pixel_reduce_noalloc(
     double* out_psnr_per_image, double* out_psnr_total,
     uint64_t* out_isum_per_image, int device, void* stream);
 
+/* ----------------------------------------------------------------------- */
+/* float64 block.  No native counterpart in the reference: its native SSIM /  */
+/* MS-SSIM / GMSD decline float64 input (backend.py:466, 602) and run the     */
+/* float64 torch path (functional.py:589-689, 697-901, 974-1082).  These      */
+/* calls keep every moment, sum and gradient in double.  dtype must be        */
+/* FA_F64; taps_host are the K double taps in HOST memory; the workspace      */
+/* (sized by the *_workspace_bytes query) needs no zeroing (each call clears  */
+/* its counters on `stream`).                                                 */
+/* ----------------------------------------------------------------------- */
+
+/* SSIM of float64 frames (reference.py:118-160 in float64): outputs as
+ * fa_b200_ssim, the map as float64 [N, C', Hout, Wout]. */
+FA_B200_API int fa_b200_ssim64_workspace_bytes(int n, int c, int h, int w, int K,
+                                               int luma, size_t* out_bytes);
+FA_B200_API int fa_b200_ssim64(const fa_view* x, const fa_view* y, const double* luma,
+                               const double* taps_host, int K, double C1, double C2,
+                               void* workspace, size_t workspace_bytes, double* map_out,
+                               double* out_plane_s, double* out_plane_cs,
+                               double* out_per_image, double* out_total, int device,
+                               void* stream);
+/* Gradient of the float64 SSIM: exactly one of dL_dmap ([N*C, Hout, Wout]),
+ * grad_scalar ([1], of the batch mean) or gs + gcs ([N*C], of the per-plane
+ * mean SSIM and cs) is given.  coef: caller scratch of 4*N*C*Hout*Wout
+ * doubles.  x, y, dx, dy: contiguous [N, C, H, W] float64. */
+FA_B200_API int fa_b200_ssim64_backward(const double* x, const double* y, int N, int C,
+                                        int H, int W, const double* taps_host, int K,
+                                        double C1, double C2, const double* dL_dmap,
+                                        const double* grad_scalar, const double* gs,
+                                        const double* gcs, double* coef, double* dx,
+                                        double* dy, int device, void* stream);
+/* 2x2 average pool of contiguous float64 planes (odd trailing row / column
+ * dropped, reference.py:231-241) and its adjoint. */
+FA_B200_API int fa_b200_pool64(const double* in, int NC, int H, int W, double* out,
+                               int device, void* stream);
+FA_B200_API int fa_b200_pool64_backward(const double* g, int NC, int H, int W,
+                                        double* dx, int device, void* stream);
+/* GMS mean / GMSD per image of float64 frames, as fa_b200_gmsd (map float64). */
+FA_B200_API int fa_b200_gmsd64_workspace_bytes(int n, int c, int h, int w, int downsample,
+                                               int luma, int device, size_t* out_bytes);
+FA_B200_API int fa_b200_gmsd64(const fa_view* x, const fa_view* y, const double* luma,
+                               double T, double eps, int downsample, void* workspace,
+                               size_t workspace_bytes, double* map_out, double* out_mean,
+                               double* out_std, int device, void* stream);
+/* Gradient of the per-image (mean, std) of q for upstream g_mean, g_std [N],
+ * given the forward's mean and std [N].  coef: caller scratch of
+ * 4*N*C*Hout*Wout doubles (the GMS map size).  Contiguous float64 frames. */
+FA_B200_API int fa_b200_gmsd64_backward(const double* x, const double* y, int N, int C,
+                                        int H, int W, int downsample, double T, double eps,
+                                        const double* g_mean, const double* g_std,
+                                        const double* mean, const double* std_,
+                                        double* coef, double* dx, double* dy, int device,
+                                        void* stream);
+
 /* No counterpart in the reference: test hook of the bounded device-side
  * waits.  Launches one thread that waits `limit_ns` (at most 1 s) for an
  * mbarrier phase that nothing completes and then records FA_E_TIMEOUT the
