@@ -2,7 +2,7 @@
 
 A drop-in for the metric path of frame_analytics: ``psnr``, ``mse``, ``l1``,
 ``charbonnier``, ``huber``, ``ssim`` (forward and fused backward),
-``ms_ssim``, ``gmsd`` / ``gms``, with the same arguments and results,
+``ms_ssim``, ``gmsd`` / ``gms``, ``ssimulacra2``, with the same arguments and results,
 computed by hand-written CUDA kernels behind a C ABI (``include/fa_b200.h``).
 
 >>> import torch, frame_analytics_b200 as fa
@@ -30,6 +30,7 @@ from .functional import (  # noqa: F401
     ssim,
 )
 from . import planes  # noqa: F401
+from .ssimulacra2 import SSIMULACRA2, ssimulacra2  # noqa: F401
 from .modules import (GMSD, L1, MSE, MSSSIM, PSNR, SSIM, Charbonnier, Huber,  # noqa: F401
                       StreamingMetrics)
 
@@ -40,7 +41,7 @@ __all__ = [
     "rgb_to_luma", "gaussian_window_1d", "set_compile_enabled",
     "set_fused_loss_grad", "metrics", "StreamingMetrics",
     "MSE", "PSNR", "SSIM", "MSSSIM", "GMSD", "L1", "Charbonnier", "Huber",
-    "backend_status",
+    "ssimulacra2", "SSIMULACRA2", "backend_status",
 ]
 
 

@@ -21,7 +21,8 @@ CSRC = HERE / "csrc"
 LIBDIR = HERE / "_lib"
 LIB = LIBDIR / "libfa_b200.so"
 SOURCES = ["abi.cu", "pixel.cu", "ssim_fwd.cu", "ssim_bwd.cu", "gmsd.cu", "pool.cu", "grad_scale.cu",
-           "ssim_compat.cu", "f64.cu"]
+           "ssim_compat.cu", "f64.cu",
+           "ssimulacra2.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -121,6 +121,8 @@ PROTOTYPES = {
     "fa_b200_pool2_backward": [_vp, _i, _i, _i, _i, _vp, _i, _vp],
     "fa_b200_wait_selftest": [ctypes.c_ulonglong, _i, _vp],
     "fa_b200_ssim_gmsd_fusable": [_pview, _pview, _i, _i, _vp],
+    "fa_b200_ssimulacra2_workspace_bytes": [_i, _i, _i, _i, _vp],
+    "fa_b200_ssimulacra2": [_pview, _pview, _d, _i, _vp, _vp, _sz, _vp, _vp, _i, _vp],
     "fa_b200_ssim64_workspace_bytes": [_i, _i, _i, _i, _i, _i, _vp],
     "fa_b200_ssim64": [_pview, _pview, _vp, _vp, _i, _d, _d, _vp, _sz, _vp, _vp, _vp, _vp, _vp,
                        _i, _vp],

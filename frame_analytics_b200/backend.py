@@ -584,6 +584,27 @@ def gms_map(x, y, *, T: float, eps: float, downsample: bool, luma=None) -> torch
 
 
 # --------------------------------------------------------------------------- #
+# SSIMULACRA 2
+# --------------------------------------------------------------------------- #
+
+def ssimulacra2(x: torch.Tensor, y: torch.Tensor, *, data_range: float, f64: bool, weights,
+                per_image: bool) -> torch.Tensor:
+    """SSIMULACRA 2 of (N, 3, H, W) sRGB pairs (any dtype and strides; channel
+    stride 0 for a replicated gray plane): float64 scores, (N,) or 0-d."""
+    L = lib()
+    x, y = same_layout(kernel_dtype(x), kernel_dtype(y))
+    vx, x = as_view(x)
+    vy, y = as_view(y)
+    nb = _cached_ws("su2", L.fa_b200_ssimulacra2_workspace_bytes, vx.n, vx.h, vx.w, int(f64))
+    ws = workspace(x, nb)
+    out = _f64(x, vx.n) if per_image else _f64(x)
+    _call(x, L.fa_b200_ssimulacra2, ctypes.byref(vx), ctypes.byref(vy), float(data_range),
+          int(f64), weights, ws.data_ptr(), ws.numel(), _ptr(out) if per_image else None,
+          None if per_image else out.data_ptr(), _dev(x), _stream(x))
+    return out
+
+
+# --------------------------------------------------------------------------- #
 # MS-SSIM pyramid pooling
 # --------------------------------------------------------------------------- #
 

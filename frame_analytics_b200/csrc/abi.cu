@@ -38,6 +38,10 @@ int pool64_impl(const double* in, int NC, int H, int W, double* out, int device,
 int pool64_bwd_impl(const double* g, int NC, int H, int W, double* dx, int device,
                     cudaStream_t st);
 size_t gmsd64_ws_bytes(int planes, int h, int w, int down, int device);
+size_t su2_ws_bytes(int N, int H, int W, int fsize);
+int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64,
+             const double* weights, void* ws, size_t ws_bytes, double* out_per_image,
+             double* out_total, int device, cudaStream_t st);
 int gmsd64_impl(const View& x, const View& y, int dtype, const double* luma, double T,
                 double eps, int down, void* ws, size_t ws_bytes, double* map,
                 double* out_mean, double* out_std, int device, cudaStream_t st);
@@ -666,6 +670,33 @@ FA_B200_API int fa_b200_gmsd64_backward(const double* x, const double* y, int N,
   FAB_DEVICE_SCOPE(device);
   return gmsd64_bwd_impl(x, y, N, C, H, W, downsample, T, eps, g_mean, g_std, mean, std_, coef,
                          dx, dy, device, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// SSIMULACRA 2
+// ---------------------------------------------------------------------------
+
+FA_B200_API int fa_b200_ssimulacra2_workspace_bytes(int n, int h, int w, int f64,
+                                                    size_t* out_bytes) {
+  if (!out_bytes) return FA_E_ARG;
+  if (n <= 0 || h < 8 || w < 8) return FA_E_SHAPE;
+  *out_bytes = su2_ws_bytes(n, h, w, f64 ? 8 : 4);
+  return FA_OK;
+}
+
+FA_B200_API int fa_b200_ssimulacra2(const fa_view* x, const fa_view* y, double data_range,
+                                    int f64, const double* weights, void* workspace,
+                                    size_t workspace_bytes, double* out_per_image,
+                                    double* out_total, int device, void* stream) {
+  FAB_PENDING();
+  if (!view_ok(x) || !view_ok(y)) return FA_E_ARG;
+  if (x->dtype != y->dtype) return FA_E_DTYPE;
+  FAB_DEVICE_SCOPE(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!workspace) return FA_E_ARG;
+  FAB_TRY(cudaMemsetAsync(workspace, 0, FAB_COUNTER_BYTES, st));
+  return su2_impl(to_view(*x), to_view(*y), x->dtype, data_range, f64, weights, workspace,
+                  workspace_bytes, out_per_image, out_total, device, st);
 }
 
 // Test hook of the bounded waits: one thread waits `limit_ns` for an mbarrier

@@ -1,0 +1,470 @@
+// SSIMULACRA 2 on sm_100a (Sneyers; libjxl tools/ssimulacra2.cc, as the
+// reference computes it: frame_analytics/ssimulacra2.py, with its float64
+// transcription in frame_analytics/reference.py:540-700).
+//
+// Per image pair (original x, distorted y; sRGB in [0, L], 3 channels):
+//   scale 0      linear RGB = sRGB EOTF(v / L)
+//   scale s > 0  2x2 box mean of the previous scale's linear RGB, an odd last
+//                row / column averaged with itself (ceil sizes); a scale is
+//                computed while the previous one is at least 8 x 8
+//   per scale    positive XYB of both images; blurred (same size, zero
+//                outside) x1, x2, x1^2 + x2^2 and (x1 - x2)^2 with the 11-tap
+//                FIR equivalent of the recursive Gaussian (sigma 1.5); per
+//                pixel and channel the SSIM' error d, and the ringing / blurring
+//                maps from e = (|x2 - mu2| - |x1 - mu1|) / (1 + |x1 - mu1|);
+//                the mean and the 4-norm of each map per channel
+//   score        108 weighted |norms|, a cubic and a power law
+//
+// Kernels (compute type F = float, the reference's default, or double):
+//   su2_down_kernel    the next scale's linear planes (from the input at
+//                      scale 1, from the previous linear planes after that)
+//   su2_scale_kernel   one block per 32 x 8 tile of one image: the tile plus a
+//                      5-pixel halo of both images is converted to XYB in
+//                      shared memory, the four groups are blurred separably
+//                      per channel, the maps are formed and the 18 per-channel
+//                      sums reduced; the last block of the launch turns each
+//                      image's sums into its 18 norms
+//   su2_score_kernel   the weighted sum and the final mapping, per image and
+//                      for the batch
+// Every sum is double.
+#include <algorithm>
+
+#include "ssim_common.cuh"  // ensure_smem
+
+namespace fab {
+
+constexpr int SU_W = 32, SU_H = 8, SU_R = 5;  // tile, blur radius
+constexpr int SU_T = SU_W * SU_H;
+constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
+constexpr int SU_SCALES = 6;
+constexpr int SU_SUMS = 18;  // 3 channels x {d, d^4, art, art^4, lost, lost^4}
+
+struct Su2Args {
+  // scale-0 input (any dtype and strides; channel stride 0 replicates gray)
+  const char* x;
+  const char* y;
+  int dtype;
+  long long sn, sc, sh;
+  double inv_range;
+  // linear planes of this scale (scale > 0): [N][3][h][w]
+  const void* lx;
+  const void* ly;
+  int N, h, w;  // this scale's size
+  int scale;
+  double taps[2 * SU_R + 1];
+  double mat[9];  // opsin absorbance matrix, row-major
+  double bias, cbrt_bias;
+  int tiles_x, tiles_y;
+  unsigned int* counter;
+  double* part;   // [N][tiles][18]
+  double* norms;  // [N][6 scales][18]
+};
+
+template <typename T>
+__device__ __forceinline__ double su_raw(const char* base, long long o) {
+  return Ld<T>::d(ldro(reinterpret_cast<const T*>(base) + o));
+}
+
+template <typename F>
+__device__ __forceinline__ F srgb_to_linear(F v) {
+  if (v <= F(0.04045)) return v / F(12.92);
+  F b = (v + F(0.055)) / F(1.055);
+  b = b > F(0) ? b : F(0);
+  if constexpr (sizeof(F) == 4) return powf(b, 2.4f);
+  else return pow(b, 2.4);
+}
+
+template <typename T, typename F>
+__device__ __forceinline__ F su_input_linear(const Su2Args& p, const char* base, int n, int c,
+                                             int r, int col) {
+  const long long o = (long long)n * p.sn + (long long)c * p.sc + (long long)r * p.sh + col;
+  return srgb_to_linear<F>(F(su_raw<T>(base, o)) * F(p.inv_range));
+}
+
+// Linear RGB of (n, c, r, col) at this scale: from the input (scale 0) or the
+// linear planes.
+template <typename T, typename F>
+__device__ __forceinline__ F su_linear(const Su2Args& p, bool second, int n, int c, int r,
+                                       int col) {
+  if (p.scale == 0) return su_input_linear<T, F>(p, second ? p.y : p.x, n, c, r, col);
+  const F* l = static_cast<const F*>(second ? p.ly : p.lx);
+  return l[(((long long)n * 3 + c) * p.h + r) * p.w + col];
+}
+
+template <typename F>
+__device__ __forceinline__ void to_xyb(const Su2Args& p, F r, F g, F b, F& X, F& Y, F& B) {
+  F m[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    F v = F(p.mat[3 * j]) * r + F(p.mat[3 * j + 1]) * g + F(p.mat[3 * j + 2]) * b + F(p.bias);
+    v = v > F(0) ? v : F(0);
+    if constexpr (sizeof(F) == 4) m[j] = cbrtf(v) - F(p.cbrt_bias);
+    else m[j] = cbrt(v) - p.cbrt_bias;
+  }
+  const F xx = F(0.5) * (m[0] - m[1]), yy = F(0.5) * (m[0] + m[1]);
+  X = xx * F(14.0) + F(0.42);
+  Y = yy + F(0.01);
+  B = (m[2] - yy) + F(0.55);
+}
+
+// 2x2 box mean, source index clamped to the edge.  SRC_INPUT: the scale-0
+// input (EOTF applied per sample first); else the previous linear planes of
+// size (ph, pw).
+template <typename T, typename F, bool SRC_INPUT>
+__global__ void __launch_bounds__(256) su2_down_kernel(const Su2Args p, int ph, int pw, F* ox,
+                                                       F* oy) {
+  const long long n_out = (long long)p.N * 3 * p.h * p.w;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n_out; i += 256LL * gridDim.x) {
+    const int col = (int)(i % p.w), r = (int)((i / p.w) % p.h);
+    const int c = (int)((i / ((long long)p.w * p.h)) % 3), n = (int)(i / (3LL * p.w * p.h));
+    const int r0 = min(2 * r, ph - 1), r1 = min(2 * r + 1, ph - 1);
+    const int c0 = min(2 * col, pw - 1), c1 = min(2 * col + 1, pw - 1);
+#pragma unroll
+    for (int img = 0; img < 2; ++img) {
+      F a, b, cc, d;
+      if constexpr (SRC_INPUT) {
+        const char* base = img ? p.y : p.x;
+        a = su_input_linear<T, F>(p, base, n, c, r0, c0);
+        b = su_input_linear<T, F>(p, base, n, c, r0, c1);
+        cc = su_input_linear<T, F>(p, base, n, c, r1, c0);
+        d = su_input_linear<T, F>(p, base, n, c, r1, c1);
+      } else {
+        const F* l = static_cast<const F*>(img ? p.ly : p.lx) + ((long long)n * 3 + c) * ph * pw;
+        a = l[(long long)r0 * pw + c0];
+        b = l[(long long)r0 * pw + c1];
+        cc = l[(long long)r1 * pw + c0];
+        d = l[(long long)r1 * pw + c1];
+      }
+      (img ? oy : ox)[i] = F(0.25) * (((a + b) + cc) + d);
+    }
+  }
+}
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p) {
+  extern __shared__ __align__(16) unsigned char su_smem[];
+  F* xyb = reinterpret_cast<F*>(su_smem);      // [2 images][3 ch][IH][IW]
+  F* hb = xyb + 2 * 3 * SU_IH * SU_IW;         // [4 groups][IH][W]
+  __shared__ double s_red[32];
+  __shared__ double s_sum[SU_SUMS];
+  __shared__ int s_flag;
+  const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
+  const int n = blockIdx.z;
+  const int ox0 = blockIdx.x * SU_W - SU_R, oy0 = blockIdx.y * SU_H - SU_R;
+
+  // XYB of the tile and its halo; zero outside the image (the blur reads 0)
+  for (int i = t; i < SU_IH * SU_IW; i += SU_T) {
+    const int r = i / SU_IW, c = i - r * SU_IW;
+    const int gr = oy0 + r, gc = ox0 + c;
+    F v[2][3] = {{F(0), F(0), F(0)}, {F(0), F(0), F(0)}};
+    if (gr >= 0 && gr < p.h && gc >= 0 && gc < p.w) {
+#pragma unroll
+      for (int img = 0; img < 2; ++img) {
+        const F R = su_linear<T, F>(p, img, n, 0, gr, gc);
+        const F G = su_linear<T, F>(p, img, n, 1, gr, gc);
+        const F B = su_linear<T, F>(p, img, n, 2, gr, gc);
+        to_xyb<F>(p, R, G, B, v[img][0], v[img][1], v[img][2]);
+      }
+    }
+#pragma unroll
+    for (int img = 0; img < 2; ++img)
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) xyb[((img * 3 + ch) * SU_IH + r) * SU_IW + c] = v[img][ch];
+  }
+  __syncthreads();
+
+  const int gy = oy0 + SU_R + ty, gx = ox0 + SU_R + tx;
+  const bool inside = gy < p.h && gx < p.w;
+  double sums[SU_SUMS];
+#pragma unroll
+  for (int k = 0; k < SU_SUMS; ++k) sums[k] = 0.0;
+  for (int ch = 0; ch < 3; ++ch) {
+    const F* a = xyb + (0 * 3 + ch) * SU_IH * SU_IW;
+    const F* b = xyb + (1 * 3 + ch) * SU_IH * SU_IW;
+    // horizontal: the four groups of every tile row at the tile's columns
+    for (int i = t; i < SU_IH * SU_W; i += SU_T) {
+      const int r = i / SU_W, c = i - r * SU_W;
+      F g0 = F(0), g1 = F(0), g2 = F(0), g3 = F(0);
+#pragma unroll
+      for (int j = 0; j < 2 * SU_R + 1; ++j) {
+        const F w = F(p.taps[j]);
+        const F u = a[r * SU_IW + c + j], v = b[r * SU_IW + c + j], d = u - v;
+        g0 += w * u;
+        g1 += w * v;
+        g2 += w * (u * u + v * v);
+        g3 += w * (d * d);
+      }
+      hb[(0 * SU_IH + r) * SU_W + c] = g0;
+      hb[(1 * SU_IH + r) * SU_W + c] = g1;
+      hb[(2 * SU_IH + r) * SU_W + c] = g2;
+      hb[(3 * SU_IH + r) * SU_W + c] = g3;
+    }
+    __syncthreads();
+    if (inside) {
+      F m1 = F(0), m2 = F(0), sp = F(0), sd = F(0);
+#pragma unroll
+      for (int j = 0; j < 2 * SU_R + 1; ++j) {
+        const F w = F(p.taps[j]);
+        m1 += w * hb[(0 * SU_IH + ty + j) * SU_W + tx];
+        m2 += w * hb[(1 * SU_IH + ty + j) * SU_W + tx];
+        sp += w * hb[(2 * SU_IH + ty + j) * SU_W + tx];
+        sd += w * hb[(3 * SU_IH + ty + j) * SU_W + tx];
+      }
+      const F x1 = a[(ty + SU_R) * SU_IW + tx + SU_R], x2 = b[(ty + SU_R) * SU_IW + tx + SU_R];
+      // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
+      // the same value, exactly 0 on an identical pair
+      // (frame_analytics/ssimulacra2.py:_scale_maps)
+      const F q = (m1 - m2) * (m1 - m2);
+      const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
+      const F num_s = (den_s - sd) + q;
+      F d = ((sd - q) + q * num_s) / den_s;
+      d = d > F(0) ? d : F(0);
+      const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
+      const F e = (e2 - e1) / (F(1) + e1);
+      const F art = e > F(0) ? e : F(0), lost = e < F(0) ? -e : F(0);
+      const F v[3] = {d, art, lost};
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const F sq = v[k] * v[k];
+        sums[ch * 6 + 2 * k] += (double)v[k];
+        sums[ch * 6 + 2 * k + 1] += (double)(sq * sq);
+      }
+    }
+    __syncthreads();
+  }
+  // block sums -> this tile's partials
+  const int tiles = p.tiles_x * p.tiles_y;
+  const long long tidx = (long long)n * tiles + blockIdx.y * p.tiles_x + blockIdx.x;
+#pragma unroll 1
+  for (int k = 0; k < SU_SUMS; ++k) {
+    const double s = block_sum(sums[k], s_red);
+    if (t == 0) p.part[tidx * SU_SUMS + k] = s;
+  }
+  if (last_block_arrived(p.counter + p.scale, gridDim.x * gridDim.y * gridDim.z, &s_flag)) {
+    const double npix = (double)p.h * p.w;
+    for (int img = 0; img < p.N; ++img) {
+      if (t < SU_SUMS) {
+        double s = 0.0;
+        for (int i = 0; i < tiles; ++i) s += p.part[((long long)img * tiles + i) * SU_SUMS + t];
+        s_sum[t] = s;
+      }
+      __syncthreads();
+      if (t < SU_SUMS) {
+        const double m = s_sum[t] / npix;
+        // odd slots hold sums of 4th powers: the 4-norm
+        p.norms[((long long)img * SU_SCALES + p.scale) * SU_SUMS + t] = (t & 1) ? sqrt(sqrt(m)) : m;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+struct Su2Score {
+  double w[108];
+  int N, scales;
+  const double* norms;
+  double* out_per_image;
+  double* out_total;
+};
+
+// Msssim::Score order: channel, scale, norm (1, 4), map (SSIM', ringing,
+// blurring); with fewer than six scales the weight index keeps counting.
+__global__ void __launch_bounds__(256) su2_score_kernel(const Su2Score s) {
+  __shared__ double s_red[32];
+  double tot = 0.0;
+  for (int n = threadIdx.x; n < s.N; n += blockDim.x) {
+    double acc = 0.0;
+    int i = 0;
+    for (int c = 0; c < 3; ++c)
+      for (int sc = 0; sc < s.scales; ++sc)
+        for (int nrm = 0; nrm < 2; ++nrm)
+          for (int mp = 0; mp < 3; ++mp) {
+            const double v = s.norms[((long long)n * SU_SCALES + sc) * SU_SUMS + c * 6 + 2 * mp + nrm];
+            acc += s.w[i++] * fabs(v);
+          }
+    double x = acc * 0.9562382616834844;
+    x = 2.326765642916932 * x - 0.020884521182843837 * x * x + 6.248496625763138e-05 * x * x * x;
+    const double score = x > 0.0 ? 100.0 - 10.0 * pow(x, 0.6276336467831387) : 100.0;
+    if (s.out_per_image) s.out_per_image[n] = score;
+    tot += score;
+  }
+  tot = block_sum(tot, s_red);
+  if (threadIdx.x == 0 && s.out_total) *s.out_total = tot / s.N;
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct Su2Plan {
+  int scales;
+  int h[SU_SCALES], w[SU_SCALES];
+  size_t lin_elems;     // per image of the pair, both ping-pong buffers
+  size_t part_elems;    // doubles
+};
+
+static Su2Plan su2_plan(int N, int H, int W) {
+  Su2Plan pl{};
+  int h = H, w = W, ph = H, pw = W;
+  for (int s = 0; s < SU_SCALES; ++s) {
+    if (ph < 8 || pw < 8) break;
+    if (s) {
+      h = (ph + 1) / 2;
+      w = (pw + 1) / 2;
+    }
+    pl.h[s] = h;
+    pl.w[s] = w;
+    pl.scales = s + 1;
+    const size_t tiles = (size_t)((w + SU_W - 1) / SU_W) * ((h + SU_H - 1) / SU_H);
+    pl.part_elems = std::max(pl.part_elems, tiles * N * SU_SUMS);
+    ph = h;
+    pw = w;
+  }
+  // ping-pong linear planes: scale 1 and scale 2 sizes (each later one fits)
+  const size_t s1 = pl.scales > 1 ? (size_t)N * 3 * pl.h[1] * pl.w[1] : 0;
+  const size_t s2 = pl.scales > 2 ? (size_t)N * 3 * pl.h[2] * pl.w[2] : 0;
+  pl.lin_elems = s1 + s2;
+  return pl;
+}
+
+size_t su2_ws_bytes(int N, int H, int W, int fsize) {
+  const Su2Plan pl = su2_plan(N, H, W);
+  const size_t lin = 2 * pl.lin_elems * fsize;  // x and y
+  const size_t a = (lin + 255) / 256 * 256;
+  return FAB_COUNTER_BYTES + a + sizeof(double) * (pl.part_elems + (size_t)N * SU_SCALES * SU_SUMS);
+}
+
+static void su2_taps(double* out) {
+  // the FIR of libjxl's recursive Gaussian at sigma 1.5 (Charalampidis 2016):
+  // three truncated cosines of radius 5 with the paper's normalised weights
+  const double sigma = 1.5;
+  const int n = SU_R;
+  const double pi = 3.14159265358979323846;
+  double w[3], pp[3], r[3], rho[3];
+  for (int k = 0; k < 3; ++k) {
+    w[k] = (2 * k + 1) * pi / (2.0 * n);
+    const double sg = (k == 1) ? -1.0 : 1.0;
+    pp[k] = sg / tan(0.5 * w[k]);
+    r[k] = sg * pp[k] * pp[k] / sin(w[k]);
+    rho[k] = exp(-0.5 * sigma * sigma * w[k] * w[k]) / n;
+  }
+  const double d13 = pp[0] * r[1] - r[0] * pp[1];
+  const double z15 = (pp[1] * r[2] - r[1] * pp[2]) / d13;
+  const double z35 = (pp[2] * r[0] - r[2] * pp[0]) / d13;
+  const double A[3][3] = {{pp[0], pp[1], pp[2]}, {r[0], r[1], r[2]}, {z15, z35, 1.0}};
+  const double g[3] = {1.0, n * n - sigma * sigma, z15 * rho[0] + z35 * rho[1] + rho[2]};
+  auto det = [](const double m[3][3]) {
+    return m[0][0] * (m[1][1] * m[2][2] - m[1][2] * m[2][1]) -
+           m[0][1] * (m[1][0] * m[2][2] - m[1][2] * m[2][0]) +
+           m[0][2] * (m[1][0] * m[2][1] - m[1][1] * m[2][0]);
+  };
+  const double D = det(A);
+  double beta[3];
+  for (int col = 0; col < 3; ++col) {
+    double M[3][3];
+    for (int i = 0; i < 3; ++i)
+      for (int j = 0; j < 3; ++j) M[i][j] = (j == col) ? g[i] : A[i][j];
+    beta[col] = det(M) / D;
+  }
+  for (int t = -n; t <= n; ++t) {
+    double v = 0.0;
+    for (int k = 0; k < 3; ++k) v += beta[k] * cos(w[k] * t);
+    out[t + n] = v;
+  }
+}
+
+template <typename T, typename F>
+static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, const Su2Score& sc_in, int device,
+                   cudaStream_t st) {
+  static bool done[64] = {false};
+  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);
+  FAB_TRY(ensure_smem(su2_scale_kernel<T, F>, smem, device, done));
+  const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
+  F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
+  const long long cap = (long long)sm_count(device) * 8;
+  for (int s = 0; s < pl.scales; ++s) {
+    p.scale = s;
+    p.h = pl.h[s];
+    p.w = pl.w[s];
+    if (s > 0) {
+      F* out = buf[(s - 1) & 1];
+      const size_t plane = (size_t)p.N * 3 * pl.h[s] * pl.w[s];
+      const long long n_out = (long long)plane;
+      const unsigned blocks = (unsigned)std::min<long long>((n_out + 255) / 256, cap);
+      if (s == 1) {
+        su2_down_kernel<T, F, true><<<blocks, 256, 0, st>>>(p, pl.h[0], pl.w[0], out, out + plane);
+      } else {
+        su2_down_kernel<T, F, false><<<blocks, 256, 0, st>>>(p, pl.h[s - 1], pl.w[s - 1], out,
+                                                             out + plane);
+      }
+      FAB_LAUNCH_CHECK();
+      p.lx = out;
+      p.ly = out + plane;
+    }
+    p.tiles_x = (p.w + SU_W - 1) / SU_W;
+    p.tiles_y = (p.h + SU_H - 1) / SU_H;
+    dim3 grid(p.tiles_x, p.tiles_y, p.N);
+    su2_scale_kernel<T, F><<<grid, SU_T, smem, st>>>(p);
+    FAB_LAUNCH_CHECK();
+  }
+  Su2Score sc = sc_in;
+  sc.scales = pl.scales;
+  su2_score_kernel<<<1, 256, 0, st>>>(sc);
+  FAB_LAUNCH_CHECK();
+  return FA_OK;
+}
+
+// x, y: (N, 3, H, W) views (channel stride 0 for a replicated gray plane).
+int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64,
+             const double* weights, void* ws, size_t ws_bytes, double* out_per_image,
+             double* out_total, int device, cudaStream_t st) {
+  if (!x.data || !y.data || !ws || !weights) return FA_E_ARG;
+  if (x.n != y.n || x.c != y.c || x.h != y.h || x.w != y.w) return FA_E_SHAPE;
+  if (x.sn != y.sn || x.sc != y.sc || x.sh != y.sh) return FA_E_SHAPE;
+  if (x.c != 3 || x.h < 8 || x.w < 8 || x.n <= 0 || x.n > 65535) return FA_E_SHAPE;
+  if (!(data_range > 0.0)) return FA_E_ARG;
+  const int fsize = f64 ? 8 : 4;
+  if (ws_bytes < su2_ws_bytes(x.n, x.h, x.w, fsize)) return FA_E_ARG;
+  const Su2Plan pl = su2_plan(x.n, x.h, x.w);
+  Su2Args p{};
+  p.x = static_cast<const char*>(x.data);
+  p.y = static_cast<const char*>(y.data);
+  p.dtype = dtype;
+  p.sn = x.sn; p.sc = x.sc; p.sh = x.sh;
+  p.inv_range = 1.0 / data_range;
+  p.N = x.n;
+  su2_taps(p.taps);
+  const double M[9] = {0.30, 1.0 - 0.078 - 0.30, 0.078,
+                       0.23, 1.0 - 0.078 - 0.23, 0.078,
+                       0.24342268924547819, 0.20476744424496821,
+                       1.0 - 0.24342268924547819 - 0.20476744424496821};
+  for (int i = 0; i < 9; ++i) p.mat[i] = M[i];
+  p.bias = 0.0037930732552754493;
+  p.cbrt_bias = cbrt(p.bias);
+  char* base = static_cast<char*>(ws);
+  p.counter = reinterpret_cast<unsigned int*>(base);
+  const size_t lin_bytes = (2 * pl.lin_elems * fsize + 255) / 256 * 256;
+  char* lin = base + FAB_COUNTER_BYTES;
+  p.part = reinterpret_cast<double*>(lin + lin_bytes);
+  p.norms = p.part + pl.part_elems;
+  Su2Score sc{};
+  for (int i = 0; i < 108; ++i) sc.w[i] = weights[i];
+  sc.N = x.n;
+  sc.norms = p.norms;
+  sc.out_per_image = out_per_image;
+  sc.out_total = out_total;
+#define FAB_SU2(TT)                                                                        \
+  return f64 ? su2_run<TT, double>(p, pl, reinterpret_cast<double*>(lin), sc, device, st) \
+             : su2_run<TT, float>(p, pl, reinterpret_cast<float*>(lin), sc, device, st)
+  switch (dtype) {
+    case FA_U8: FAB_SU2(unsigned char);
+    case FA_F16: FAB_SU2(f16_t);
+    case FA_BF16: FAB_SU2(bf16_t);
+    case FA_F32: FAB_SU2(float);
+    case FA_F64: FAB_SU2(double);
+    case FA_U16: FAB_SU2(unsigned short);
+    default: return FA_E_DTYPE;
+  }
+#undef FAB_SU2
+}
+
+}  // namespace fab

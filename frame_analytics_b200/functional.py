@@ -529,7 +529,8 @@ def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: Optional[float] = None
 # several metrics of one frame pair
 # --------------------------------------------------------------------------- #
 
-METRIC_NAMES = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber")
+METRIC_NAMES = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber",
+                "ssimulacra2")
 
 
 def metrics(x: torch.Tensor, y: torch.Tensor, names: Sequence[str] = ("mse", "psnr", "ssim"),
@@ -600,11 +601,17 @@ def metrics(x: torch.Tensor, y: torch.Tensor, names: Sequence[str] = ("mse", "ps
         "l1": lambda: l1(x4, y4, reduction=reduction),
         "charbonnier": lambda: charbonnier(x4, y4, reduction=reduction),
         "huber": lambda: huber(x4, y4, reduction=reduction),
+        "ssimulacra2": lambda: _ssimulacra2()(x4, y4, reduction=reduction, **kw_range),
     }
     for n in names:
         if n not in out:
             out[n] = table[n]()
     return out
+
+
+def _ssimulacra2():
+    from .ssimulacra2 import ssimulacra2
+    return ssimulacra2
 
 
 # --------------------------------------------------------------------------- #

@@ -192,11 +192,12 @@ class StreamingMetrics:
 
     ``metrics`` defaults to ``("mse", "psnr", "ssim")``, which
     :func:`frame_analytics_b200.metrics` computes in a single launch and one
-    read of the pair.  The reference's ``lpips`` and ``ssimulacra2`` are
-    outside this package and raise ``NotImplementedError``."""
+    read of the pair.  The reference's ``lpips`` is outside this package and
+    raises ``NotImplementedError``."""
 
-    _KNOWN = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber")
-    _ELSEWHERE = ("lpips", "ssimulacra2")
+    _KNOWN = ("mse", "psnr", "ssim", "ms_ssim", "gmsd", "gms", "l1", "charbonnier", "huber",
+              "ssimulacra2")
+    _ELSEWHERE = ("lpips",)
 
     def __init__(self, shape, device="cuda", dtype=torch.uint8,
                  data_range: Optional[float] = None, metrics=("mse", "psnr", "ssim"),

@@ -57,12 +57,13 @@ FEATURES: Tuple[Feature, ...] = (
     Feature(8, "l1", "per_plane", "l1", takes_range=False),
     Feature(9, "charbonnier", "per_plane", "charbonnier", takes_range=False),
     Feature(10, "huber", "per_plane", "huber", takes_range=False),
+    Feature(12, "ssimulacra2", "rgb", "ssimulacra2"),
 )
 _NAMED = {f.name: f for f in FEATURES}
 _NUMBERED = {f.id: f for f in FEATURES}
 # features of the reference this package does not compute, with why
 _ABSENT = {1: "psnr_hvs (a libvmaf feature)", 4: "ciede2000 (a libvmaf feature)",
-           11: "lpips (not part of this package)", 12: "ssimulacra2 (not part of this package)"}
+           11: "lpips (not part of this package)"}
 _SUFFIXES = {"gray": ("_y",), "yuv": ("_y", "_cb", "_cr"), "rgb": ("_r", "_g", "_b")}
 
 
@@ -85,8 +86,8 @@ def resolve_features(feature) -> List[Feature]:
     for item in feature:
         if isinstance(item, str):
             key = item.strip().lower().replace("-", "_")
-            if key in ("lpips", "ssimulacra2"):
-                raise ValueError(f"feature {item!r}: {_ABSENT[11 if key == 'lpips' else 12]}")
+            if key == "lpips":
+                raise ValueError(f"feature {item!r}: {_ABSENT[11]}")
             if key not in _NAMED:
                 raise ValueError(f"unknown feature {item!r}; expected one of {sorted(_NAMED)}")
             f = _NAMED[key]
@@ -147,7 +148,8 @@ def frame_planes(buf: torch.Tensor, width: int, height: int,
 
 _PER_PLANE = {"psnr": F.psnr, "mse": F.mse, "l1": F.l1, "charbonnier": F.charbonnier,
               "huber": F.huber}
-_IMAGE = {"ssim": F.ssim, "ms_ssim": F.ms_ssim, "gmsd": F.gmsd, "gms": F.gms}
+_IMAGE = {"ssim": F.ssim, "ms_ssim": F.ms_ssim, "gmsd": F.gmsd, "gms": F.gms,
+          "ssimulacra2": F._ssimulacra2()}
 
 
 class PlaneScorer:
@@ -217,7 +219,7 @@ class PlaneScorer:
                 x, y = ref[i], dist[i]
                 for f in per:
                     out[f.prop + sfx] = float(_PER_PLANE[f.name](x, y, **self._kw(f, L)))
-            image = [f for f in self.features if f.kind == "image"]
+            image = [f for f in self.features if f.kind in ("image", "rgb")]
             if image:
                 if self.family == "rgb":
                     x = torch.cat([F._as_nchw(p) for p in ref], 1)

@@ -516,6 +516,22 @@ FA_B200_API int fa_b200_gmsd64_backward(const double* x, const double* y, int N,
                                         double* coef, double* dx, double* dy, int device,
                                         void* stream);
 
+/* SSIMULACRA 2 (replaces the reference's torch pipeline frame_analytics/
+ * ssimulacra2.py:465-590, whose float64 transcription is reference.py:
+ * 540-700).  x (original) and y (distorted): (N, 3, H, W) sRGB in
+ * [0, data_range], any dtype and strides (stride_c = 0 replicates a gray
+ * plane), H, W >= 8.  f64 = 0 computes colour, blur and maps in float (the
+ * reference's default), 1 in double; sums are double either way.  weights:
+ * the 108 Msssim::Score weights in HOST memory.  Outputs: per-image score [N]
+ * and batch mean (nullable).  The workspace (size from the query; holds the
+ * pyramid's linear planes) needs no zeroing. */
+FA_B200_API int fa_b200_ssimulacra2_workspace_bytes(int n, int h, int w, int f64,
+                                                    size_t* out_bytes);
+FA_B200_API int fa_b200_ssimulacra2(const fa_view* x, const fa_view* y, double data_range,
+                                    int f64, const double* weights, void* workspace,
+                                    size_t workspace_bytes, double* out_per_image,
+                                    double* out_total, int device, void* stream);
+
 /* No counterpart in the reference: test hook of the bounded device-side
  * waits.  Launches one thread that waits `limit_ns` (at most 1 s) for an
  * mbarrier phase that nothing completes and then records FA_E_TIMEOUT the

@@ -289,3 +289,128 @@ def gmsd(x, y, data_range=255.0, T=None, downsample=True, eps=None,
     q = gms_map(x, y, data_range, T, downsample, eps, luma, crop_border)
     f = q.reshape(q.shape[0], -1)
     return f.mean(axis=1), f.std(axis=1)
+
+
+# --------------------------------------------------------------------------- #
+# SSIMULACRA 2 (reference.py:540-700, the float64 transcription of libjxl's
+# tools/ssimulacra2.cc; frame_analytics/ssimulacra2.py for the conventions)
+# --------------------------------------------------------------------------- #
+
+# Msssim::Score weights: channel-major, then scale, then norm (1, 4), then the
+# three maps (SSIM', ringing, blurring).  A published constant of the metric.
+SSIMULACRA2_WEIGHTS = (
+    0.0, 0.0007376606707406586, 0.0, 0.0, 0.0007793481682867309, 0.0,
+    0.0, 0.0004371155730107379, 0.0, 1.1041726426657346, 0.00066284834129271, 0.00015231632783718752,
+    0.0, 0.0016406437456599754, 0.0, 1.8422455520539298, 11.441172603757666, 0.0,
+    0.0007989109436015163, 0.000176816438078653, 0.0, 1.8787594979546387, 10.94906990605142, 0.0,
+    0.0007289346991508072, 0.9677937080626833, 0.0, 0.00014003424285435884, 0.9981766977854967, 0.00031949755934435053,
+    0.0004550992113792063, 0.0, 0.0, 0.0013648766163243398, 0.0, 0.0,
+    0.0, 0.0, 0.0, 7.466890328078848, 0.0, 17.445833984131262,
+    0.0006235601634041466, 0.0, 0.0, 6.683678146179332, 0.00037724407979611296, 1.027889937768264,
+    225.20515300849274, 0.0, 0.0, 19.213238186143016, 0.0011401524586618361, 0.001237755635509985,
+    176.39317598450694, 0.0, 0.0, 24.43300999870476, 0.28520802612117757, 0.0004485436923833408,
+    0.0, 0.0, 0.0, 34.77906344483772, 44.835625328877896, 0.0,
+    0.0, 0.0, 0.0, 0.0, 0.0, 0.0,
+    0.0, 0.0008680556573291698, 0.0, 0.0, 0.0, 0.0,
+    0.0, 0.0005313191874358747, 0.0, 0.00016533814161379112, 0.0, 0.0,
+    0.0, 0.0, 0.0, 0.0004179171803251336, 0.0017290828234722833, 0.0,
+    0.0020827005846636437, 0.0, 0.0, 8.826982764996862, 23.19243343998926, 0.0,
+    95.1080498811086, 0.9863978034400682, 0.9834382792465353, 0.0012286405048278493, 171.2667255897307, 0.9807858872435379,
+    0.0, 0.0, 0.0, 0.0005130064588990679, 0.0, 0.00010854057858411537,
+)
+_S2_OPSIN = np.array([[0.30, 1.0 - 0.078 - 0.30, 0.078],
+                      [0.23, 1.0 - 0.078 - 0.23, 0.078],
+                      [0.24342268924547819, 0.20476744424496821,
+                       1.0 - 0.24342268924547819 - 0.20476744424496821]])
+_S2_BIAS = 0.0037930732552754493
+_S2_C2 = 0.0009
+
+
+def recursive_gaussian_taps(sigma: float = 1.5) -> np.ndarray:
+    """The FIR equivalent of the truncated-cosine recursive Gaussian of
+    Charalampidis (2016), the blur libjxl's SSIMULACRA 2 uses: three cosines
+    cos(w_k t), w_k = (2k+1) pi / (2N), N = round(3.2795 sigma + 0.2546),
+    weighted by the beta that solves the paper's normalisation, first-moment
+    and Gaussian-fit conditions (eqs. 37-56); 2N + 1 taps, the outer two 0."""
+    n = int(round(3.2795 * sigma + 0.2546))
+    w = np.array([1.0, 3.0, 5.0]) * np.pi / (2.0 * n)
+    p = np.array([1.0, -1.0, 1.0]) / np.tan(0.5 * w)
+    r = np.array([1.0, -1.0, 1.0]) * p * p / np.sin(w)
+    rho = np.exp(-0.5 * sigma * sigma * w * w) / n
+    d13 = p[0] * r[1] - r[0] * p[1]
+    z15 = (p[1] * r[2] - r[1] * p[2]) / d13
+    z35 = (p[2] * r[0] - r[2] * p[0]) / d13
+    beta = np.linalg.solve(np.array([p, r, [z15, z35, 1.0]]),
+                           np.array([1.0, n * n - sigma * sigma,
+                                     z15 * rho[0] + z35 * rho[1] + rho[2]]))
+    t = np.arange(-n, n + 1, dtype=np.float64)
+    return (beta[:, None] * np.cos(w[:, None] * t[None, :])).sum(axis=0)
+
+
+def _s2_blur(img: np.ndarray, taps: np.ndarray) -> np.ndarray:
+    """Separable same-size blur of (..., H, W) planes, zero outside."""
+    k = len(taps) // 2
+    out = np.zeros_like(img)
+    pad = np.pad(img, [(0, 0)] * (img.ndim - 1) + [(k, k)])
+    for j, w in enumerate(taps):
+        out += w * pad[..., j:j + img.shape[-1]]
+    pad = np.pad(out, [(0, 0)] * (img.ndim - 2) + [(k, k), (0, 0)])
+    out2 = np.zeros_like(img)
+    for j, w in enumerate(taps):
+        out2 += w * pad[..., j:j + img.shape[-2], :]
+    return out2
+
+
+def _s2_linear(v: np.ndarray) -> np.ndarray:
+    return np.where(v <= 0.04045, v / 12.92, ((v + 0.055) / 1.055) ** 2.4)
+
+
+def _s2_xyb(lin: np.ndarray) -> np.ndarray:
+    """(3, H, W) linear sRGB -> positive XYB."""
+    m = np.einsum("ji,ihw->jhw", _S2_OPSIN, lin) + _S2_BIAS
+    m = np.cbrt(np.maximum(m, 0.0)) - np.cbrt(_S2_BIAS)
+    x, y = 0.5 * (m[0] - m[1]), 0.5 * (m[0] + m[1])
+    return np.stack([14.0 * x + 0.42, y + 0.01, (m[2] - y) + 0.55])
+
+
+def _s2_down(img: np.ndarray) -> np.ndarray:
+    """2x2 box mean, an odd last row / column averaged with itself."""
+    c, h, w = img.shape
+    p = np.pad(img, [(0, 0), (0, h % 2), (0, w % 2)], mode="edge")
+    return 0.25 * (p[:, 0::2, 0::2] + p[:, 1::2, 0::2] + p[:, 0::2, 1::2] + p[:, 1::2, 1::2])
+
+
+def ssimulacra2(x: np.ndarray, y: np.ndarray, data_range: float = 255.0) -> float:
+    """SSIMULACRA 2 of one (3, H, W) sRGB pair (original x, distorted y)."""
+    taps = recursive_gaussian_taps(1.5)
+    l1 = _s2_linear(np.asarray(x, np.float64) / data_range)
+    l2 = _s2_linear(np.asarray(y, np.float64) / data_range)
+    norms = []
+    prev = l1.shape[1:]
+    for scale in range(6):
+        if min(prev) < 8:
+            break
+        if scale:
+            l1, l2 = _s2_down(l1), _s2_down(l2)
+        a, b = _s2_xyb(l1), _s2_xyb(l2)
+        mu1, mu2 = _s2_blur(a, taps), _s2_blur(b, taps)
+        s11, s22, s12 = _s2_blur(a * a, taps), _s2_blur(b * b, taps), _s2_blur(a * b, taps)
+        num_m = 1.0 - (mu1 - mu2) ** 2
+        num_s = 2.0 * (s12 - mu1 * mu2) + _S2_C2
+        den_s = (s11 - mu1 * mu1) + (s22 - mu2 * mu2) + _S2_C2
+        d = np.maximum(1.0 - num_m * num_s / den_s, 0.0)
+        e = (1.0 + np.abs(b - mu2)) / (1.0 + np.abs(a - mu1)) - 1.0
+        maps = (d, np.maximum(e, 0.0), np.maximum(-e, 0.0))
+        norms.append([(m.mean(axis=(1, 2)), np.sqrt(np.sqrt((m ** 4).mean(axis=(1, 2)))))
+                      for m in maps])
+        prev = l1.shape[1:]
+    total, i = 0.0, 0
+    for c in range(3):
+        for sc in norms:
+            for nrm in range(2):
+                for mp in range(3):
+                    total += SSIMULACRA2_WEIGHTS[i] * abs(sc[mp][nrm][c])
+                    i += 1
+    s = total * 0.9562382616834844
+    s = 2.326765642916932 * s - 0.020884521182843837 * s * s + 6.248496625763138e-05 * s ** 3
+    return 100.0 if s <= 0.0 else 100.0 - 10.0 * s ** 0.6276336467831387

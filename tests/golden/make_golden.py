@@ -29,8 +29,9 @@ REPO = HERE.parents[1]
 
 def _reference_path() -> Path:
     """argv[1], else $FA_REFERENCE, else BASELINE.json's reference_path."""
-    if len(sys.argv) > 1:
-        return Path(sys.argv[1])
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    if args:
+        return Path(args[0])
     if os.environ.get("FA_REFERENCE"):
         return Path(os.environ["FA_REFERENCE"])
     return Path(json.loads((REPO / "BASELINE.json").read_text())["reference_path"])
@@ -209,5 +210,55 @@ def main():
     print(f"wrote {HERE / 'golden.npz'}: {len(out)} arrays")
 
 
+def _smooth_rgb(h, w, noise, seed):
+    """A smooth colour image and a noisy copy (uint8 values), the kind of pair
+    SSIMULACRA 2 is tuned on."""
+    rng = np.random.default_rng(seed)
+    yy, xx = np.mgrid[0:h, 0:w].astype(np.float64)
+    base = 120 + 55 * np.sin(xx / 8.0) * np.cos(yy / 6.0)
+    a = np.stack([np.clip(base + 25 * np.sin(xx / 21.0), 0, 255),
+                  np.clip(0.75 * base + 45, 0, 255),
+                  np.clip(1.1 * base - 12 + 18 * np.cos(yy / 15.0), 0, 255)]).round()
+    b = np.clip(a + noise * rng.standard_normal(a.shape), 0, 255).round()
+    return a.astype(np.uint8), b.astype(np.uint8)
+
+
+def ssimulacra2_fixtures():
+    """tests/golden/ssimulacra2.npz: pairs scored by the reference's float64
+    transcription of libjxl (reference.ssimulacra2_reference, which runs the
+    recursive Gaussian itself) and by its torch path (frame_analytics.
+    ssimulacra2 on the CPU, float32 and float64)."""
+    import torch
+    import frame_analytics as ref_s2
+    cases = {
+        "s0": _smooth_rgb(64, 72, 6.0, 11),
+        "s1": _smooth_rgb(100, 60, 20.0, 2),    # five scales
+        "s2": _smooth_rgb(37, 45, 3.0, 5),      # odd sizes, three scales
+        "s3": _smooth_rgb(8, 9, 10.0, 7),       # the 8x8 floor
+    }
+    rng = np.random.default_rng(4)
+    a = rng.integers(0, 256, (3, 96, 128)).astype(np.uint8)
+    cases["r0"] = (a, np.clip(a + np.round(rng.normal(0, 8, a.shape)), 0, 255).astype(np.uint8))
+    g, gb = _smooth_rgb(48, 56, 8.0, 9)
+    cases["g0"] = (g[:1], gb[:1])               # grayscale, replicated to RGB
+    out = {}
+    for k, (x, y) in cases.items():
+        out[f"{k}_a"], out[f"{k}_b"] = x, y
+        x3 = np.repeat(x, 3, axis=0) if x.shape[0] == 1 else x
+        y3 = np.repeat(y, 3, axis=0) if y.shape[0] == 1 else y
+        out[f"{k}_ref64"] = ref.ssimulacra2_reference(x3.astype(np.float64),
+                                                     y3.astype(np.float64), 255.0)
+        tx, ty = torch.from_numpy(x), torch.from_numpy(y)
+        out[f"{k}_torch32"] = float(ref_s2.ssimulacra2(tx, ty, data_range=255.0))
+        out[f"{k}_torch64"] = float(ref_s2.ssimulacra2(tx, ty, data_range=255.0,
+                                                       dtype=torch.float64))
+    np.savez_compressed(HERE / "ssimulacra2.npz", **out)
+    print(f"wrote {HERE / 'ssimulacra2.npz'}: {len(out)} arrays")
+
+
 if __name__ == "__main__":
-    main()
+    if "--ssimulacra2" in sys.argv:
+        sys.argv.remove("--ssimulacra2")
+        ssimulacra2_fixtures()
+    else:
+        main()

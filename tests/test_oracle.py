@@ -8,6 +8,9 @@ import numpy as np
 import pytest
 
 import fa_oracle as O
+from conftest import REPO
+
+GOLDEN_DIR = REPO / "tests" / "golden"
 
 V = ["v0", "v1", "v2", "v3"]
 M = ["m0", "m1", "m2"]
@@ -111,3 +114,24 @@ def test_matlab_downsample_pinned(golden, f):
     x = golden["mdown_x"].astype(np.float64)
     # the reference computes in float32: relative agreement to a few float32 ulp
     np.testing.assert_allclose(O.matlab_downsample(x, f), golden[f"mdown_f{f}"], rtol=1e-6, atol=0)
+
+
+S2 = ["s0", "s1", "s2", "s3", "r0", "g0"]
+
+
+@pytest.mark.parametrize("k", S2)
+def test_ssimulacra2_oracle_matches_the_reference(k):
+    """tests/golden/ssimulacra2.npz holds scores of the reference's float64
+    transcription of libjxl (recursive Gaussian run as a recursion); the
+    oracle convolves the FIR taps instead and must agree to float64 noise."""
+    d = np.load(GOLDEN_DIR / "ssimulacra2.npz")
+    a, b = d[f"{k}_a"], d[f"{k}_b"]
+    if a.shape[0] == 1:
+        a, b = np.repeat(a, 3, axis=0), np.repeat(b, 3, axis=0)
+    assert abs(O.ssimulacra2(a, b, 255.0) - float(d[f"{k}_ref64"])) < 1e-8
+    assert abs(float(d[f"{k}_torch64"]) - float(d[f"{k}_ref64"])) < 1e-8
+
+
+def test_ssimulacra2_taps_sum_to_one():
+    t = O.recursive_gaussian_taps(1.5)
+    assert len(t) == 11 and abs(t.sum() - 1.0) < 1e-12 and abs(t[0]) < 1e-15
