@@ -320,7 +320,21 @@ def run_only(args):
 
     ua, ub = u8_pair((args.images,) + PIX_SHAPE[1:], 5.0, 0)
     xu, yu = torch.from_numpy(ua).cuda(), torch.from_numpy(ub).cuda()
-    fn = {"psnr": fa.psnr, "ssim_u8": fa.ssim, "gmsd_u8": fa.gmsd}[args.only]
+    if args.only == "ssim_loss":
+        # the headline step (config 2's fused SSIM value + gradient) on
+        # args.images fp32 frames
+        g = torch.Generator().manual_seed(0)
+        a = torch.rand((args.images,) + SHAPE[1:], generator=g).cuda()
+        b = (a + 0.05 * torch.randn(a.shape, generator=g).cuda()).clamp_(0, 1)
+
+        def fn(x, y):
+            yy = b.requires_grad_(True)
+            torch.autograd.grad(1.0 - fa.ssim(a, yy, data_range=1.0), yy)
+    elif args.only == "ssimulacra2":
+        def fn(x, y):
+            return fa.ssimulacra2(x, y, data_range=255.0)
+    else:
+        fn = {"psnr": fa.psnr, "ssim_u8": fa.ssim, "gmsd_u8": fa.gmsd}[args.only]
     for _ in range(args.warmup + args.steps):
         fn(xu, yu)
     torch.cuda.synchronize()
@@ -751,6 +765,15 @@ def run_ours(args):
             "workload": "MSE loss fwd+bwd, fp32 8x3x1080x1920, grad w.r.t. b",
             "fused_ms": mse_t[True], "two_pass_ms": mse_t[False],
             "fused_GB/s": 12 * px_step / (mse_t[True] / 1e3) / 1e9}
+        # SSIMULACRA 2 of the config-1 frames (uint8 sRGB, 6 scales), float32 pipeline
+        for _ in range(2):
+            fa.ssimulacra2(xu, yu, data_range=255.0)
+        s2m = timed_stream(lambda: fa.ssimulacra2(xu, yu, data_range=255.0), ev, flush,
+                           reps=max(5, args.steps // 4))
+        extra["ssimulacra2_u8"] = {"workload": "SSIMULACRA 2 uint8 8x3x1080x1920 (6 scales, float32 "
+                                               "pipeline), L2 flushed by a 256 MB read",
+                                   "ms": s2m,
+                                   "Gpixel/s": int(np.prod(PIX_SHAPE)) / (s2m / 1e3) / 1e9}
         # config 3: MS-SSIM forward, 5 scales, uint8 input read in place
         ca, cb = u8_pair(PIX_SHAPE, 8.0, 0)
         xm, ym = torch.from_numpy(ca).to(dev), torch.from_numpy(cb).to(dev)
@@ -826,7 +849,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--only", choices=["psnr", "ssim_u8", "gmsd_u8"], default=None,
+    ap.add_argument("--only", choices=["psnr", "ssim_u8", "gmsd_u8", "ssim_loss", "ssimulacra2"],
+                    default=None,
                     help="profiling mode: only this uint8 kernel (config-1 frames)")
     ap.add_argument("--no-extra", action="store_true",
                     help="time only the headline step (profiling runs)")
