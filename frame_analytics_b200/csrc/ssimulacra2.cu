@@ -18,12 +18,15 @@
 // Kernels (compute type F = float, the reference's default, or double):
 //   su2_down_kernel    the next scale's linear planes (from the input at
 //                      scale 1, from the previous linear planes after that)
-//   su2_scale_kernel   one block per 32 x 8 tile of one image: the tile plus a
-//                      5-pixel halo of both images is converted to XYB in
-//                      shared memory, the four groups are blurred separably
-//                      per channel, the maps are formed and the 18 per-channel
-//                      sums reduced; the last block of the launch turns each
-//                      image's sums into its 18 norms
+//   su2_xyb_kernel     both images' positive XYB planes of this scale, each
+//                      pixel converted once (scale 0 straight from the input)
+//   su2_scale_kernel   a few hundred blocks per image walk its 32 x 32 tiles:
+//                      the tile plus a 5-pixel halo of both images' XYB is
+//                      staged in shared memory (zero outside), the four groups
+//                      are blurred separably per channel, the maps are formed
+//                      and the 18 per-channel sums kept in registers; the last
+//                      block of the launch turns each image's sums into its
+//                      18 norms, one warp per (image, sum)
 //   su2_score_kernel   the weighted sum and the final mapping, per image and
 //                      for the batch
 // Every sum is double.
@@ -33,8 +36,9 @@
 
 namespace fab {
 
-constexpr int SU_W = 32, SU_H = 8, SU_R = 5;  // tile, blur radius
-constexpr int SU_T = SU_W * SU_H;
+constexpr int SU_W = 32, SU_H = 32, SU_R = 5;  // tile, blur radius
+constexpr int SU_BPI = 148 * 3;  // scale-kernel blocks per image at most
+constexpr int SU_T = 256;
 constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
 constexpr int SU_SCALES = 6;
 constexpr int SU_SUMS = 18;  // 3 channels x {d, d^4, art, art^4, lost, lost^4}
@@ -140,121 +144,146 @@ __global__ void __launch_bounds__(256) su2_down_kernel(const Su2Args p, int ph, 
   }
 }
 
+// Positive XYB planes of both images at this scale: [2][N][3][h][w].
 template <typename T, typename F>
-__global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p) {
+__global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
+  const long long plane = (long long)p.h * p.w;
+  const long long npx = (long long)p.N * plane;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < npx; i += 256LL * gridDim.x) {
+    const int n = (int)(i / plane);
+    const long long o = i - (long long)n * plane;
+    const int r = (int)(o / p.w), col = (int)(o - (long long)r * p.w);
+#pragma unroll
+    for (int img = 0; img < 2; ++img) {
+      const F R = su_linear<T, F>(p, img, n, 0, r, col);
+      const F G = su_linear<T, F>(p, img, n, 1, r, col);
+      const F B = su_linear<T, F>(p, img, n, 2, r, col);
+      F X, Y, Bc;
+      to_xyb<F>(p, R, G, B, X, Y, Bc);
+      F* out = xyb + ((long long)img * p.N + n) * 3 * plane + o;
+      out[0] = X;
+      out[plane] = Y;
+      out[2 * plane] = Bc;
+    }
+  }
+}
+
+// One block per (strip of tiles, image): the block walks its image's 32 x 32
+// tiles with a stride, keeping the 18 per-channel sums in registers; each
+// thread computes four output rows of a tile.
+template <typename F>
+__global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const F* xyb) {
   extern __shared__ __align__(16) unsigned char su_smem[];
-  F* xyb = reinterpret_cast<F*>(su_smem);      // [2 images][3 ch][IH][IW]
-  F* hb = xyb + 2 * 3 * SU_IH * SU_IW;         // [4 groups][IH][W]
+  F* tile = reinterpret_cast<F*>(su_smem);      // [2 images][3 ch][IH][IW]
+  F* hb = tile + 2 * 3 * SU_IH * SU_IW;         // [4 groups][IH][W]
   __shared__ double s_red[32];
-  __shared__ double s_sum[SU_SUMS];
   __shared__ int s_flag;
   const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
-  const int n = blockIdx.z;
-  const int ox0 = blockIdx.x * SU_W - SU_R, oy0 = blockIdx.y * SU_H - SU_R;
-
-  // XYB of the tile and its halo; zero outside the image (the blur reads 0)
-  for (int i = t; i < SU_IH * SU_IW; i += SU_T) {
-    const int r = i / SU_IW, c = i - r * SU_IW;
-    const int gr = oy0 + r, gc = ox0 + c;
-    F v[2][3] = {{F(0), F(0), F(0)}, {F(0), F(0), F(0)}};
-    if (gr >= 0 && gr < p.h && gc >= 0 && gc < p.w) {
-#pragma unroll
-      for (int img = 0; img < 2; ++img) {
-        const F R = su_linear<T, F>(p, img, n, 0, gr, gc);
-        const F G = su_linear<T, F>(p, img, n, 1, gr, gc);
-        const F B = su_linear<T, F>(p, img, n, 2, gr, gc);
-        to_xyb<F>(p, R, G, B, v[img][0], v[img][1], v[img][2]);
-      }
-    }
-#pragma unroll
-    for (int img = 0; img < 2; ++img)
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) xyb[((img * 3 + ch) * SU_IH + r) * SU_IW + c] = v[img][ch];
-  }
-  __syncthreads();
-
-  const int gy = oy0 + SU_R + ty, gx = ox0 + SU_R + tx;
-  const bool inside = gy < p.h && gx < p.w;
+  const int n = blockIdx.y;
+  const long long plane = (long long)p.h * p.w;
+  const F* xa = xyb + (long long)n * 3 * plane;                    // image x
+  const F* xb = xyb + ((long long)p.N + n) * 3 * plane;            // image y
+  const int tiles = p.tiles_x * p.tiles_y;
   double sums[SU_SUMS];
 #pragma unroll
   for (int k = 0; k < SU_SUMS; ++k) sums[k] = 0.0;
-  for (int ch = 0; ch < 3; ++ch) {
-    const F* a = xyb + (0 * 3 + ch) * SU_IH * SU_IW;
-    const F* b = xyb + (1 * 3 + ch) * SU_IH * SU_IW;
-    // horizontal: the four groups of every tile row at the tile's columns
-    for (int i = t; i < SU_IH * SU_W; i += SU_T) {
-      const int r = i / SU_W, c = i - r * SU_W;
-      F g0 = F(0), g1 = F(0), g2 = F(0), g3 = F(0);
+
+  for (int tl = blockIdx.x; tl < tiles; tl += gridDim.x) {
+    const int ox0 = (tl % p.tiles_x) * SU_W - SU_R, oy0 = (tl / p.tiles_x) * SU_H - SU_R;
+    __syncthreads();  // the previous tile's reads of `tile` are done
+    for (int i = t; i < SU_IH * SU_IW; i += SU_T) {
+      const int r = i / SU_IW, c = i - r * SU_IW;
+      const int gr = oy0 + r, gc = ox0 + c;
+      const bool in = gr >= 0 && gr < p.h && gc >= 0 && gc < p.w;
+      const long long o = in ? (long long)gr * p.w + gc : 0;
 #pragma unroll
-      for (int j = 0; j < 2 * SU_R + 1; ++j) {
-        const F w = F(p.taps[j]);
-        const F u = a[r * SU_IW + c + j], v = b[r * SU_IW + c + j], d = u - v;
-        g0 += w * u;
-        g1 += w * v;
-        g2 += w * (u * u + v * v);
-        g3 += w * (d * d);
-      }
-      hb[(0 * SU_IH + r) * SU_W + c] = g0;
-      hb[(1 * SU_IH + r) * SU_W + c] = g1;
-      hb[(2 * SU_IH + r) * SU_W + c] = g2;
-      hb[(3 * SU_IH + r) * SU_W + c] = g3;
-    }
-    __syncthreads();
-    if (inside) {
-      F m1 = F(0), m2 = F(0), sp = F(0), sd = F(0);
-#pragma unroll
-      for (int j = 0; j < 2 * SU_R + 1; ++j) {
-        const F w = F(p.taps[j]);
-        m1 += w * hb[(0 * SU_IH + ty + j) * SU_W + tx];
-        m2 += w * hb[(1 * SU_IH + ty + j) * SU_W + tx];
-        sp += w * hb[(2 * SU_IH + ty + j) * SU_W + tx];
-        sd += w * hb[(3 * SU_IH + ty + j) * SU_W + tx];
-      }
-      const F x1 = a[(ty + SU_R) * SU_IW + tx + SU_R], x2 = b[(ty + SU_R) * SU_IW + tx + SU_R];
-      // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
-      // the same value, exactly 0 on an identical pair
-      // (frame_analytics/ssimulacra2.py:_scale_maps)
-      const F q = (m1 - m2) * (m1 - m2);
-      const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
-      const F num_s = (den_s - sd) + q;
-      F d = ((sd - q) + q * num_s) / den_s;
-      d = d > F(0) ? d : F(0);
-      const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
-      const F e = (e2 - e1) / (F(1) + e1);
-      const F art = e > F(0) ? e : F(0), lost = e < F(0) ? -e : F(0);
-      const F v[3] = {d, art, lost};
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const F sq = v[k] * v[k];
-        sums[ch * 6 + 2 * k] += (double)v[k];
-        sums[ch * 6 + 2 * k + 1] += (double)(sq * sq);
+      for (int ch = 0; ch < 3; ++ch) {
+        tile[((0 * 3 + ch) * SU_IH + r) * SU_IW + c] = in ? xa[ch * plane + o] : F(0);
+        tile[((1 * 3 + ch) * SU_IH + r) * SU_IW + c] = in ? xb[ch * plane + o] : F(0);
       }
     }
     __syncthreads();
-  }
-  // block sums -> this tile's partials
-  const int tiles = p.tiles_x * p.tiles_y;
-  const long long tidx = (long long)n * tiles + blockIdx.y * p.tiles_x + blockIdx.x;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      const F* a = tile + (0 * 3 + ch) * SU_IH * SU_IW;
+      const F* b = tile + (1 * 3 + ch) * SU_IH * SU_IW;
+      // horizontal: the four groups of every tile row at the tile's columns
+      for (int i = t; i < SU_IH * SU_W; i += SU_T) {
+        const int r = i / SU_W, c = i - r * SU_W;
+        F g0 = F(0), g1 = F(0), g2 = F(0), g3 = F(0);
+#pragma unroll
+        for (int j = 0; j < 2 * SU_R + 1; ++j) {
+          const F w = F(p.taps[j]);
+          const F u = a[r * SU_IW + c + j], v = b[r * SU_IW + c + j], d = u - v;
+          g0 += w * u;
+          g1 += w * v;
+          g2 += w * (u * u + v * v);
+          g3 += w * (d * d);
+        }
+        hb[(0 * SU_IH + r) * SU_W + c] = g0;
+        hb[(1 * SU_IH + r) * SU_W + c] = g1;
+        hb[(2 * SU_IH + r) * SU_W + c] = g2;
+        hb[(3 * SU_IH + r) * SU_W + c] = g3;
+      }
+      __syncthreads();
 #pragma unroll 1
+      for (int rr = ty; rr < SU_H; rr += SU_T / SU_W) {
+        const int gy = oy0 + SU_R + rr, gx = ox0 + SU_R + tx;
+        if (gy >= p.h || gx >= p.w) continue;
+        F m1 = F(0), m2 = F(0), sp = F(0), sd = F(0);
+#pragma unroll
+        for (int j = 0; j < 2 * SU_R + 1; ++j) {
+          const F w = F(p.taps[j]);
+          m1 += w * hb[(0 * SU_IH + rr + j) * SU_W + tx];
+          m2 += w * hb[(1 * SU_IH + rr + j) * SU_W + tx];
+          sp += w * hb[(2 * SU_IH + rr + j) * SU_W + tx];
+          sd += w * hb[(3 * SU_IH + rr + j) * SU_W + tx];
+        }
+        const F x1 = a[(rr + SU_R) * SU_IW + tx + SU_R], x2 = b[(rr + SU_R) * SU_IW + tx + SU_R];
+        // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
+        // the same value, exactly 0 on an identical pair
+        // (frame_analytics/ssimulacra2.py:_scale_maps)
+        const F q = (m1 - m2) * (m1 - m2);
+        const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
+        const F num_s = (den_s - sd) + q;
+        F d = ((sd - q) + q * num_s) / den_s;
+        d = d > F(0) ? d : F(0);
+        const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
+        const F e = (e2 - e1) / (F(1) + e1);
+        const F art = e > F(0) ? e : F(0), lost = e < F(0) ? -e : F(0);
+        const F v[3] = {d, art, lost};
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const F sq = v[k] * v[k];
+          sums[ch * 6 + 2 * k] += (double)v[k];
+          sums[ch * 6 + 2 * k + 1] += (double)(sq * sq);
+        }
+      }
+      __syncthreads();  // hb is rewritten for the next channel
+    }
+  }
+  // this block's sums -> partials [N][blocks][18]
+  const long long pidx = ((long long)n * gridDim.x + blockIdx.x) * SU_SUMS;
+#pragma unroll
   for (int k = 0; k < SU_SUMS; ++k) {
     const double s = block_sum(sums[k], s_red);
-    if (t == 0) p.part[tidx * SU_SUMS + k] = s;
+    if (t == 0) p.part[pidx + k] = s;
   }
-  if (last_block_arrived(p.counter + p.scale, gridDim.x * gridDim.y * gridDim.z, &s_flag)) {
+  if (last_block_arrived(p.counter + p.scale, gridDim.x * gridDim.y, &s_flag)) {
+    // one warp per (image, sum): the blocks' partials in a fixed order
     const double npix = (double)p.h * p.w;
-    for (int img = 0; img < p.N; ++img) {
-      if (t < SU_SUMS) {
-        double s = 0.0;
-        for (int i = 0; i < tiles; ++i) s += p.part[((long long)img * tiles + i) * SU_SUMS + t];
-        s_sum[t] = s;
-      }
-      __syncthreads();
-      if (t < SU_SUMS) {
-        const double m = s_sum[t] / npix;
+    const int lane = t & 31, wid = t >> 5;
+    for (int pair = wid; pair < p.N * SU_SUMS; pair += SU_T / 32) {
+      const int img = pair / SU_SUMS, k = pair - img * SU_SUMS;
+      double s = 0.0;
+      for (int i = lane; i < (int)gridDim.x; i += 32)
+        s += p.part[((long long)img * gridDim.x + i) * SU_SUMS + k];
+      s = warp_sum(s);
+      if (lane == 0) {
+        const double m = s / npix;
         // odd slots hold sums of 4th powers: the 4-norm
-        p.norms[((long long)img * SU_SCALES + p.scale) * SU_SUMS + t] = (t & 1) ? sqrt(sqrt(m)) : m;
+        p.norms[((long long)img * SU_SCALES + p.scale) * SU_SUMS + k] = (k & 1) ? sqrt(sqrt(m)) : m;
       }
-      __syncthreads();
     }
   }
 }
@@ -295,9 +324,16 @@ __global__ void __launch_bounds__(256) su2_score_kernel(const Su2Score s) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+// scale-kernel blocks per image: enough to fill the GPU a few times over
+static int su2_bpi(size_t tiles, int N) {
+  const size_t want = ((size_t)SU_BPI + N - 1) / N;
+  return (int)std::max<size_t>(1, std::min(tiles, want));
+}
+
 struct Su2Plan {
   int scales;
-  int h[SU_SCALES], w[SU_SCALES];
+  int h[SU_SCALES], w[SU_SCALES], bpi[SU_SCALES];
+  size_t xyb_elems;     // both images' XYB planes at scale 0
   size_t lin_elems;     // per image of the pair, both ping-pong buffers
   size_t part_elems;    // doubles
 };
@@ -315,7 +351,8 @@ static Su2Plan su2_plan(int N, int H, int W) {
     pl.w[s] = w;
     pl.scales = s + 1;
     const size_t tiles = (size_t)((w + SU_W - 1) / SU_W) * ((h + SU_H - 1) / SU_H);
-    pl.part_elems = std::max(pl.part_elems, tiles * N * SU_SUMS);
+    pl.bpi[s] = su2_bpi(tiles, N);
+    pl.part_elems = std::max(pl.part_elems, (size_t)pl.bpi[s] * N * SU_SUMS);
     ph = h;
     pw = w;
   }
@@ -323,14 +360,16 @@ static Su2Plan su2_plan(int N, int H, int W) {
   const size_t s1 = pl.scales > 1 ? (size_t)N * 3 * pl.h[1] * pl.w[1] : 0;
   const size_t s2 = pl.scales > 2 ? (size_t)N * 3 * pl.h[2] * pl.w[2] : 0;
   pl.lin_elems = s1 + s2;
+  pl.xyb_elems = (size_t)2 * N * 3 * H * W;
   return pl;
 }
 
 size_t su2_ws_bytes(int N, int H, int W, int fsize) {
   const Su2Plan pl = su2_plan(N, H, W);
-  const size_t lin = 2 * pl.lin_elems * fsize;  // x and y
-  const size_t a = (lin + 255) / 256 * 256;
-  return FAB_COUNTER_BYTES + a + sizeof(double) * (pl.part_elems + (size_t)N * SU_SCALES * SU_SUMS);
+  const size_t lin = (2 * pl.lin_elems * fsize + 255) / 256 * 256;  // x and y
+  const size_t xyb = (pl.xyb_elems * fsize + 255) / 256 * 256;
+  return FAB_COUNTER_BYTES + lin + xyb +
+         sizeof(double) * (pl.part_elems + (size_t)N * SU_SCALES * SU_SUMS);
 }
 
 static void su2_taps(double* out) {
@@ -373,11 +412,11 @@ static void su2_taps(double* out) {
 }
 
 template <typename T, typename F>
-static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, const Su2Score& sc_in, int device,
-                   cudaStream_t st) {
+static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score& sc_in,
+                   int device, cudaStream_t st) {
   static bool done[64] = {false};
   const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);
-  FAB_TRY(ensure_smem(su2_scale_kernel<T, F>, smem, device, done));
+  FAB_TRY(ensure_smem(su2_scale_kernel<F>, smem, device, done));
   const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
   F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
   const long long cap = (long long)sm_count(device) * 8;
@@ -400,10 +439,16 @@ static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, const Su2Score& sc_in,
       p.lx = out;
       p.ly = out + plane;
     }
+    {
+      const long long npx = (long long)p.N * p.h * p.w;
+      const unsigned blocks = (unsigned)std::min<long long>((npx + 255) / 256, cap);
+      su2_xyb_kernel<T, F><<<blocks, 256, 0, st>>>(p, xyb);
+      FAB_LAUNCH_CHECK();
+    }
     p.tiles_x = (p.w + SU_W - 1) / SU_W;
     p.tiles_y = (p.h + SU_H - 1) / SU_H;
-    dim3 grid(p.tiles_x, p.tiles_y, p.N);
-    su2_scale_kernel<T, F><<<grid, SU_T, smem, st>>>(p);
+    dim3 grid(pl.bpi[s], p.N);
+    su2_scale_kernel<F><<<grid, SU_T, smem, st>>>(p, xyb);
     FAB_LAUNCH_CHECK();
   }
   Su2Score sc = sc_in;
@@ -443,8 +488,10 @@ int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64
   char* base = static_cast<char*>(ws);
   p.counter = reinterpret_cast<unsigned int*>(base);
   const size_t lin_bytes = (2 * pl.lin_elems * fsize + 255) / 256 * 256;
+  const size_t xyb_bytes = (pl.xyb_elems * fsize + 255) / 256 * 256;
   char* lin = base + FAB_COUNTER_BYTES;
-  p.part = reinterpret_cast<double*>(lin + lin_bytes);
+  char* xyb = lin + lin_bytes;
+  p.part = reinterpret_cast<double*>(xyb + xyb_bytes);
   p.norms = p.part + pl.part_elems;
   Su2Score sc{};
   for (int i = 0; i < 108; ++i) sc.w[i] = weights[i];
@@ -453,8 +500,10 @@ int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64
   sc.out_per_image = out_per_image;
   sc.out_total = out_total;
 #define FAB_SU2(TT)                                                                        \
-  return f64 ? su2_run<TT, double>(p, pl, reinterpret_cast<double*>(lin), sc, device, st) \
-             : su2_run<TT, float>(p, pl, reinterpret_cast<float*>(lin), sc, device, st)
+  return f64 ? su2_run<TT, double>(p, pl, reinterpret_cast<double*>(lin),                   \
+                                   reinterpret_cast<double*>(xyb), sc, device, st)          \
+             : su2_run<TT, float>(p, pl, reinterpret_cast<float*>(lin),                     \
+                                  reinterpret_cast<float*>(xyb), sc, device, st)
   switch (dtype) {
     case FA_U8: FAB_SU2(unsigned char);
     case FA_F16: FAB_SU2(f16_t);
