@@ -227,7 +227,7 @@ struct GmWin {
 // Ring rows 0..n-1 hold pooled rows g0 .. g0+n-1 of the block (g counted from
 // the block's first pooled row); a map row is emitted from pooled row g >= 2
 // (map row r0 + g - 2).
-template <bool MAP, bool DOWN>
+template <bool MAP, bool DOWN, int NR = GM_R + 2>
 __device__ __forceinline__ void gm_rows_window(const GmsdArgs& p, const float2* ring, int pitch,
                                                int n, int g0, int t, int dc0, int plane, int r0,
                                                GmWin& w, float& fs, float& fs2) {
@@ -238,7 +238,7 @@ __device__ __forceinline__ void gm_rows_window(const GmsdArgs& p, const float2* 
   const float2 kk = make_float2(K, K), ee = make_float2(p.eps, p.eps);
   const float2 m1 = make_float2(-1.f, -1.f);
 #pragma unroll
-  for (int q = 0; q < GM_R + 2; ++q) {
+  for (int q = 0; q < NR; ++q) {
     if (q < n) {
       const float2* rowp = ring + q * pitch;
       const float4 A = *reinterpret_cast<const float4*>(rowp + c0t);
@@ -412,6 +412,50 @@ __device__ __forceinline__ unsigned gm_bytes4(const unsigned char* row, int o) {
   return __funnelshift_r(w[0], w[1], (o & 3) * 8);
 }
 
+// Rows q < n (n <= NR) of the staged bytes pooled (or converted) into the
+// (x, y) float ring of the uint8 TMA kernel: exact integer 2x2 sums by dp4a
+// (the 1/4 is folded into the Prewitt constant).
+template <bool DOWN, int NR>
+__device__ __forceinline__ void gm_pool_rows(const unsigned char* rawx, const unsigned char* rawy,
+                                             float2* ring, int sofs, int t, int n) {
+  using G = GmTma<DOWN>;
+  const bool al4 = (sofs & 3) == 0;  // uniform: staged words are aligned
+#pragma unroll
+  for (int q = 0; q < NR; ++q) {
+    if (q < n) {
+      float4 v;
+      if (DOWN) {
+        const int o = sofs + 4 * t;
+        const unsigned char* x0r = rawx + (2 * q) * G::IW;
+        const unsigned char* y0r = rawy + (2 * q) * G::IW;
+        unsigned ax, bx, ay, by;
+        if (al4) {
+          ax = *reinterpret_cast<const unsigned*>(x0r + o);
+          bx = *reinterpret_cast<const unsigned*>(x0r + G::IW + o);
+          ay = *reinterpret_cast<const unsigned*>(y0r + o);
+          by = *reinterpret_cast<const unsigned*>(y0r + G::IW + o);
+        } else {
+          ax = gm_bytes4(x0r, o);
+          bx = gm_bytes4(x0r + G::IW, o);
+          ay = gm_bytes4(y0r, o);
+          by = gm_bytes4(y0r + G::IW, o);
+        }
+        constexpr unsigned LO = 0x00000101u, HI = 0x01010000u;
+        v = make_float4((float)__dp4a(ax, LO, __dp4a(bx, LO, 0u)),
+                        (float)__dp4a(ay, LO, __dp4a(by, LO, 0u)),
+                        (float)__dp4a(ax, HI, __dp4a(bx, HI, 0u)),
+                        (float)__dp4a(ay, HI, __dp4a(by, HI, 0u)));
+      } else {
+        const unsigned a = gm_bytes4(rawx + q * G::IW, sofs + 2 * t);
+        const unsigned b = gm_bytes4(rawy + q * G::IW, sofs + 2 * t);
+        v = make_float4((float)(a & 0xff), (float)(b & 0xff), (float)((a >> 8) & 0xff),
+                        (float)((b >> 8) & 0xff));
+      }
+      reinterpret_cast<float4*>(ring + q * G::RP)[t] = v;
+    }
+  }
+}
+
 template <bool DOWN, bool MAP>
 __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant__ GmsdArgs p) {
   using G = GmTma<DOWN>;
@@ -467,46 +511,21 @@ __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant
     const int g0 = first_of(it), n = count_of(it);
     mbar_wait(&s_bar, it & 1, p.err);
     // pool (or convert) the staged bytes into the ring: exact integer 2x2
-    // sums by dp4a (the 1/4 is folded into the Prewitt constant)
-    const bool al4 = (sofs & 3) == 0;  // uniform: staged words are aligned
-#pragma unroll
-    for (int q = 0; q < GM_R + 2; ++q) {
-      if (q < n) {
-        float4 v;
-        if (DOWN) {
-          const int o = sofs + 4 * t;
-          const unsigned char* x0r = rawx + (2 * q) * G::IW;
-          const unsigned char* y0r = rawy + (2 * q) * G::IW;
-          unsigned ax, bx, ay, by;
-          if (al4) {
-            ax = *reinterpret_cast<const unsigned*>(x0r + o);
-            bx = *reinterpret_cast<const unsigned*>(x0r + G::IW + o);
-            ay = *reinterpret_cast<const unsigned*>(y0r + o);
-            by = *reinterpret_cast<const unsigned*>(y0r + G::IW + o);
-          } else {
-            ax = gm_bytes4(x0r, o);
-            bx = gm_bytes4(x0r + G::IW, o);
-            ay = gm_bytes4(y0r, o);
-            by = gm_bytes4(y0r + G::IW, o);
-          }
-          constexpr unsigned LO = 0x00000101u, HI = 0x01010000u;
-          v = make_float4((float)__dp4a(ax, LO, __dp4a(bx, LO, 0u)),
-                          (float)__dp4a(ay, LO, __dp4a(by, LO, 0u)),
-                          (float)__dp4a(ax, HI, __dp4a(bx, HI, 0u)),
-                          (float)__dp4a(ay, HI, __dp4a(by, HI, 0u)));
-        } else {
-          const unsigned a = gm_bytes4(rawx + q * G::IW, sofs + 2 * t);
-          const unsigned b = gm_bytes4(rawy + q * G::IW, sofs + 2 * t);
-          v = make_float4((float)(a & 0xff), (float)(b & 0xff), (float)((a >> 8) & 0xff),
-                          (float)((b >> 8) & 0xff));
-        }
-        reinterpret_cast<float4*>(ring + q * G::RP)[t] = v;
-      }
-    }
+    // sums by dp4a (the 1/4 is folded into the Prewitt constant).  The row
+    // count is a compile-time bound for the first (GM_R + 2) and the steady
+    // (GM_R) iterations, so no predicated-off row is issued there.
+    if (n == GM_R + 2) gm_pool_rows<DOWN, GM_R + 2>(rawx, rawy, ring, sofs, t, n);
+    else if (n == GM_R) gm_pool_rows<DOWN, GM_R>(rawx, rawy, ring, sofs, t, n);
+    else gm_pool_rows<DOWN, GM_R + 2>(rawx, rawy, ring, sofs, t, n);
     __syncthreads();
     if (first_of(it + 1) < np_total) issue(it + 1);  // the staging buffer is free again
     float fs = 0.f, fs2 = 0.f;
-    gm_rows_window<MAP, DOWN>(p, ring, G::RP, n, g0, t, dc0, plane, r0, win, fs, fs2);
+    if (n == GM_R + 2)
+      gm_rows_window<MAP, DOWN, GM_R + 2>(p, ring, G::RP, n, g0, t, dc0, plane, r0, win, fs, fs2);
+    else if (n == GM_R)
+      gm_rows_window<MAP, DOWN, GM_R>(p, ring, G::RP, n, g0, t, dc0, plane, r0, win, fs, fs2);
+    else
+      gm_rows_window<MAP, DOWN, GM_R + 2>(p, ring, G::RP, n, g0, t, dc0, plane, r0, win, fs, fs2);
     acc += (double)fs;
     acc2 += (double)fs2;
     __syncthreads();  // the ring is rewritten next iteration
