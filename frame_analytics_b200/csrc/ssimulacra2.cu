@@ -31,6 +31,7 @@
 //                      for the batch
 // Every sum is double.
 #include <algorithm>
+#include <type_traits>
 
 #include "ssim_common.cuh"  // ensure_smem
 
@@ -168,14 +169,90 @@ __global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
   }
 }
 
+// Scale 0: each thread takes one 2x2 block of input pixels (indices clamped
+// to the edge): it writes the XYB of the pixels it owns and, when there is a
+// next scale, the block's mean linear RGB as that scale's pixel -- so every
+// input sample goes through the EOTF once.  uint8 input reads the EOTF from a
+// 256-entry table the block fills first (the same device arithmetic).
+template <typename T, typename F>
+__global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, int h1, int w1,
+                                                        F* lin1x, F* lin1y) {
+  constexpr bool LUT = std::is_same<T, unsigned char>::value;
+  __shared__ F s_lut[LUT ? 256 : 1];
+  if constexpr (LUT) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+      s_lut[i] = srgb_to_linear<F>(F((double)i) * F(p.inv_range));
+    __syncthreads();
+  }
+  const long long plane = (long long)p.h * p.w, plane1 = (long long)h1 * w1;
+  const long long nblk = (long long)p.N * plane1;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < nblk; i += 256LL * gridDim.x) {
+    const int n = (int)(i / plane1);
+    const long long o1 = i - (long long)n * plane1;
+    const int br = (int)(o1 / w1), bc = (int)(o1 - (long long)br * w1);
+#pragma unroll
+    for (int img = 0; img < 2; ++img) {
+      const char* base = img ? p.y : p.x;
+      F acc[3] = {F(0), F(0), F(0)};
+#pragma unroll
+      for (int dr = 0; dr < 2; ++dr)
+#pragma unroll
+        for (int dc = 0; dc < 2; ++dc) {
+          const int r = min(2 * br + dr, p.h - 1), col = min(2 * bc + dc, p.w - 1);
+          F rgb[3];
+#pragma unroll
+          for (int c = 0; c < 3; ++c) {
+            const long long off = (long long)n * p.sn + (long long)c * p.sc + (long long)r * p.sh + col;
+            if constexpr (LUT) rgb[c] = s_lut[reinterpret_cast<const unsigned char*>(base)[off]];
+            else rgb[c] = srgb_to_linear<F>(F(su_raw<T>(base, off)) * F(p.inv_range));
+            acc[c] += rgb[c];
+          }
+          if (2 * br + dr < p.h && 2 * bc + dc < p.w) {
+            F X, Y, B;
+            to_xyb<F>(p, rgb[0], rgb[1], rgb[2], X, Y, B);
+            F* out = xyb + ((long long)img * p.N + n) * 3 * plane + (long long)r * p.w + col;
+            out[0] = X;
+            out[plane] = Y;
+            out[2 * plane] = B;
+          }
+        }
+      F* l1 = img ? lin1y : lin1x;
+      if (l1) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          l1[((long long)n * 3 + c) * plane1 + o1] = F(0.25) * acc[c];
+      }
+    }
+  }
+}
+
+// (x, y) pairs: packed f32x2 arithmetic for float, plain pairs for double.
+template <typename F> struct Pair;
+template <> struct Pair<float> {
+  using V = float2;
+  static __device__ __forceinline__ V make(float a, float b) { return make_float2(a, b); }
+  static __device__ __forceinline__ V fma(V w, V a, V c) { return __ffma2_rn(w, a, c); }
+};
+template <> struct Pair<double> {
+  using V = double2;
+  static __device__ __forceinline__ V make(double a, double b) { return make_double2(a, b); }
+  static __device__ __forceinline__ V fma(V w, V a, V c) {
+    return make_double2(::fma(w.x, a.x, c.x), ::fma(w.y, a.y, c.y));
+  }
+};
+
 // One block per (strip of tiles, image): the block walks its image's 32 x 32
 // tiles with a stride, keeping the 18 per-channel sums in registers; each
-// thread computes four output rows of a tile.
+// thread computes four output rows of a tile.  The tile holds (x1, x2) pairs
+// per pixel and the horizontal pass (mu1, mu2) and (x1^2 + x2^2, (x1 - x2)^2)
+// pairs, so every tap is two packed FMAs.
 template <typename F>
 __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const F* xyb) {
+  using P = Pair<F>;
+  using V = typename P::V;
   extern __shared__ __align__(16) unsigned char su_smem[];
-  F* tile = reinterpret_cast<F*>(su_smem);      // [2 images][3 ch][IH][IW]
-  F* hb = tile + 2 * 3 * SU_IH * SU_IW;         // [4 groups][IH][W]
+  V* tile = reinterpret_cast<V*>(su_smem);      // [3 ch][IH][IW] (x1, x2)
+  V* hb = tile + 3 * SU_IH * SU_IW;             // [IH][W][2]: (g0, g1), (g2, g3)
   __shared__ double s_red[32];
   __shared__ int s_flag;
   const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
@@ -197,56 +274,53 @@ __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const 
       const bool in = gr >= 0 && gr < p.h && gc >= 0 && gc < p.w;
       const long long o = in ? (long long)gr * p.w + gc : 0;
 #pragma unroll
-      for (int ch = 0; ch < 3; ++ch) {
-        tile[((0 * 3 + ch) * SU_IH + r) * SU_IW + c] = in ? xa[ch * plane + o] : F(0);
-        tile[((1 * 3 + ch) * SU_IH + r) * SU_IW + c] = in ? xb[ch * plane + o] : F(0);
-      }
+      for (int ch = 0; ch < 3; ++ch)
+        tile[(ch * SU_IH + r) * SU_IW + c] =
+            in ? P::make(xa[ch * plane + o], xb[ch * plane + o]) : P::make(F(0), F(0));
     }
     __syncthreads();
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
-      const F* a = tile + (0 * 3 + ch) * SU_IH * SU_IW;
-      const F* b = tile + (1 * 3 + ch) * SU_IH * SU_IW;
-      // horizontal: the four groups of every tile row at the tile's columns
+      const V* tc = tile + ch * SU_IH * SU_IW;
+      // horizontal: the two pairs of every tile row at the tile's columns
       for (int i = t; i < SU_IH * SU_W; i += SU_T) {
         const int r = i / SU_W, c = i - r * SU_W;
-        F g0 = F(0), g1 = F(0), g2 = F(0), g3 = F(0);
+        V m = P::make(F(0), F(0)), q = P::make(F(0), F(0));
 #pragma unroll
         for (int j = 0; j < 2 * SU_R + 1; ++j) {
-          const F w = F(p.taps[j]);
-          const F u = a[r * SU_IW + c + j], v = b[r * SU_IW + c + j], d = u - v;
-          g0 += w * u;
-          g1 += w * v;
-          g2 += w * (u * u + v * v);
-          g3 += w * (d * d);
+          const F wj = F(p.taps[j]);
+          const V w = P::make(wj, wj);
+          const V u = tc[r * SU_IW + c + j];
+          const F d = u.x - u.y;
+          m = P::fma(w, u, m);
+          q = P::fma(w, P::make(u.x * u.x + u.y * u.y, d * d), q);
         }
-        hb[(0 * SU_IH + r) * SU_W + c] = g0;
-        hb[(1 * SU_IH + r) * SU_W + c] = g1;
-        hb[(2 * SU_IH + r) * SU_W + c] = g2;
-        hb[(3 * SU_IH + r) * SU_W + c] = g3;
+        hb[(r * SU_W + c) * 2] = m;
+        hb[(r * SU_W + c) * 2 + 1] = q;
       }
       __syncthreads();
 #pragma unroll 1
       for (int rr = ty; rr < SU_H; rr += SU_T / SU_W) {
         const int gy = oy0 + SU_R + rr, gx = ox0 + SU_R + tx;
         if (gy >= p.h || gx >= p.w) continue;
-        F m1 = F(0), m2 = F(0), sp = F(0), sd = F(0);
+        V m = P::make(F(0), F(0)), q = P::make(F(0), F(0));
 #pragma unroll
         for (int j = 0; j < 2 * SU_R + 1; ++j) {
-          const F w = F(p.taps[j]);
-          m1 += w * hb[(0 * SU_IH + rr + j) * SU_W + tx];
-          m2 += w * hb[(1 * SU_IH + rr + j) * SU_W + tx];
-          sp += w * hb[(2 * SU_IH + rr + j) * SU_W + tx];
-          sd += w * hb[(3 * SU_IH + rr + j) * SU_W + tx];
+          const F wj = F(p.taps[j]);
+          const V w = P::make(wj, wj);
+          m = P::fma(w, hb[((rr + j) * SU_W + tx) * 2], m);
+          q = P::fma(w, hb[((rr + j) * SU_W + tx) * 2 + 1], q);
         }
-        const F x1 = a[(rr + SU_R) * SU_IW + tx + SU_R], x2 = b[(rr + SU_R) * SU_IW + tx + SU_R];
+        const F m1 = m.x, m2 = m.y, sp = q.x, sd = q.y;
+        const V xc = tc[(rr + SU_R) * SU_IW + tx + SU_R];
+        const F x1 = xc.x, x2 = xc.y;
         // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
         // the same value, exactly 0 on an identical pair
         // (frame_analytics/ssimulacra2.py:_scale_maps)
-        const F q = (m1 - m2) * (m1 - m2);
+        const F qq = (m1 - m2) * (m1 - m2);
         const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
-        const F num_s = (den_s - sd) + q;
-        F d = ((sd - q) + q * num_s) / den_s;
+        const F num_s = (den_s - sd) + qq;
+        F d = ((sd - qq) + qq * num_s) / den_s;
         d = d > F(0) ? d : F(0);
         const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
         const F e = (e2 - e1) / (F(1) + e1);
@@ -415,7 +489,7 @@ template <typename T, typename F>
 static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score& sc_in,
                    int device, cudaStream_t st) {
   static bool done[64] = {false};
-  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);
+  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);  // pairs
   FAB_TRY(ensure_smem(su2_scale_kernel<F>, smem, device, done));
   const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
   F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
@@ -424,22 +498,32 @@ static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score
     p.scale = s;
     p.h = pl.h[s];
     p.w = pl.w[s];
-    if (s > 0) {
+    if (s == 0) {
+      // XYB of scale 0 and, in the same pass, scale 1's linear planes
+      const int h1 = pl.scales > 1 ? pl.h[1] : (p.h + 1) / 2;
+      const int w1 = pl.scales > 1 ? pl.w[1] : (p.w + 1) / 2;
+      const size_t plane1 = (size_t)p.N * 3 * h1 * w1;
+      F* o = pl.scales > 1 ? buf[0] : nullptr;
+      const long long nb = (long long)p.N * h1 * w1;
+      const unsigned blocks = (unsigned)std::min<long long>((nb + 255) / 256, cap);
+      su2_xyb0_kernel<T, F><<<blocks, 256, 0, st>>>(p, xyb, h1, w1, o, o ? o + plane1 : nullptr);
+      FAB_LAUNCH_CHECK();
+    } else if (s == 1) {
+      const size_t plane = (size_t)p.N * 3 * pl.h[1] * pl.w[1];
+      p.lx = buf[0];
+      p.ly = buf[0] + plane;
+    } else {
       F* out = buf[(s - 1) & 1];
       const size_t plane = (size_t)p.N * 3 * pl.h[s] * pl.w[s];
       const long long n_out = (long long)plane;
       const unsigned blocks = (unsigned)std::min<long long>((n_out + 255) / 256, cap);
-      if (s == 1) {
-        su2_down_kernel<T, F, true><<<blocks, 256, 0, st>>>(p, pl.h[0], pl.w[0], out, out + plane);
-      } else {
-        su2_down_kernel<T, F, false><<<blocks, 256, 0, st>>>(p, pl.h[s - 1], pl.w[s - 1], out,
-                                                             out + plane);
-      }
+      su2_down_kernel<T, F, false><<<blocks, 256, 0, st>>>(p, pl.h[s - 1], pl.w[s - 1], out,
+                                                           out + plane);
       FAB_LAUNCH_CHECK();
       p.lx = out;
       p.ly = out + plane;
     }
-    {
+    if (s > 0) {
       const long long npx = (long long)p.N * p.h * p.w;
       const unsigned blocks = (unsigned)std::min<long long>((npx + 255) / 256, cap);
       su2_xyb_kernel<T, F><<<blocks, 256, 0, st>>>(p, xyb);
