@@ -44,3 +44,19 @@ def test_yuv420_scores_match_the_oracle(bits):
     assert abs(got["float_ssim"] - O.ssim(x, y, data_range=L)) < 5e-6
     _, sd = O.gmsd(x, y, data_range=L, eps=(1e-6 * L) ** 2)
     assert abs(got["gmsd"] - float(sd[0])) < 5e-6
+
+
+def test_rgb_planes_score_ssimulacra2_and_ssim():
+    """Planar RGB frames: the image features see all three channels."""
+    w, h = 96, 64
+    rng = np.random.default_rng(3)
+    a = rng.integers(0, 256, 3 * h * w).astype(np.uint8)
+    b = np.clip(a.astype(np.int16) + rng.integers(-6, 7, a.shape), 0, 255).astype(np.uint8)
+    ra = planes.frame_planes(torch.from_numpy(a).cuda(), w, h, "rgbp")
+    rb = planes.frame_planes(torch.from_numpy(b).cuda(), w, h, "rgbp")
+    got = planes.PlaneScorer(["ssim", "ssimulacra2", "psnr"], family="rgb").scores(ra, rb)
+    x = a.reshape(1, 3, h, w)
+    y = b.reshape(1, 3, h, w)
+    assert abs(got["float_ssim"] - O.ssim(x, y)) < 5e-6
+    assert abs(got["ssimulacra2"] - O.ssimulacra2(x[0], y[0], 255.0)) < 5e-3
+    assert set(got) == {"float_ssim", "ssimulacra2", "psnr_r", "psnr_g", "psnr_b"}
