@@ -134,21 +134,31 @@ __device__ __forceinline__ bool last_block_arrived(unsigned int* counter,
 // ---------------------------------------------------------------------------
 // host plumbing
 // ---------------------------------------------------------------------------
-struct DeviceScope {
-  int prev = -1;
-  bool changed = false;
-  cudaError_t status = cudaSuccess;
-  explicit DeviceScope(int dev) {
-    status = cudaGetDevice(&prev);
-    if (status == cudaSuccess && dev >= 0 && dev != prev) {
-      status = cudaSetDevice(dev);
-      changed = (status == cudaSuccess);
+// Makes `dev` current for its lifetime and puts the caller's device back;
+// dev < 0 keeps whatever is current.
+class ScopedDevice {
+ public:
+  explicit ScopedDevice(int dev) : err_(cudaGetDevice(&saved_)) {
+    if (err_ == cudaSuccess && dev >= 0 && dev != saved_) {
+      err_ = cudaSetDevice(dev);
+      switched_ = err_ == cudaSuccess;
     }
   }
-  ~DeviceScope() {
-    if (changed) cudaSetDevice(prev);
+  ~ScopedDevice() {
+    if (switched_) cudaSetDevice(saved_);
   }
+  ScopedDevice(const ScopedDevice&) = delete;
+  ScopedDevice& operator=(const ScopedDevice&) = delete;
+  cudaError_t error() const { return err_; }
+
+ private:
+  int saved_ = -1;
+  cudaError_t err_;
+  bool switched_ = false;
 };
+
+// A CUDA error as this library's status: 0, or minus the error code.
+constexpr int status_of(cudaError_t e) { return e == cudaSuccess ? 0 : -static_cast<int>(e); }
 
 int sm_count(int device);
 
@@ -180,17 +190,12 @@ struct GmOut {
 
 }  // namespace fab
 
-#define FAB_TRY(EXPR)                                   \
-  do {                                                  \
-    const cudaError_t e_ = (EXPR);                      \
-    if (e_ != cudaSuccess) return -static_cast<int>(e_); \
+#define FAB_TRY(EXPR)                                         \
+  do {                                                        \
+    if (const int st_ = ::fab::status_of(EXPR)) return st_;   \
   } while (0)
 
-#define FAB_LAUNCH_CHECK()                              \
-  do {                                                  \
-    const cudaError_t e_ = cudaGetLastError();          \
-    if (e_ != cudaSuccess) return -static_cast<int>(e_); \
-  } while (0)
+#define FAB_LAUNCH_CHECK() FAB_TRY(cudaGetLastError())
 
 // First statement of every compute entry point: report a wait that gave up.
 #define FAB_PENDING()                                          \
@@ -198,9 +203,9 @@ struct GmOut {
     if (const int pend_ = ::fab::take_wait_error()) return pend_; \
   } while (0)
 
-#define FAB_DEVICE_SCOPE(DEV)        \
-  ::fab::DeviceScope guard_(DEV);    \
-  if (guard_.status != cudaSuccess) return -static_cast<int>(guard_.status)
+#define FAB_DEVICE_SCOPE(DEV)                                            \
+  const ::fab::ScopedDevice scoped_dev_(DEV);                            \
+  if (const int st_ = ::fab::status_of(scoped_dev_.error())) return st_
 
 // bytes reserved at the head of every workspace for completion counters
 #define FAB_COUNTER_BYTES 256
