@@ -60,3 +60,20 @@ def test_rgb_planes_score_ssimulacra2_and_ssim():
     assert abs(got["float_ssim"] - O.ssim(x, y)) < 5e-6
     assert abs(got["ssimulacra2"] - O.ssimulacra2(x[0], y[0], 255.0)) < 5e-3
     assert set(got) == {"float_ssim", "ssimulacra2", "psnr_r", "psnr_g", "psnr_b"}
+
+
+def test_yuv422_and_444_views_score_each_plane():
+    for layout, (cw, ch) in (("yuv422p", (2, 1)), ("yuv444p", (1, 1))):
+        w, h = 64, 48
+        n = h * w + 2 * (h // ch) * (w // cw)
+        rng = np.random.default_rng(cw)
+        a = rng.integers(0, 256, n).astype(np.uint8)
+        b = np.clip(a.astype(np.int16) + rng.integers(-5, 6, n), 0, 255).astype(np.uint8)
+        ra = planes.frame_planes(torch.from_numpy(a).cuda(), w, h, layout)
+        rb = planes.frame_planes(torch.from_numpy(b).cuda(), w, h, layout)
+        got = planes.PlaneScorer(["mse"], family="yuv").scores(ra, rb)
+        na = planes.frame_planes(torch.from_numpy(a.astype(np.int64)), w, h, layout)
+        nb = planes.frame_planes(torch.from_numpy(b.astype(np.int64)), w, h, layout)
+        for i, sfx in enumerate(("_y", "_cb", "_cr")):
+            d = (na[i] - nb[i]).double()
+            assert got["mse" + sfx] == float((d * d).mean())

@@ -74,3 +74,24 @@ def test_monotone_in_distortion():
     s = [float(fa.ssimulacra2(x, torch.as_tensor(v, dtype=torch.uint8, device="cuda"),
                               data_range=255.0)) for v in (mild, harsh)]
     assert s[0] > s[1]
+
+
+def test_uint16_strided_and_gray_inputs():
+    """16-bit input (data_range 65535), a strided crop view, and a 1-channel
+    frame (replicated through a zero channel stride) all match the oracle."""
+    a, b = G["s0_a"].astype(np.float64), G["s0_b"].astype(np.float64)
+    x16 = torch.as_tensor((a * 257).astype(np.uint16), device="cuda")
+    y16 = torch.as_tensor((b * 257).astype(np.uint16), device="cuda")
+    want = float(G["s0_ref64"])
+    assert abs(float(fa.ssimulacra2(x16, y16, data_range=65535.0)) - want) < 5e-3
+    big = torch.zeros((3, 80, 96), dtype=torch.uint8, device="cuda")
+    big2 = big.clone()
+    big[:, 5:69, 7:79] = _t("s0", "a")
+    big2[:, 5:69, 7:79] = _t("s0", "b")
+    view_x, view_y = big[:, 5:69, 7:79], big2[:, 5:69, 7:79]
+    assert not view_x.is_contiguous()
+    assert abs(float(fa.ssimulacra2(view_x, view_y, data_range=255.0, dtype=torch.float64))
+               - want) < 1e-8
+    g_ref = float(G["g0_ref64"])
+    assert abs(float(fa.ssimulacra2(_t("g0", "a"), _t("g0", "b"), data_range=255.0,
+                                    dtype=torch.float64)) - g_ref) < 1e-8
