@@ -485,7 +485,7 @@ def cfg4_sweep(args, world: int, rank: int, dev, hbm: float):
                     "shard and one NCCL all-gather of both metrics' per-image values per step",
         "images_total": n, "images_per_rank_max": -(-n // world), "ms_per_step": ms,
         "Gpixel/s": px / (ms / 1e3) / 1e9,
-        # SURVEY's per-pass algorithmic bytes (2 B per pixel pair, two metric passes)
+        # algorithmic bytes per metric pass: 2 B per pixel pair; SSIM and GMSD are two passes
         "GB/s_algorithmic_two_passes": 4 * px / (ms / 1e3) / 1e9,
         "hbm_frac_per_gpu_two_passes": 4 * per_gpu_px / (kern_ms / 1e3) / 1e9 / hbm,
         "kernels_ms_per_rank": kern_ms, "single_pass_fused_ms_per_rank": sep_ms,
