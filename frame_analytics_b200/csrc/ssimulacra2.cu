@@ -22,7 +22,8 @@
 //                      pixel converted once (scale 0 straight from the input)
 //   su2_scale_kernel   a few hundred blocks per image walk its 32 x 32 tiles:
 //                      the tile plus a 5-pixel halo of both images' XYB is
-//                      staged in shared memory (zero outside), the four groups
+//                      staged in shared memory (zero outside; the next tile
+//                      is copied by cp.async while this one is computed), the four groups
 //                      are blurred separably per channel, the maps are formed
 //                      and the 18 per-channel sums kept in registers; the last
 //                      block of the launch turns each image's sums into its
@@ -145,7 +146,8 @@ __global__ void __launch_bounds__(256) su2_down_kernel(const Su2Args p, int ph, 
   }
 }
 
-// Positive XYB planes of both images at this scale: [2][N][3][h][w].
+// Positive XYB planes of both images at this scale: [N][3][h][w] of (x, y)
+// pairs, the layout the scale kernel stages tiles from.
 template <typename T, typename F>
 __global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
   const long long plane = (long long)p.h * p.w;
@@ -161,10 +163,10 @@ __global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
       const F B = su_linear<T, F>(p, img, n, 2, r, col);
       F X, Y, Bc;
       to_xyb<F>(p, R, G, B, X, Y, Bc);
-      F* out = xyb + ((long long)img * p.N + n) * 3 * plane + o;
+      F* out = xyb + ((long long)n * 3 * plane + o) * 2 + img;
       out[0] = X;
-      out[plane] = Y;
-      out[2 * plane] = Bc;
+      out[2 * plane] = Y;
+      out[4 * plane] = Bc;
     }
   }
 }
@@ -210,10 +212,10 @@ __global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, 
           if (2 * br + dr < p.h && 2 * bc + dc < p.w) {
             F X, Y, B;
             to_xyb<F>(p, rgb[0], rgb[1], rgb[2], X, Y, B);
-            F* out = xyb + ((long long)img * p.N + n) * 3 * plane + (long long)r * p.w + col;
+            F* out = xyb + ((long long)n * 3 * plane + (long long)r * p.w + col) * 2 + img;
             out[0] = X;
-            out[plane] = Y;
-            out[2 * plane] = B;
+            out[2 * plane] = Y;
+            out[4 * plane] = B;
           }
         }
       F* l1 = img ? lin1y : lin1x;
@@ -241,44 +243,79 @@ template <> struct Pair<double> {
   }
 };
 
+// One tile of (x1, x2) pairs plus its halo into shared memory by cp.async,
+// zero outside the image (a zero source size fills the destination with 0).
+template <typename V>
+__device__ __forceinline__ void su2_load_tile(V* dst, const V* src, long long plane, int h, int w,
+                                              int ox0, int oy0) {
+  for (int i = threadIdx.x; i < SU_IH * SU_IW; i += SU_T) {
+    const int r = i / SU_IW, c = i - r * SU_IW;
+    const int gr = oy0 + r, gc = ox0 + c;
+    const bool in = gr >= 0 && gr < h && gc >= 0 && gc < w;
+    const long long o = in ? (long long)gr * w + gc : 0;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      const unsigned d = smem_u32(dst + (ch * SU_IH + r) * SU_IW + c);
+      const V* g = src + ch * plane + o;
+      if constexpr (sizeof(V) == 16) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(g),
+                     "r"(in ? 16 : 0) : "memory");
+      } else {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(g),
+                     "r"(in ? 8 : 0) : "memory");
+      }
+    }
+  }
+}
+
 // One block per (strip of tiles, image): the block walks its image's 32 x 32
 // tiles with a stride, keeping the 18 per-channel sums in registers; each
-// thread computes four output rows of a tile.  The tile holds (x1, x2) pairs
-// per pixel and the horizontal pass (mu1, mu2) and (x1^2 + x2^2, (x1 - x2)^2)
-// pairs, so every tap is two packed FMAs.
+// thread computes four output rows of a tile.  The next tile is copied
+// (cp.async) into a second buffer while this one is computed.  The tile holds
+// (x1, x2) pairs per pixel and the horizontal pass (mu1, mu2) and
+// (x1^2 + x2^2, (x1 - x2)^2) pairs, so every tap is two packed FMAs.
 template <typename F>
 __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const F* xyb) {
   using P = Pair<F>;
   using V = typename P::V;
   extern __shared__ __align__(16) unsigned char su_smem[];
-  V* tile = reinterpret_cast<V*>(su_smem);      // [3 ch][IH][IW] (x1, x2)
-  V* hb = tile + 3 * SU_IH * SU_IW;             // [IH][W][2]: (g0, g1), (g2, g3)
+  V* tiles_buf = reinterpret_cast<V*>(su_smem);      // 2 x [3 ch][IH][IW] (x1, x2)
+  V* hb = tiles_buf + 2 * 3 * SU_IH * SU_IW;         // [IH][W][2]: (g0, g1), (g2, g3)
   __shared__ double s_red[32];
   __shared__ int s_flag;
   const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
   const int n = blockIdx.y;
   const long long plane = (long long)p.h * p.w;
-  const F* xa = xyb + (long long)n * 3 * plane;                    // image x
-  const F* xb = xyb + ((long long)p.N + n) * 3 * plane;            // image y
+  const V* src = reinterpret_cast<const V*>(xyb) + (long long)n * 3 * plane;
   const int tiles = p.tiles_x * p.tiles_y;
   double sums[SU_SUMS];
 #pragma unroll
   for (int k = 0; k < SU_SUMS; ++k) sums[k] = 0.0;
 
-  for (int tl = blockIdx.x; tl < tiles; tl += gridDim.x) {
-    const int ox0 = (tl % p.tiles_x) * SU_W - SU_R, oy0 = (tl / p.tiles_x) * SU_H - SU_R;
-    __syncthreads();  // the previous tile's reads of `tile` are done
-    for (int i = t; i < SU_IH * SU_IW; i += SU_T) {
-      const int r = i / SU_IW, c = i - r * SU_IW;
-      const int gr = oy0 + r, gc = ox0 + c;
-      const bool in = gr >= 0 && gr < p.h && gc >= 0 && gc < p.w;
-      const long long o = in ? (long long)gr * p.w + gc : 0;
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch)
-        tile[(ch * SU_IH + r) * SU_IW + c] =
-            in ? P::make(xa[ch * plane + o], xb[ch * plane + o]) : P::make(F(0), F(0));
+  auto origin = [&](int tl, int& ox0, int& oy0) {
+    ox0 = (tl % p.tiles_x) * SU_W - SU_R;
+    oy0 = (tl / p.tiles_x) * SU_H - SU_R;
+  };
+  if ((int)blockIdx.x < tiles) {
+    int ox0, oy0;
+    origin(blockIdx.x, ox0, oy0);
+    su2_load_tile(tiles_buf, src, plane, p.h, p.w, ox0, oy0);
+  }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  int cur = 0;
+  for (int tl = blockIdx.x; tl < tiles; tl += gridDim.x, cur ^= 1) {
+    int ox0, oy0;
+    origin(tl, ox0, oy0);
+    const int nxt = tl + gridDim.x;
+    if (nxt < tiles) {  // the other buffer was last read before the previous barrier
+      int nx0, ny0;
+      origin(nxt, nx0, ny0);
+      su2_load_tile(tiles_buf + (cur ^ 1) * 3 * SU_IH * SU_IW, src, plane, p.h, p.w, nx0, ny0);
     }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // this tile has landed
     __syncthreads();
+    const V* tile = tiles_buf + cur * 3 * SU_IH * SU_IW;
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
       const V* tc = tile + ch * SU_IH * SU_IW;
@@ -489,7 +526,8 @@ template <typename T, typename F>
 static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score& sc_in,
                    int device, cudaStream_t st) {
   static bool done[64] = {false};
-  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);  // pairs
+  // two tiles of (x1, x2) pairs and the horizontal pairs
+  const size_t smem = sizeof(F) * (2 * 2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);
   FAB_TRY(ensure_smem(su2_scale_kernel<F>, smem, device, done));
   const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
   F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
