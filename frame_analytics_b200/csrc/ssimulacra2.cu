@@ -39,9 +39,11 @@
 namespace fab {
 
 constexpr int SU_W = 32, SU_H = 32, SU_R = 5;  // tile, blur radius
-constexpr int SU_BPI = 148 * 3;  // scale-kernel blocks per image at most
+constexpr int SU_BPI = 148 * 2;  // scale-kernel blocks of one launch at most
 constexpr int SU_T = 256;
 constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
+static_assert(SU_H / (SU_T / SU_W) == 4 && SU_W % 4 == 0, 
+              "the blur passes compute four outputs per item");
 constexpr int SU_SCALES = 6;
 constexpr int SU_SUMS = 18;  // 3 channels x {d, d^4, art, art^4, lost, lost^4}
 
@@ -234,6 +236,15 @@ template <> struct Pair<float> {
   using V = float2;
   static __device__ __forceinline__ V make(float a, float b) { return make_float2(a, b); }
   static __device__ __forceinline__ V fma(V w, V a, V c) { return __ffma2_rn(w, a, c); }
+  // two adjacent pairs in one 16-byte shared-memory access
+  static __device__ __forceinline__ void load2(const V* p, V& a, V& b) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    a = make_float2(v.x, v.y);
+    b = make_float2(v.z, v.w);
+  }
+  static __device__ __forceinline__ void store2(V* p, V a, V b) {
+    *reinterpret_cast<float4*>(p) = make_float4(a.x, a.y, b.x, b.y);
+  }
 };
 template <> struct Pair<double> {
   using V = double2;
@@ -241,6 +252,8 @@ template <> struct Pair<double> {
   static __device__ __forceinline__ V fma(V w, V a, V c) {
     return make_double2(::fma(w.x, a.x, c.x), ::fma(w.y, a.y, c.y));
   }
+  static __device__ __forceinline__ void load2(const V* p, V& a, V& b) { a = p[0]; b = p[1]; }
+  static __device__ __forceinline__ void store2(V* p, V a, V b) { p[0] = a; p[1] = b; }
 };
 
 // One tile of (x1, x2) pairs plus its halo into shared memory by cp.async,
@@ -319,55 +332,87 @@ __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const 
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
       const V* tc = tile + ch * SU_IH * SU_IW;
-      // horizontal: the two pairs of every tile row at the tile's columns
-      for (int i = t; i < SU_IH * SU_W; i += SU_T) {
-        const int r = i / SU_W, c = i - r * SU_W;
-        V m = P::make(F(0), F(0)), q = P::make(F(0), F(0));
+      // horizontal: four adjacent columns of one tile row per item, from a
+      // 14-wide window of pairs; the squares of every input are formed once
+      for (int i = t; i < SU_IH * (SU_W / 4); i += SU_T) {
+        const int r = i / (SU_W / 4), c0 = (i - r * (SU_W / 4)) * 4;
+        const V* row = tc + r * SU_IW + c0;
+        V m[4], q[4];
 #pragma unroll
-        for (int j = 0; j < 2 * SU_R + 1; ++j) {
-          const F wj = F(p.taps[j]);
-          const V w = P::make(wj, wj);
-          const V u = tc[r * SU_IW + c + j];
-          const F d = u.x - u.y;
-          m = P::fma(w, u, m);
-          q = P::fma(w, P::make(u.x * u.x + u.y * u.y, d * d), q);
+        for (int o = 0; o < 4; ++o) m[o] = q[o] = P::make(F(0), F(0));
+#pragma unroll
+        for (int j2 = 0; j2 < 7; ++j2) {
+          V uu[2];
+          P::load2(row + 2 * j2, uu[0], uu[1]);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = 2 * j2 + e;
+            const V u = uu[e];
+            const F d = u.x - u.y;
+            const V sq = P::make(u.x * u.x + u.y * u.y, d * d);
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+              const int k = j - o;
+              if (k >= 0 && k < 2 * SU_R + 1) {
+                const V w = P::make(F(p.taps[k]), F(p.taps[k]));
+                m[o] = P::fma(w, u, m[o]);
+                q[o] = P::fma(w, sq, q[o]);
+              }
+            }
+          }
         }
-        hb[(r * SU_W + c) * 2] = m;
-        hb[(r * SU_W + c) * 2 + 1] = q;
+#pragma unroll
+        for (int o = 0; o < 4; ++o) P::store2(hb + (r * SU_W + c0 + o) * 2, m[o], q[o]);
       }
       __syncthreads();
-#pragma unroll 1
-      for (int rr = ty; rr < SU_H; rr += SU_T / SU_W) {
-        const int gy = oy0 + SU_R + rr, gx = ox0 + SU_R + tx;
-        if (gy >= p.h || gx >= p.w) continue;
-        V m = P::make(F(0), F(0)), q = P::make(F(0), F(0));
+      {
+        // vertical: four adjacent rows of one column per thread, from a
+        // 14-high window of (mu, sq) pair couples
+        const int r0 = ty * (SU_H / (SU_T / SU_W));
+        V m[4], q[4];
 #pragma unroll
-        for (int j = 0; j < 2 * SU_R + 1; ++j) {
-          const F wj = F(p.taps[j]);
-          const V w = P::make(wj, wj);
-          m = P::fma(w, hb[((rr + j) * SU_W + tx) * 2], m);
-          q = P::fma(w, hb[((rr + j) * SU_W + tx) * 2 + 1], q);
+        for (int o = 0; o < 4; ++o) m[o] = q[o] = P::make(F(0), F(0));
+#pragma unroll
+        for (int j = 0; j < 2 * SU_R + 4; ++j) {
+          V a, b2;
+          P::load2(hb + ((r0 + j) * SU_W + tx) * 2, a, b2);
+#pragma unroll
+          for (int o = 0; o < 4; ++o) {
+            const int k = j - o;
+            if (k >= 0 && k < 2 * SU_R + 1) {
+              const V w = P::make(F(p.taps[k]), F(p.taps[k]));
+              m[o] = P::fma(w, a, m[o]);
+              q[o] = P::fma(w, b2, q[o]);
+            }
+          }
         }
-        const F m1 = m.x, m2 = m.y, sp = q.x, sd = q.y;
-        const V xc = tc[(rr + SU_R) * SU_IW + tx + SU_R];
-        const F x1 = xc.x, x2 = xc.y;
-        // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
-        // the same value, exactly 0 on an identical pair
-        // (frame_analytics/ssimulacra2.py:_scale_maps)
-        const F qq = (m1 - m2) * (m1 - m2);
-        const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
-        const F num_s = (den_s - sd) + qq;
-        F d = ((sd - qq) + qq * num_s) / den_s;
-        d = d > F(0) ? d : F(0);
-        const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
-        const F e = (e2 - e1) / (F(1) + e1);
-        const F art = e > F(0) ? e : F(0), lost = e < F(0) ? -e : F(0);
-        const F v[3] = {d, art, lost};
+        const int gx = ox0 + SU_R + tx;
 #pragma unroll
-        for (int k = 0; k < 3; ++k) {
-          const F sq = v[k] * v[k];
-          sums[ch * 6 + 2 * k] += (double)v[k];
-          sums[ch * 6 + 2 * k + 1] += (double)(sq * sq);
+        for (int o = 0; o < 4; ++o) {
+          const int rr = r0 + o;
+          const int gy = oy0 + SU_R + rr;
+          if (gy >= p.h || gx >= p.w) continue;
+          const F m1 = m[o].x, m2 = m[o].y, sp = q[o].x, sd = q[o].y;
+          const V xc = tc[(rr + SU_R) * SU_IW + tx + SU_R];
+          const F x1 = xc.x, x2 = xc.y;
+          // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
+          // the same value, exactly 0 on an identical pair
+          // (frame_analytics/ssimulacra2.py:_scale_maps)
+          const F qq = (m1 - m2) * (m1 - m2);
+          const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
+          const F num_s = (den_s - sd) + qq;
+          F d = ((sd - qq) + qq * num_s) / den_s;
+          d = d > F(0) ? d : F(0);
+          const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
+          const F e = (e2 - e1) / (F(1) + e1);
+          const F art = e > F(0) ? e : F(0), lost = e < F(0) ? -e : F(0);
+          const F v[3] = {d, art, lost};
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            const F sq = v[k] * v[k];
+            sums[ch * 6 + 2 * k] += (double)v[k];
+            sums[ch * 6 + 2 * k + 1] += (double)(sq * sq);
+          }
         }
       }
       __syncthreads();  // hb is rewritten for the next channel
@@ -435,10 +480,12 @@ __global__ void __launch_bounds__(256) su2_score_kernel(const Su2Score s) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-// scale-kernel blocks per image: enough to fill the GPU a few times over
+// scale-kernel blocks per image: at most SU_BPI blocks in all (one wave of
+// two resident blocks per SM), each walking the same number of tiles give or
+// take one, so no second partial wave and no idle tail
 static int su2_bpi(size_t tiles, int N) {
-  const size_t want = ((size_t)SU_BPI + N - 1) / N;
-  return (int)std::max<size_t>(1, std::min(tiles, want));
+  const size_t per = (tiles * N + SU_BPI - 1) / SU_BPI;  // tiles per block
+  return (int)std::max<size_t>(1, (tiles + per - 1) / per);
 }
 
 struct Su2Plan {
