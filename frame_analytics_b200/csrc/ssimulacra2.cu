@@ -20,7 +20,7 @@
 //                      scale 1, from the previous linear planes after that)
 //   su2_xyb_kernel     both images' positive XYB planes of this scale, each
 //                      pixel converted once (scale 0 straight from the input)
-//   su2_scale_kernel   a few hundred blocks per image walk its 32 x 32 tiles:
+//   su2_scale_kernel   a few hundred blocks per image walk its 32 x 54 tiles:
 //                      the tile plus a 5-pixel halo of both images' XYB is
 //                      staged in shared memory (zero outside; the next tile
 //                      is copied by cp.async while this one is computed), the four groups
@@ -38,12 +38,16 @@
 
 namespace fab {
 
-constexpr int SU_W = 32, SU_H = 32, SU_R = 5;  // tile, blur radius
+constexpr int SU_W = 32, SU_H = 54, SU_R = 5;  // tile, blur radius
 constexpr int SU_BPI = 148 * 2;  // scale-kernel blocks of one launch at most
 constexpr int SU_T = 256;
 constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
-static_assert(SU_H / (SU_T / SU_W) == 4 && SU_W % 4 == 0, 
-              "the blur passes compute four outputs per item");
+// vertical pass: SU_VR adjacent rows per thread; the horizontal buffer has
+// rows for the last thread's whole window (the rows past the tile are zero)
+constexpr int SU_VR = (SU_H + SU_T / SU_W - 1) / (SU_T / SU_W);
+constexpr int SU_HBR = SU_VR * (SU_T / SU_W) + 2 * SU_R;
+// the horizontal pass is exactly two four-column items per thread
+static_assert(SU_IH * (SU_W / 4) == 2 * SU_T && SU_HBR >= SU_IH, "tile shape");
 constexpr int SU_SCALES = 6;
 constexpr int SU_SUMS = 18;  // 3 channels x {d, d^4, art, art^4, lost, lost^4}
 
@@ -256,44 +260,50 @@ template <> struct Pair<double> {
   static __device__ __forceinline__ void store2(V* p, V a, V b) { p[0] = a; p[1] = b; }
 };
 
-// One tile of (x1, x2) pairs plus its halo into shared memory by cp.async,
-// zero outside the image (a zero source size fills the destination with 0).
+// One channel of a tile of (x1, x2) pairs plus its halo into shared memory by
+// cp.async, zero outside the image (a zero source size fills with 0).
 template <typename V>
-__device__ __forceinline__ void su2_load_tile(V* dst, const V* src, long long plane, int h, int w,
-                                              int ox0, int oy0) {
+__device__ __forceinline__ void su2_load_plane(V* dst, const V* src, int h, int w, int ox0,
+                                               int oy0) {
   for (int i = threadIdx.x; i < SU_IH * SU_IW; i += SU_T) {
     const int r = i / SU_IW, c = i - r * SU_IW;
     const int gr = oy0 + r, gc = ox0 + c;
     const bool in = gr >= 0 && gr < h && gc >= 0 && gc < w;
-    const long long o = in ? (long long)gr * w + gc : 0;
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch) {
-      const unsigned d = smem_u32(dst + (ch * SU_IH + r) * SU_IW + c);
-      const V* g = src + ch * plane + o;
-      if constexpr (sizeof(V) == 16) {
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(g),
-                     "r"(in ? 16 : 0) : "memory");
-      } else {
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(g),
-                     "r"(in ? 8 : 0) : "memory");
-      }
+    const V* g = src + (in ? (long long)gr * w + gc : 0);
+    const unsigned d = smem_u32(dst + i);
+    if constexpr (sizeof(V) == 16) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(g),
+                   "r"(in ? 16 : 0) : "memory");
+    } else {
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(g),
+                   "r"(in ? 8 : 0) : "memory");
     }
   }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
-// One block per (strip of tiles, image): the block walks its image's 32 x 32
-// tiles with a stride, keeping the 18 per-channel sums in registers; each
-// thread computes four output rows of a tile.  The next tile is copied
-// (cp.async) into a second buffer while this one is computed.  The tile holds
-// (x1, x2) pairs per pixel and the horizontal pass (mu1, mu2) and
-// (x1^2 + x2^2, (x1 - x2)^2) pairs, so every tap is two packed FMAs.
 template <typename F>
-__global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const F* xyb) {
+__device__ __forceinline__ F su_div(F a, F b) {
+  if constexpr (sizeof(F) == 4) return __fdividef(a, b);  // within 2 ulp
+  else return a / b;
+}
+
+// One block per (strip of tiles, image): the block walks its image's 32 x 54
+// tiles with a stride, keeping the 18 per-channel sums in registers; each
+// thread computes seven output rows of a tile.  The tile buffer is a ring of
+// the three channel planes: as soon as channel c of this tile is done, channel
+// c of the block's next tile is copied (cp.async) into its slot, two channel
+// computations ahead of its use.  The tile holds (x1, x2) pairs per pixel and
+// the horizontal pass (mu1, mu2) and (x1^2 + x2^2, (x1 - x2)^2) pairs, so
+// every tap is two packed FMAs.
+template <typename F>
+__global__ void __launch_bounds__(SU_T)
+    su2_scale_kernel(const Su2Args p, const F* xyb) {
   using P = Pair<F>;
   using V = typename P::V;
   extern __shared__ __align__(16) unsigned char su_smem[];
-  V* tiles_buf = reinterpret_cast<V*>(su_smem);      // 2 x [3 ch][IH][IW] (x1, x2)
-  V* hb = tiles_buf + 2 * 3 * SU_IH * SU_IW;         // [IH][W][2]: (g0, g1), (g2, g3)
+  V* tile = reinterpret_cast<V*>(su_smem);    // [3 ch][IH][IW] (x1, x2)
+  V* hb = tile + 3 * SU_IH * SU_IW;           // [HBR][W][2]: (g0, g1), (g2, g3)
   __shared__ double s_red[32];
   __shared__ int s_flag;
   const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
@@ -309,29 +319,27 @@ __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const 
     ox0 = (tl % p.tiles_x) * SU_W - SU_R;
     oy0 = (tl / p.tiles_x) * SU_H - SU_R;
   };
-  if ((int)blockIdx.x < tiles) {
+  for (int i = SU_IH * SU_W * 2 + t; i < SU_HBR * SU_W * 2; i += SU_T) hb[i] = P::make(F(0), F(0));
+  if ((int)blockIdx.x >= tiles) goto reduce;
+  {
     int ox0, oy0;
     origin(blockIdx.x, ox0, oy0);
-    su2_load_tile(tiles_buf, src, plane, p.h, p.w, ox0, oy0);
+#pragma unroll 1
+    for (int ch = 0; ch < 3; ++ch)
+      su2_load_plane(tile + ch * SU_IH * SU_IW, src + ch * plane, p.h, p.w, ox0, oy0);
   }
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
-  int cur = 0;
-  for (int tl = blockIdx.x; tl < tiles; tl += gridDim.x, cur ^= 1) {
-    int ox0, oy0;
+  // one commit group per (tile, channel), in use order: before channel c of a
+  // tile is read, every group but the newest one has landed
+  asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+  __syncthreads();
+  for (int tl = blockIdx.x; tl < tiles; tl += gridDim.x) {
+    int ox0, oy0, nx0 = 0, ny0 = 0;
     origin(tl, ox0, oy0);
     const int nxt = tl + gridDim.x;
-    if (nxt < tiles) {  // the other buffer was last read before the previous barrier
-      int nx0, ny0;
-      origin(nxt, nx0, ny0);
-      su2_load_tile(tiles_buf + (cur ^ 1) * 3 * SU_IH * SU_IW, src, plane, p.h, p.w, nx0, ny0);
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-    asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // this tile has landed
-    __syncthreads();
-    const V* tile = tiles_buf + cur * 3 * SU_IH * SU_IW;
-#pragma unroll
+    if (nxt < tiles) origin(nxt, nx0, ny0);
+#pragma unroll 1
     for (int ch = 0; ch < 3; ++ch) {
-      const V* tc = tile + ch * SU_IH * SU_IW;
+      V* tc = tile + ch * SU_IH * SU_IW;
       // horizontal: four adjacent columns of one tile row per item, from a
       // 14-wide window of pairs; the squares of every input are formed once
       for (int i = t; i < SU_IH * (SU_W / 4); i += SU_T) {
@@ -366,18 +374,18 @@ __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const 
       }
       __syncthreads();
       {
-        // vertical: four adjacent rows of one column per thread, from a
-        // 14-high window of (mu, sq) pair couples
-        const int r0 = ty * (SU_H / (SU_T / SU_W));
-        V m[4], q[4];
+        // vertical: SU_VR adjacent rows of one column per thread, from a
+        // (SU_VR + 10)-high window of (mu, sq) pair couples
+        const int r0 = ty * SU_VR;
+        V m[SU_VR], q[SU_VR];
 #pragma unroll
-        for (int o = 0; o < 4; ++o) m[o] = q[o] = P::make(F(0), F(0));
+        for (int o = 0; o < SU_VR; ++o) m[o] = q[o] = P::make(F(0), F(0));
 #pragma unroll
-        for (int j = 0; j < 2 * SU_R + 4; ++j) {
+        for (int j = 0; j < 2 * SU_R + SU_VR; ++j) {
           V a, b2;
           P::load2(hb + ((r0 + j) * SU_W + tx) * 2, a, b2);
 #pragma unroll
-          for (int o = 0; o < 4; ++o) {
+          for (int o = 0; o < SU_VR; ++o) {
             const int k = j - o;
             if (k >= 0 && k < 2 * SU_R + 1) {
               const V w = P::make(F(p.taps[k]), F(p.taps[k]));
@@ -387,11 +395,12 @@ __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const 
           }
         }
         const int gx = ox0 + SU_R + tx;
+        F ls[6] = {F(0), F(0), F(0), F(0), F(0), F(0)};
 #pragma unroll
-        for (int o = 0; o < 4; ++o) {
+        for (int o = 0; o < SU_VR; ++o) {
           const int rr = r0 + o;
           const int gy = oy0 + SU_R + rr;
-          if (gy >= p.h || gx >= p.w) continue;
+          if (rr >= SU_H || gy >= p.h || gx >= p.w) continue;
           const F m1 = m[o].x, m2 = m[o].y, sp = q[o].x, sd = q[o].y;
           const V xc = tc[(rr + SU_R) * SU_IW + tx + SU_R];
           const F x1 = xc.x, x2 = xc.y;
@@ -401,23 +410,37 @@ __global__ void __launch_bounds__(SU_T) su2_scale_kernel(const Su2Args p, const 
           const F qq = (m1 - m2) * (m1 - m2);
           const F den_s = (sp - (m1 * m1 + m2 * m2)) + F(0.0009);
           const F num_s = (den_s - sd) + qq;
-          F d = ((sd - qq) + qq * num_s) / den_s;
+          F d = su_div((sd - qq) + qq * num_s, den_s);
           d = d > F(0) ? d : F(0);
           const F e1 = fabs(x1 - m1), e2 = fabs(x2 - m2);
-          const F e = (e2 - e1) / (F(1) + e1);
+          const F e = su_div(e2 - e1, F(1) + e1);
           const F art = e > F(0) ? e : F(0), lost = e < F(0) ? -e : F(0);
           const F v[3] = {d, art, lost};
 #pragma unroll
           for (int k = 0; k < 3; ++k) {
             const F sq = v[k] * v[k];
-            sums[ch * 6 + 2 * k] += (double)v[k];
-            sums[ch * 6 + 2 * k + 1] += (double)(sq * sq);
+            ls[2 * k] += v[k];
+            ls[2 * k + 1] += sq * sq;
           }
         }
+        // the thread's four pixels, summed in F, join the double sums: the
+        // channel index is uniform here, so the sums stay in registers
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          if (c == ch) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) sums[c * 6 + k] += (double)ls[k];
+          }
       }
-      __syncthreads();  // hb is rewritten for the next channel
+      // the next channel has landed, and every thread is done with hb and
+      // with this channel's slot
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+      __syncthreads();
+      if (nxt < tiles) su2_load_plane(tc, src + ch * plane, p.h, p.w, nx0, ny0);
+      else asm volatile("cp.async.commit_group;\n" ::: "memory");
     }
   }
+reduce:
   // this block's sums -> partials [N][blocks][18]
   const long long pidx = ((long long)n * gridDim.x + blockIdx.x) * SU_SUMS;
 #pragma unroll
@@ -573,8 +596,8 @@ template <typename T, typename F>
 static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score& sc_in,
                    int device, cudaStream_t st) {
   static bool done[64] = {false};
-  // two tiles of (x1, x2) pairs and the horizontal pairs
-  const size_t smem = sizeof(F) * (2 * 2 * 3 * SU_IH * SU_IW + 4 * SU_IH * SU_W);
+  // one tile of (x1, x2) pairs and the horizontal pairs
+  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_HBR * SU_W);
   FAB_TRY(ensure_smem(su2_scale_kernel<F>, smem, device, done));
   const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
   F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
