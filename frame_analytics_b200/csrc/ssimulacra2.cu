@@ -152,6 +152,16 @@ __global__ void __launch_bounds__(256) su2_down_kernel(const Su2Args p, int ph, 
   }
 }
 
+// One pixel's XYB of both images as (x1, x2) pairs in the three planes.
+template <typename F>
+__device__ __forceinline__ void su2_store_xyb(F* out, long long plane, const F* X, const F* Y,
+                                              const F* B) {
+  using V = std::conditional_t<sizeof(F) == 4, float2, double2>;
+  *reinterpret_cast<V*>(out) = V{X[0], X[1]};
+  *reinterpret_cast<V*>(out + 2 * plane) = V{Y[0], Y[1]};
+  *reinterpret_cast<V*>(out + 4 * plane) = V{B[0], B[1]};
+}
+
 // Positive XYB planes of both images at this scale: [N][3][h][w] of (x, y)
 // pairs, the layout the scale kernel stages tiles from.
 template <typename T, typename F>
@@ -162,18 +172,15 @@ __global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
     const int n = (int)(i / plane);
     const long long o = i - (long long)n * plane;
     const int r = (int)(o / p.w), col = (int)(o - (long long)r * p.w);
+    F X[2], Y[2], Bc[2];
 #pragma unroll
     for (int img = 0; img < 2; ++img) {
       const F R = su_linear<T, F>(p, img, n, 0, r, col);
       const F G = su_linear<T, F>(p, img, n, 1, r, col);
       const F B = su_linear<T, F>(p, img, n, 2, r, col);
-      F X, Y, Bc;
-      to_xyb<F>(p, R, G, B, X, Y, Bc);
-      F* out = xyb + ((long long)n * 3 * plane + o) * 2 + img;
-      out[0] = X;
-      out[2 * plane] = Y;
-      out[4 * plane] = Bc;
+      to_xyb<F>(p, R, G, B, X[img], Y[img], Bc[img]);
     }
+    su2_store_xyb(xyb + ((long long)n * 3 * plane + o) * 2, plane, X, Y, Bc);
   }
 }
 
@@ -198,37 +205,56 @@ __global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, 
     const int n = (int)(i / plane1);
     const long long o1 = i - (long long)n * plane1;
     const int br = (int)(o1 / w1), bc = (int)(o1 - (long long)br * w1);
+    F acc[2][3] = {{F(0), F(0), F(0)}, {F(0), F(0), F(0)}};
+    const int c0 = 2 * bc, c1 = min(2 * bc + 1, p.w - 1);
 #pragma unroll
-    for (int img = 0; img < 2; ++img) {
-      const char* base = img ? p.y : p.x;
-      F acc[3] = {F(0), F(0), F(0)};
+    for (int dr = 0; dr < 2; ++dr) {
+      const int r = min(2 * br + dr, p.h - 1);
+      F rgb[2][2][3];  // [image][column][channel]
 #pragma unroll
-      for (int dr = 0; dr < 2; ++dr)
+      for (int img = 0; img < 2; ++img) {
+        const char* base = img ? p.y : p.x;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          const long long off = (long long)n * p.sn + (long long)c * p.sc + (long long)r * p.sh + c0;
+          if constexpr (LUT) {
+            const unsigned char* b8 = reinterpret_cast<const unsigned char*>(base) + off;
+            unsigned v0, v1;
+            if (c1 > c0 && (reinterpret_cast<size_t>(b8) & 1) == 0) {  // one 16-bit load
+              const unsigned v = ldro(reinterpret_cast<const unsigned short*>(b8));
+              v0 = v & 0xffu;
+              v1 = v >> 8;
+            } else {
+              v0 = b8[0];
+              v1 = b8[c1 - c0];
+            }
+            rgb[img][0][c] = s_lut[v0];
+            rgb[img][1][c] = s_lut[v1];
+          } else {
+            rgb[img][0][c] = srgb_to_linear<F>(F(su_raw<T>(base, off)) * F(p.inv_range));
+            rgb[img][1][c] = srgb_to_linear<F>(F(su_raw<T>(base, off + (c1 - c0))) * F(p.inv_range));
+          }
+          acc[img][c] += rgb[img][0][c] + rgb[img][1][c];
+        }
+      }
+      if (2 * br + dr < p.h) {
 #pragma unroll
         for (int dc = 0; dc < 2; ++dc) {
-          const int r = min(2 * br + dr, p.h - 1), col = min(2 * bc + dc, p.w - 1);
-          F rgb[3];
+          if (2 * bc + dc >= p.w) continue;
+          F X[2], Y[2], B[2];
 #pragma unroll
-          for (int c = 0; c < 3; ++c) {
-            const long long off = (long long)n * p.sn + (long long)c * p.sc + (long long)r * p.sh + col;
-            if constexpr (LUT) rgb[c] = s_lut[reinterpret_cast<const unsigned char*>(base)[off]];
-            else rgb[c] = srgb_to_linear<F>(F(su_raw<T>(base, off)) * F(p.inv_range));
-            acc[c] += rgb[c];
-          }
-          if (2 * br + dr < p.h && 2 * bc + dc < p.w) {
-            F X, Y, B;
-            to_xyb<F>(p, rgb[0], rgb[1], rgb[2], X, Y, B);
-            F* out = xyb + ((long long)n * 3 * plane + (long long)r * p.w + col) * 2 + img;
-            out[0] = X;
-            out[2 * plane] = Y;
-            out[4 * plane] = B;
-          }
+          for (int img = 0; img < 2; ++img)
+            to_xyb<F>(p, rgb[img][dc][0], rgb[img][dc][1], rgb[img][dc][2], X[img], Y[img], B[img]);
+          su2_store_xyb(xyb + ((long long)n * 3 * plane + (long long)r * p.w + c0 + dc) * 2, plane,
+                        X, Y, B);
         }
-      F* l1 = img ? lin1y : lin1x;
-      if (l1) {
+      }
+    }
+    if (lin1x) {
 #pragma unroll
-        for (int c = 0; c < 3; ++c)
-          l1[((long long)n * 3 + c) * plane1 + o1] = F(0.25) * acc[c];
+      for (int c = 0; c < 3; ++c) {
+        lin1x[((long long)n * 3 + c) * plane1 + o1] = F(0.25) * acc[0][c];
+        lin1y[((long long)n * 3 + c) * plane1 + o1] = F(0.25) * acc[1][c];
       }
     }
   }
