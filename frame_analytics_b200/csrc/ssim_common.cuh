@@ -511,6 +511,11 @@ static cudaError_t ensure_smem(K* kern, size_t bytes, int device, bool (&done)[6
 // multiples of 16 bytes, or no driver entry point); callers then stage with
 // register loads.
 bool make_row_map(CUtensorMap* map, const View& v, int dtype, int box_w, int* d);
+// A 3-D map of 8-byte units {d0, d1, d2} with byte strides s1, s2 (multiples
+// of 16) and box {b0, b1, 1}; elements outside the dims read as zero.
+bool make_map_3d_u64(CUtensorMap* map, const void* base, unsigned long long d0,
+                     unsigned long long d1, unsigned long long d2, unsigned long long s1,
+                     unsigned long long s2, int b0, int b1);
 
 struct SsimPlan {
   int strips, chunks, RH;

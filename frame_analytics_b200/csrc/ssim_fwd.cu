@@ -122,6 +122,22 @@ bool make_row_map(CUtensorMap* map, const View& v, int dtype, int box_w, int* d)
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_3d_u64(CUtensorMap* map, const void* base, unsigned long long d0,
+                     unsigned long long d1, unsigned long long d2, unsigned long long s1,
+                     unsigned long long s2, int b0, int b1) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || reinterpret_cast<uintptr_t>(base) % 16 || s1 % 16 || s2 % 16) return false;
+  if (b0 <= 0 || b0 > 256 || b1 <= 0 || b1 > 256 || (b0 * 8) % 16) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <int KW>
 static int box_width(int dtype) {
   switch (dtype) {

@@ -42,6 +42,9 @@ constexpr int SU_W = 32, SU_H = 54, SU_R = 5;  // tile, blur radius
 constexpr int SU_BPI = 148 * 2;  // scale-kernel blocks of one launch at most
 constexpr int SU_T = 256;
 constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
+// staged tile row: one pair more on the left, so that the TMA box starts at an
+// even column (16-byte x coordinate), and one more on the right
+constexpr int SU_TW = SU_IW + 2;
 // vertical pass: SU_VR adjacent rows per thread; the horizontal buffer has
 // rows for the last thread's whole window (the rows past the tile are zero)
 constexpr int SU_VR = (SU_H + SU_T / SU_W - 1) / (SU_T / SU_W);
@@ -67,6 +70,10 @@ struct Su2Args {
   double mat[9];  // opsin absorbance matrix, row-major
   double bias, cbrt_bias;
   int tiles_x, tiles_y;
+  int pitch;         // XYB row pitch in pixels (even: 16-byte TMA strides)
+  unsigned int* err; // error word of the bounded waits
+  CUtensorMap tm;    // XYB pair planes of this scale as 8-byte units:
+                     // {w * units per pair, h, N * 3}
   unsigned int* counter;
   double* part;   // [N][tiles][18]
   double* norms;  // [N][6 scales][18]
@@ -162,11 +169,11 @@ __device__ __forceinline__ void su2_store_xyb(F* out, long long plane, const F* 
   *reinterpret_cast<V*>(out + 4 * plane) = V{B[0], B[1]};
 }
 
-// Positive XYB planes of both images at this scale: [N][3][h][w] of (x, y)
-// pairs, the layout the scale kernel stages tiles from.
+// Positive XYB planes of both images at this scale: [N][3][h][pitch] of
+// (x, y) pairs, the layout the scale kernel stages tiles from.
 template <typename T, typename F>
 __global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
-  const long long plane = (long long)p.h * p.w;
+  const long long plane = (long long)p.h * p.w, pp = (long long)p.h * p.pitch;
   const long long npx = (long long)p.N * plane;
   for (long long i = blockIdx.x * 256LL + threadIdx.x; i < npx; i += 256LL * gridDim.x) {
     const int n = (int)(i / plane);
@@ -180,7 +187,7 @@ __global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
       const F B = su_linear<T, F>(p, img, n, 2, r, col);
       to_xyb<F>(p, R, G, B, X[img], Y[img], Bc[img]);
     }
-    su2_store_xyb(xyb + ((long long)n * 3 * plane + o) * 2, plane, X, Y, Bc);
+    su2_store_xyb(xyb + ((long long)n * 3 * pp + (long long)r * p.pitch + col) * 2, pp, X, Y, Bc);
   }
 }
 
@@ -199,7 +206,7 @@ __global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, 
       s_lut[i] = srgb_to_linear<F>(F((double)i) * F(p.inv_range));
     __syncthreads();
   }
-  const long long plane = (long long)p.h * p.w, plane1 = (long long)h1 * w1;
+  const long long pp = (long long)p.h * p.pitch, plane1 = (long long)h1 * w1;
   const long long nblk = (long long)p.N * plane1;
   for (long long i = blockIdx.x * 256LL + threadIdx.x; i < nblk; i += 256LL * gridDim.x) {
     const int n = (int)(i / plane1);
@@ -245,7 +252,7 @@ __global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, 
 #pragma unroll
           for (int img = 0; img < 2; ++img)
             to_xyb<F>(p, rgb[img][dc][0], rgb[img][dc][1], rgb[img][dc][2], X[img], Y[img], B[img]);
-          su2_store_xyb(xyb + ((long long)n * 3 * plane + (long long)r * p.w + c0 + dc) * 2, plane,
+          su2_store_xyb(xyb + ((long long)n * 3 * pp + (long long)r * p.pitch + c0 + dc) * 2, pp,
                         X, Y, B);
         }
       }
@@ -286,26 +293,19 @@ template <> struct Pair<double> {
   static __device__ __forceinline__ void store2(V* p, V a, V b) { p[0] = a; p[1] = b; }
 };
 
-// One channel of a tile of (x1, x2) pairs plus its halo into shared memory by
-// cp.async, zero outside the image (a zero source size fills with 0).
-template <typename V>
-__device__ __forceinline__ void su2_load_plane(V* dst, const V* src, int h, int w, int ox0,
-                                               int oy0) {
-  for (int i = threadIdx.x; i < SU_IH * SU_IW; i += SU_T) {
-    const int r = i / SU_IW, c = i - r * SU_IW;
-    const int gr = oy0 + r, gc = ox0 + c;
-    const bool in = gr >= 0 && gr < h && gc >= 0 && gc < w;
-    const V* g = src + (in ? (long long)gr * w + gc : 0);
-    const unsigned d = smem_u32(dst + i);
-    if constexpr (sizeof(V) == 16) {
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(g),
-                   "r"(in ? 16 : 0) : "memory");
-    } else {
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(g),
-                   "r"(in ? 8 : 0) : "memory");
-    }
-  }
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
+// One channel of a tile of (x1, x2) pairs plus its halo into shared memory:
+// one TMA box {SU_TW pairs, SU_IH rows, 1 plane} whose x coordinate is the
+// tile's first halo column minus one (an even pixel: a 16-byte boundary);
+// rows and columns outside the image arrive as zeros.
+__device__ __forceinline__ void su2_tma_plane(void* dst, const CUtensorMap* map, int x, int y,
+                                              int z, unsigned long long* bar, unsigned bytes) {
+  fence_async_smem();  // the slot's earlier generic reads come first
+  mbar_expect_tx(bar, bytes);
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<unsigned long long>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
 }
 
 template <typename F>
@@ -317,70 +317,77 @@ __device__ __forceinline__ F su_div(F a, F b) {
 // One block per (strip of tiles, image): the block walks its image's 32 x 54
 // tiles with a stride, keeping the 18 per-channel sums in registers; each
 // thread computes seven output rows of a tile.  The tile buffer is a ring of
-// the three channel planes: as soon as channel c of this tile is done, channel
-// c of the block's next tile is copied (cp.async) into its slot, two channel
-// computations ahead of its use.  The tile holds (x1, x2) pairs per pixel and
-// the horizontal pass (mu1, mu2) and (x1^2 + x2^2, (x1 - x2)^2) pairs, so
-// every tap is two packed FMAs.
+// the three channel planes: as soon as channel c of this tile is done, thread
+// 0 has TMA copy channel c of the block's next tile into its slot, two
+// channel computations ahead of its use.  The tile holds (x1, x2) pairs per
+// pixel and the horizontal pass (mu1, mu2) and (x1^2 + x2^2, (x1 - x2)^2)
+// pairs, so every tap is two packed FMAs.
 template <typename F>
 __global__ void __launch_bounds__(SU_T)
-    su2_scale_kernel(const Su2Args p, const F* xyb) {
+    su2_scale_kernel(const __grid_constant__ Su2Args p) {
   using P = Pair<F>;
   using V = typename P::V;
-  extern __shared__ __align__(16) unsigned char su_smem[];
-  V* tile = reinterpret_cast<V*>(su_smem);    // [3 ch][IH][IW] (x1, x2)
-  V* hb = tile + 3 * SU_IH * SU_IW;           // [HBR][W][2]: (g0, g1), (g2, g3)
+  constexpr int U = sizeof(V) / 8;                  // 8-byte map units per pair
+  constexpr unsigned kPlaneBytes = SU_IH * SU_TW * sizeof(V);
+  extern __shared__ __align__(128) unsigned char su_smem[];
+  V* tile = reinterpret_cast<V*>(su_smem);    // [3 ch][IH][TW] (x1, x2)
+  V* hb = tile + 3 * SU_IH * SU_TW;           // [HBR][W][2]: (g0, g1), (g2, g3)
   __shared__ double s_red[32];
   __shared__ int s_flag;
+  __shared__ __align__(8) unsigned long long s_bar[3];
   const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
   const int n = blockIdx.y;
-  const long long plane = (long long)p.h * p.w;
-  const V* src = reinterpret_cast<const V*>(xyb) + (long long)n * 3 * plane;
   const int tiles = p.tiles_x * p.tiles_y;
   double sums[SU_SUMS];
 #pragma unroll
   for (int k = 0; k < SU_SUMS; ++k) sums[k] = 0.0;
 
+  // tile origin: its first halo column and row
   auto origin = [&](int tl, int& ox0, int& oy0) {
     ox0 = (tl % p.tiles_x) * SU_W - SU_R;
     oy0 = (tl / p.tiles_x) * SU_H - SU_R;
   };
-  for (int i = SU_IH * SU_W * 2 + t; i < SU_HBR * SU_W * 2; i += SU_T) hb[i] = P::make(F(0), F(0));
-  if ((int)blockIdx.x >= tiles) goto reduce;
-  {
+  auto issue = [&](int tl, int ch) {
     int ox0, oy0;
-    origin(blockIdx.x, ox0, oy0);
-#pragma unroll 1
-    for (int ch = 0; ch < 3; ++ch)
-      su2_load_plane(tile + ch * SU_IH * SU_IW, src + ch * plane, p.h, p.w, ox0, oy0);
+    origin(tl, ox0, oy0);
+    su2_tma_plane(tile + ch * SU_IH * SU_TW, &p.tm, (ox0 - 1) * U, oy0, n * 3 + ch, &s_bar[ch],
+                  kPlaneBytes);
+  };
+  for (int i = SU_IH * SU_W * 2 + t; i < SU_HBR * SU_W * 2; i += SU_T) hb[i] = P::make(F(0), F(0));
+  if (t == 0) {
+    for (int ch = 0; ch < 3; ++ch) mbar_init(&s_bar[ch], 1);
   }
-  // one commit group per (tile, channel), in use order: before channel c of a
-  // tile is read, every group but the newest one has landed
-  asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+  fence_async_smem();
   __syncthreads();
-  for (int tl = blockIdx.x; tl < tiles; tl += gridDim.x) {
-    int ox0, oy0, nx0 = 0, ny0 = 0;
+  if ((int)blockIdx.x >= tiles) goto reduce;
+  if (t == 0) {
+    for (int ch = 0; ch < 3; ++ch) issue(blockIdx.x, ch);
+  }
+  for (int tl = blockIdx.x, k = 0; tl < tiles; tl += gridDim.x, ++k) {
+    int ox0, oy0;
     origin(tl, ox0, oy0);
     const int nxt = tl + gridDim.x;
-    if (nxt < tiles) origin(nxt, nx0, ny0);
 #pragma unroll 1
     for (int ch = 0; ch < 3; ++ch) {
-      V* tc = tile + ch * SU_IH * SU_IW;
+      // pair (r, c) of the tile with its halo sits at tc[r * SU_TW + c + 1]
+      const V* tc = tile + ch * SU_IH * SU_TW;
+      mbar_wait(&s_bar[ch], k & 1, p.err);
       // horizontal: four adjacent columns of one tile row per item, from a
       // 14-wide window of pairs; the squares of every input are formed once
       for (int i = t; i < SU_IH * (SU_W / 4); i += SU_T) {
         const int r = i / (SU_W / 4), c0 = (i - r * (SU_W / 4)) * 4;
-        const V* row = tc + r * SU_IW + c0;
+        const V* row = tc + r * SU_TW + c0;  // 16-byte aligned; the window is row[1..14]
         V m[4], q[4];
 #pragma unroll
         for (int o = 0; o < 4; ++o) m[o] = q[o] = P::make(F(0), F(0));
 #pragma unroll
-        for (int j2 = 0; j2 < 7; ++j2) {
+        for (int j2 = 0; j2 < 8; ++j2) {
           V uu[2];
           P::load2(row + 2 * j2, uu[0], uu[1]);
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int j = 2 * j2 + e;
+            const int j = 2 * j2 + e - 1;
+            if (j < 0 || j >= 2 * SU_R + 4) continue;
             const V u = uu[e];
             const F d = u.x - u.y;
             const V sq = P::make(u.x * u.x + u.y * u.y, d * d);
@@ -428,7 +435,7 @@ __global__ void __launch_bounds__(SU_T)
           const int gy = oy0 + SU_R + rr;
           if (rr >= SU_H || gy >= p.h || gx >= p.w) continue;
           const F m1 = m[o].x, m2 = m[o].y, sp = q[o].x, sd = q[o].y;
-          const V xc = tc[(rr + SU_R) * SU_IW + tx + SU_R];
+          const V xc = tc[(rr + SU_R) * SU_TW + tx + SU_R + 1];
           const F x1 = xc.x, x2 = xc.y;
           // 1 - (1 - q) num_s / den_s rewritten as ((sd - q) + q num_s) / den_s:
           // the same value, exactly 0 on an identical pair
@@ -458,12 +465,8 @@ __global__ void __launch_bounds__(SU_T)
             for (int k = 0; k < 6; ++k) sums[c * 6 + k] += (double)ls[k];
           }
       }
-      // the next channel has landed, and every thread is done with hb and
-      // with this channel's slot
-      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-      __syncthreads();
-      if (nxt < tiles) su2_load_plane(tc, src + ch * plane, p.h, p.w, nx0, ny0);
-      else asm volatile("cp.async.commit_group;\n" ::: "memory");
+      __syncthreads();  // every thread is done with hb and with this channel's slot
+      if (t == 0 && nxt < tiles) issue(nxt, ch);
     }
   }
 reduce:
@@ -567,7 +570,7 @@ static Su2Plan su2_plan(int N, int H, int W) {
   const size_t s1 = pl.scales > 1 ? (size_t)N * 3 * pl.h[1] * pl.w[1] : 0;
   const size_t s2 = pl.scales > 2 ? (size_t)N * 3 * pl.h[2] * pl.w[2] : 0;
   pl.lin_elems = s1 + s2;
-  pl.xyb_elems = (size_t)2 * N * 3 * H * W;
+  pl.xyb_elems = (size_t)2 * N * 3 * H * ((W + 1) & ~1);  // even row pitch
   return pl;
 }
 
@@ -623,7 +626,7 @@ static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score
                    int device, cudaStream_t st) {
   static bool done[64] = {false};
   // one tile of (x1, x2) pairs and the horizontal pairs
-  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_IW + 4 * SU_HBR * SU_W);
+  const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_TW + 4 * SU_HBR * SU_W);
   FAB_TRY(ensure_smem(su2_scale_kernel<F>, smem, device, done));
   const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
   F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
@@ -632,6 +635,7 @@ static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score
     p.scale = s;
     p.h = pl.h[s];
     p.w = pl.w[s];
+    p.pitch = (p.w + 1) & ~1;
     if (s == 0) {
       // XYB of scale 0 and, in the same pass, scale 1's linear planes
       const int h1 = pl.scales > 1 ? pl.h[1] : (p.h + 1) / 2;
@@ -665,8 +669,12 @@ static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score
     }
     p.tiles_x = (p.w + SU_W - 1) / SU_W;
     p.tiles_y = (p.h + SU_H - 1) / SU_H;
+    constexpr int U = 2 * (int)sizeof(F) / 8;  // 8-byte units per pair
+    if (!make_map_3d_u64(&p.tm, xyb, (unsigned long long)p.w * U, p.h, 3ULL * p.N,
+                         8ULL * U * p.pitch, 8ULL * U * p.pitch * p.h, SU_TW * U, SU_IH))
+      return FA_E_INTERNAL;
     dim3 grid(pl.bpi[s], p.N);
-    su2_scale_kernel<F><<<grid, SU_T, smem, st>>>(p, xyb);
+    su2_scale_kernel<F><<<grid, SU_T, smem, st>>>(p);
     FAB_LAUNCH_CHECK();
   }
   Su2Score sc = sc_in;
@@ -695,6 +703,7 @@ int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64
   p.sn = x.sn; p.sc = x.sc; p.sh = x.sh;
   p.inv_range = 1.0 / data_range;
   p.N = x.n;
+  p.err = wait_error_word();
   su2_taps(p.taps);
   const double M[9] = {0.30, 1.0 - 0.078 - 0.30, 0.078,
                        0.23, 1.0 - 0.078 - 0.23, 0.078,
