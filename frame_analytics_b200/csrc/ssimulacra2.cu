@@ -16,18 +16,21 @@
 //   score        108 weighted |norms|, a cubic and a power law
 //
 // Kernels (compute type F = float, the reference's default, or double):
-//   su2_down_kernel    the next scale's linear planes (from the input at
-//                      scale 1, from the previous linear planes after that)
-//   su2_xyb_kernel     both images' positive XYB planes of this scale, each
-//                      pixel converted once (scale 0 straight from the input)
-//   su2_scale_kernel   a few hundred blocks per image walk its 32 x 54 tiles:
-//                      the tile plus a 5-pixel halo of both images' XYB is
-//                      staged in shared memory (zero outside; the next tile
-//                      is copied by cp.async while this one is computed), the four groups
-//                      are blurred separably per channel, the maps are formed
-//                      and the 18 per-channel sums kept in registers; the last
-//                      block of the launch turns each image's sums into its
-//                      18 norms, one warp per (image, sum)
+//   su2_xyb0_kernel    one pass over the input: scale 0's XYB of both images,
+//                      and from each 2 x 2 block's mean linear RGB scale 1's
+//                      XYB (and its linear planes when scale 2 needs them)
+//   su2_down_kernel    scales 2..5: the 2 x 2 mean of the previous scale's
+//                      linear planes, written as this scale's XYB (and linear
+//                      planes when a later scale needs them)
+//   su2_scale_kernel   one launch over every scale: blocks walk 32 x 54
+//                      tiles; each channel of a tile plus a 5-pixel halo of
+//                      both images' XYB is staged in shared memory by TMA
+//                      (zero outside the image; the next tile's channel is in
+//                      flight while this one is computed), the four groups
+//                      are blurred separably, the maps are formed and the 18
+//                      per-channel sums kept in registers; the last block of
+//                      each scale turns each image's sums into its 18 norms,
+//                      one warp per (image, sum)
 //   su2_score_kernel   the weighted sum and the final mapping, per image and
 //                      for the batch
 // Every sum is double.
@@ -39,7 +42,7 @@
 namespace fab {
 
 constexpr int SU_W = 32, SU_H = 54, SU_R = 5;  // tile, blur radius
-constexpr int SU_BPI = 148 * 2;  // scale-kernel blocks of one launch at most
+constexpr int SU_BPI = 148 * 2;  // scale-kernel blocks of the launch, about
 constexpr int SU_T = 256;
 constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
 // staged tile row: one pair more on the left, so that the TMA box starts at an
@@ -54,6 +57,7 @@ static_assert(SU_IH * (SU_W / 4) == 2 * SU_T && SU_HBR >= SU_IH, "tile shape");
 constexpr int SU_SCALES = 6;
 constexpr int SU_SUMS = 18;  // 3 channels x {d, d^4, art, art^4, lost, lost^4}
 
+// Arguments of the converters (input -> linear RGB -> XYB, and the pyramid).
 struct Su2Args {
   // scale-0 input (any dtype and strides; channel stride 0 replicates gray)
   const char* x;
@@ -61,21 +65,25 @@ struct Su2Args {
   int dtype;
   long long sn, sc, sh;
   double inv_range;
-  // linear planes of this scale (scale > 0): [N][3][h][w]
-  const void* lx;
-  const void* ly;
-  int N, h, w;  // this scale's size
-  int scale;
-  double taps[2 * SU_R + 1];
+  int N, h, w;    // size of the scale being written
+  int pitch;      // its XYB row pitch in pixels (even: 16-byte TMA strides)
   double mat[9];  // opsin absorbance matrix, row-major
   double bias, cbrt_bias;
-  int tiles_x, tiles_y;
-  int pitch;         // XYB row pitch in pixels (even: 16-byte TMA strides)
-  unsigned int* err; // error word of the bounded waits
-  CUtensorMap tm;    // XYB pair planes of this scale as 8-byte units:
-                     // {w * units per pair, h, N * 3}
-  unsigned int* counter;
-  double* part;   // [N][tiles][18]
+};
+
+// Arguments of the one scale-kernel launch that covers every scale: blocks
+// [start[s], start[s + 1]) work on scale s, bpi[s] per image.
+struct Su2Tiles {
+  CUtensorMap tm[SU_SCALES];  // XYB pair planes of each scale as 8-byte units:
+                              // {w * units per pair, h, N * 3}
+  double taps[2 * SU_R + 1];
+  int scales, N;
+  int h[SU_SCALES], w[SU_SCALES], tiles_x[SU_SCALES], bpi[SU_SCALES];
+  int start[SU_SCALES + 1];
+  long long part_off[SU_SCALES];  // of each scale's [N][bpi][18] partials
+  unsigned int* err;              // error word of the bounded waits
+  unsigned int* counter;          // one per scale
+  double* part;
   double* norms;  // [N][6 scales][18]
 };
 
@@ -91,23 +99,6 @@ __device__ __forceinline__ F srgb_to_linear(F v) {
   b = b > F(0) ? b : F(0);
   if constexpr (sizeof(F) == 4) return powf(b, 2.4f);
   else return pow(b, 2.4);
-}
-
-template <typename T, typename F>
-__device__ __forceinline__ F su_input_linear(const Su2Args& p, const char* base, int n, int c,
-                                             int r, int col) {
-  const long long o = (long long)n * p.sn + (long long)c * p.sc + (long long)r * p.sh + col;
-  return srgb_to_linear<F>(F(su_raw<T>(base, o)) * F(p.inv_range));
-}
-
-// Linear RGB of (n, c, r, col) at this scale: from the input (scale 0) or the
-// linear planes.
-template <typename T, typename F>
-__device__ __forceinline__ F su_linear(const Su2Args& p, bool second, int n, int c, int r,
-                                       int col) {
-  if (p.scale == 0) return su_input_linear<T, F>(p, second ? p.y : p.x, n, c, r, col);
-  const F* l = static_cast<const F*>(second ? p.ly : p.lx);
-  return l[(((long long)n * 3 + c) * p.h + r) * p.w + col];
 }
 
 template <typename F>
@@ -126,39 +117,6 @@ __device__ __forceinline__ void to_xyb(const Su2Args& p, F r, F g, F b, F& X, F&
   B = (m[2] - yy) + F(0.55);
 }
 
-// 2x2 box mean, source index clamped to the edge.  SRC_INPUT: the scale-0
-// input (EOTF applied per sample first); else the previous linear planes of
-// size (ph, pw).
-template <typename T, typename F, bool SRC_INPUT>
-__global__ void __launch_bounds__(256) su2_down_kernel(const Su2Args p, int ph, int pw, F* ox,
-                                                       F* oy) {
-  const long long n_out = (long long)p.N * 3 * p.h * p.w;
-  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n_out; i += 256LL * gridDim.x) {
-    const int col = (int)(i % p.w), r = (int)((i / p.w) % p.h);
-    const int c = (int)((i / ((long long)p.w * p.h)) % 3), n = (int)(i / (3LL * p.w * p.h));
-    const int r0 = min(2 * r, ph - 1), r1 = min(2 * r + 1, ph - 1);
-    const int c0 = min(2 * col, pw - 1), c1 = min(2 * col + 1, pw - 1);
-#pragma unroll
-    for (int img = 0; img < 2; ++img) {
-      F a, b, cc, d;
-      if constexpr (SRC_INPUT) {
-        const char* base = img ? p.y : p.x;
-        a = su_input_linear<T, F>(p, base, n, c, r0, c0);
-        b = su_input_linear<T, F>(p, base, n, c, r0, c1);
-        cc = su_input_linear<T, F>(p, base, n, c, r1, c0);
-        d = su_input_linear<T, F>(p, base, n, c, r1, c1);
-      } else {
-        const F* l = static_cast<const F*>(img ? p.ly : p.lx) + ((long long)n * 3 + c) * ph * pw;
-        a = l[(long long)r0 * pw + c0];
-        b = l[(long long)r0 * pw + c1];
-        cc = l[(long long)r1 * pw + c0];
-        d = l[(long long)r1 * pw + c1];
-      }
-      (img ? oy : ox)[i] = F(0.25) * (((a + b) + cc) + d);
-    }
-  }
-}
-
 // One pixel's XYB of both images as (x1, x2) pairs in the three planes.
 template <typename F>
 __device__ __forceinline__ void su2_store_xyb(F* out, long long plane, const F* X, const F* Y,
@@ -169,36 +127,63 @@ __device__ __forceinline__ void su2_store_xyb(F* out, long long plane, const F* 
   *reinterpret_cast<V*>(out + 4 * plane) = V{B[0], B[1]};
 }
 
-// Positive XYB planes of both images at this scale: [N][3][h][pitch] of
-// (x, y) pairs, the layout the scale kernel stages tiles from.
-template <typename T, typename F>
-__global__ void __launch_bounds__(256) su2_xyb_kernel(const Su2Args p, F* xyb) {
+// XYB planes of both images at one scale: [N][3][h][pitch] of (x1, x2)
+// pairs, the layout the scale kernel stages tiles from.
+
+// Scales 2..5: each thread takes one pixel of the scale: the 2x2 box mean of
+// the previous scale's linear planes (size ph x pw, source index clamped to
+// the edge, so an odd last row / column is averaged with itself), written as
+// this scale's linear planes when a later scale needs them (lx / ly may be
+// null) and as this scale's XYB.
+template <typename F>
+__global__ void __launch_bounds__(256) su2_down_kernel(const Su2Args p, const F* __restrict__ px,
+                                                       const F* __restrict__ py, int ph, int pw,
+                                                       F* lx, F* ly, F* xyb) {
   const long long plane = (long long)p.h * p.w, pp = (long long)p.h * p.pitch;
+  const long long pplane = (long long)ph * pw;
   const long long npx = (long long)p.N * plane;
   for (long long i = blockIdx.x * 256LL + threadIdx.x; i < npx; i += 256LL * gridDim.x) {
     const int n = (int)(i / plane);
     const long long o = i - (long long)n * plane;
     const int r = (int)(o / p.w), col = (int)(o - (long long)r * p.w);
-    F X[2], Y[2], Bc[2];
+    const int r0 = 2 * r, r1 = min(2 * r + 1, ph - 1);
+    const int c0 = 2 * col, c1 = min(2 * col + 1, pw - 1);
+    F lin[2][3];
 #pragma unroll
     for (int img = 0; img < 2; ++img) {
-      const F R = su_linear<T, F>(p, img, n, 0, r, col);
-      const F G = su_linear<T, F>(p, img, n, 1, r, col);
-      const F B = su_linear<T, F>(p, img, n, 2, r, col);
-      to_xyb<F>(p, R, G, B, X[img], Y[img], Bc[img]);
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const F* l = (img ? py : px) + ((long long)n * 3 + c) * pplane;
+        const F a = l[(long long)r0 * pw + c0], b = l[(long long)r0 * pw + c1];
+        const F cc = l[(long long)r1 * pw + c0], d = l[(long long)r1 * pw + c1];
+        lin[img][c] = F(0.25) * (((a + b) + cc) + d);
+      }
     }
-    su2_store_xyb(xyb + ((long long)n * 3 * pp + (long long)r * p.pitch + col) * 2, pp, X, Y, Bc);
+    if (lx) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        lx[((long long)n * 3 + c) * plane + o] = lin[0][c];
+        ly[((long long)n * 3 + c) * plane + o] = lin[1][c];
+      }
+    }
+    F X[2], Y[2], B[2];
+#pragma unroll
+    for (int img = 0; img < 2; ++img) to_xyb<F>(p, lin[img][0], lin[img][1], lin[img][2], X[img], Y[img], B[img]);
+    su2_store_xyb(xyb + ((long long)n * 3 * pp + (long long)r * p.pitch + col) * 2, pp, X, Y, B);
   }
 }
 
-// Scale 0: each thread takes one 2x2 block of input pixels (indices clamped
-// to the edge): it writes the XYB of the pixels it owns and, when there is a
-// next scale, the block's mean linear RGB as that scale's pixel -- so every
-// input sample goes through the EOTF once.  uint8 input reads the EOTF from a
-// 256-entry table the block fills first (the same device arithmetic).
+// Scales 0 and 1: each thread takes one 2x2 block of input pixels (indices
+// clamped to the edge): it writes the XYB of the pixels it owns and, when
+// there is a next scale, the block's mean linear RGB as that scale's pixel:
+// its XYB (xyb1, row pitch pitch1) and, when scale 2 needs them, its linear
+// planes (lin1x / lin1y) -- so every input sample goes through the EOTF once.
+// uint8 input reads the EOTF from a 256-entry table the block fills first
+// (the same device arithmetic).
 template <typename T, typename F>
 __global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, int h1, int w1,
-                                                        F* lin1x, F* lin1y) {
+                                                        F* xyb1, int pitch1, F* lin1x,
+                                                        F* lin1y) {
   constexpr bool LUT = std::is_same<T, unsigned char>::value;
   __shared__ F s_lut[LUT ? 256 : 1];
   if constexpr (LUT) {
@@ -257,12 +242,23 @@ __global__ void __launch_bounds__(256) su2_xyb0_kernel(const Su2Args p, F* xyb, 
         }
       }
     }
-    if (lin1x) {
+    if (xyb1) {
 #pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        lin1x[((long long)n * 3 + c) * plane1 + o1] = F(0.25) * acc[0][c];
-        lin1y[((long long)n * 3 + c) * plane1 + o1] = F(0.25) * acc[1][c];
+      for (int img = 0; img < 2; ++img)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) acc[img][c] *= F(0.25);
+      if (lin1x) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          lin1x[((long long)n * 3 + c) * plane1 + o1] = acc[0][c];
+          lin1y[((long long)n * 3 + c) * plane1 + o1] = acc[1][c];
+        }
       }
+      F X[2], Y[2], B[2];
+#pragma unroll
+      for (int img = 0; img < 2; ++img) to_xyb<F>(p, acc[img][0], acc[img][1], acc[img][2], X[img], Y[img], B[img]);
+      const long long pp1 = (long long)h1 * pitch1;
+      su2_store_xyb(xyb1 + ((long long)n * 3 * pp1 + (long long)br * pitch1 + bc) * 2, pp1, X, Y, B);
     }
   }
 }
@@ -314,8 +310,9 @@ __device__ __forceinline__ F su_div(F a, F b) {
   else return a / b;
 }
 
-// One block per (strip of tiles, image): the block walks its image's 32 x 54
-// tiles with a stride, keeping the 18 per-channel sums in registers; each
+// One launch covers every scale: blocks [start[s], start[s + 1]) take scale s,
+// bpi[s] blocks per image.  A block walks its image's 32 x 54 tiles of its
+// scale with a stride, keeping the 18 per-channel sums in registers; each
 // thread computes seven output rows of a tile.  The tile buffer is a ring of
 // the three channel planes: as soon as channel c of this tile is done, thread
 // 0 has TMA copy channel c of the block's next tile into its slot, two
@@ -324,7 +321,7 @@ __device__ __forceinline__ F su_div(F a, F b) {
 // pairs, so every tap is two packed FMAs.
 template <typename F>
 __global__ void __launch_bounds__(SU_T)
-    su2_scale_kernel(const __grid_constant__ Su2Args p) {
+    su2_scale_kernel(const __grid_constant__ Su2Tiles p) {
   using P = Pair<F>;
   using V = typename P::V;
   constexpr int U = sizeof(V) / 8;                  // 8-byte map units per pair
@@ -336,21 +333,25 @@ __global__ void __launch_bounds__(SU_T)
   __shared__ int s_flag;
   __shared__ __align__(8) unsigned long long s_bar[3];
   const int t = threadIdx.x, tx = t % SU_W, ty = t / SU_W;
-  const int n = blockIdx.y;
-  const int tiles = p.tiles_x * p.tiles_y;
+  int sc = 0;  // this block's scale
+  while (sc + 1 < p.scales && (int)blockIdx.x >= p.start[sc + 1]) ++sc;
+  const int bpi = p.bpi[sc], tiles_x = p.tiles_x[sc], H = p.h[sc], W = p.w[sc];
+  const int tiles = tiles_x * ((H + SU_H - 1) / SU_H);
+  const int n = ((int)blockIdx.x - p.start[sc]) / bpi;
+  const int bx = (int)blockIdx.x - p.start[sc] - n * bpi;
   double sums[SU_SUMS];
 #pragma unroll
   for (int k = 0; k < SU_SUMS; ++k) sums[k] = 0.0;
 
   // tile origin: its first halo column and row
   auto origin = [&](int tl, int& ox0, int& oy0) {
-    ox0 = (tl % p.tiles_x) * SU_W - SU_R;
-    oy0 = (tl / p.tiles_x) * SU_H - SU_R;
+    ox0 = (tl % tiles_x) * SU_W - SU_R;
+    oy0 = (tl / tiles_x) * SU_H - SU_R;
   };
   auto issue = [&](int tl, int ch) {
     int ox0, oy0;
     origin(tl, ox0, oy0);
-    su2_tma_plane(tile + ch * SU_IH * SU_TW, &p.tm, (ox0 - 1) * U, oy0, n * 3 + ch, &s_bar[ch],
+    su2_tma_plane(tile + ch * SU_IH * SU_TW, &p.tm[sc], (ox0 - 1) * U, oy0, n * 3 + ch, &s_bar[ch],
                   kPlaneBytes);
   };
   for (int i = SU_IH * SU_W * 2 + t; i < SU_HBR * SU_W * 2; i += SU_T) hb[i] = P::make(F(0), F(0));
@@ -359,14 +360,14 @@ __global__ void __launch_bounds__(SU_T)
   }
   fence_async_smem();
   __syncthreads();
-  if ((int)blockIdx.x >= tiles) goto reduce;
+  if (bx >= tiles) goto reduce;
   if (t == 0) {
-    for (int ch = 0; ch < 3; ++ch) issue(blockIdx.x, ch);
+    for (int ch = 0; ch < 3; ++ch) issue(bx, ch);
   }
-  for (int tl = blockIdx.x, k = 0; tl < tiles; tl += gridDim.x, ++k) {
+  for (int tl = bx, k = 0; tl < tiles; tl += bpi, ++k) {
     int ox0, oy0;
     origin(tl, ox0, oy0);
-    const int nxt = tl + gridDim.x;
+    const int nxt = tl + bpi;
 #pragma unroll 1
     for (int ch = 0; ch < 3; ++ch) {
       // pair (r, c) of the tile with its halo sits at tc[r * SU_TW + c + 1]
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(SU_T)
         for (int o = 0; o < SU_VR; ++o) {
           const int rr = r0 + o;
           const int gy = oy0 + SU_R + rr;
-          if (rr >= SU_H || gy >= p.h || gx >= p.w) continue;
+          if (rr >= SU_H || gy >= H || gx >= W) continue;
           const F m1 = m[o].x, m2 = m[o].y, sp = q[o].x, sd = q[o].y;
           const V xc = tc[(rr + SU_R) * SU_TW + tx + SU_R + 1];
           const F x1 = xc.x, x2 = xc.y;
@@ -470,27 +471,27 @@ __global__ void __launch_bounds__(SU_T)
     }
   }
 reduce:
-  // this block's sums -> partials [N][blocks][18]
-  const long long pidx = ((long long)n * gridDim.x + blockIdx.x) * SU_SUMS;
+  // this block's sums -> the scale's partials [N][bpi][18]
+  double* part = p.part + p.part_off[sc];
+  const long long pidx = ((long long)n * bpi + bx) * SU_SUMS;
 #pragma unroll
   for (int k = 0; k < SU_SUMS; ++k) {
     const double s = block_sum(sums[k], s_red);
-    if (t == 0) p.part[pidx + k] = s;
+    if (t == 0) part[pidx + k] = s;
   }
-  if (last_block_arrived(p.counter + p.scale, gridDim.x * gridDim.y, &s_flag)) {
+  if (last_block_arrived(p.counter + sc, p.N * bpi, &s_flag)) {
     // one warp per (image, sum): the blocks' partials in a fixed order
-    const double npix = (double)p.h * p.w;
+    const double npix = (double)H * W;
     const int lane = t & 31, wid = t >> 5;
     for (int pair = wid; pair < p.N * SU_SUMS; pair += SU_T / 32) {
       const int img = pair / SU_SUMS, k = pair - img * SU_SUMS;
       double s = 0.0;
-      for (int i = lane; i < (int)gridDim.x; i += 32)
-        s += p.part[((long long)img * gridDim.x + i) * SU_SUMS + k];
+      for (int i = lane; i < bpi; i += 32) s += part[((long long)img * bpi + i) * SU_SUMS + k];
       s = warp_sum(s);
       if (lane == 0) {
         const double m = s / npix;
         // odd slots hold sums of 4th powers: the 4-norm
-        p.norms[((long long)img * SU_SCALES + p.scale) * SU_SUMS + k] = (k & 1) ? sqrt(sqrt(m)) : m;
+        p.norms[((long long)img * SU_SCALES + sc) * SU_SUMS + k] = (k & 1) ? sqrt(sqrt(m)) : m;
       }
     }
   }
@@ -532,25 +533,25 @@ __global__ void __launch_bounds__(256) su2_score_kernel(const Su2Score s) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-// scale-kernel blocks per image: at most SU_BPI blocks in all (one wave of
-// two resident blocks per SM), each walking the same number of tiles give or
-// take one, so no second partial wave and no idle tail
-static int su2_bpi(size_t tiles, int N) {
-  const size_t per = (tiles * N + SU_BPI - 1) / SU_BPI;  // tiles per block
-  return (int)std::max<size_t>(1, (tiles + per - 1) / per);
-}
-
 struct Su2Plan {
   int scales;
-  int h[SU_SCALES], w[SU_SCALES], bpi[SU_SCALES];
-  size_t xyb_elems;     // both images' XYB planes at scale 0
-  size_t lin_elems;     // per image of the pair, both ping-pong buffers
-  size_t part_elems;    // doubles
+  int h[SU_SCALES], w[SU_SCALES], pitch[SU_SCALES], bpi[SU_SCALES];
+  int start[SU_SCALES + 1];   // first scale-kernel block of each scale
+  size_t xyb_off[SU_SCALES];  // elements, from the XYB region's start
+  size_t xyb_elems;           // every scale's XYB planes of both images
+  size_t lin_elems;           // per image of the pair, both ping-pong buffers
+  long long part_off[SU_SCALES];
+  size_t part_elems;          // doubles
 };
 
+// Scale sizes (ceil halving while the previous scale is at least 8 x 8) and
+// the one scale-kernel launch over all of them: every block walks the same
+// number of tiles, give or take one (tiles of all scales / SU_BPI), so the
+// launch is about one wave with no long tail.
 static Su2Plan su2_plan(int N, int H, int W) {
   Su2Plan pl{};
   int h = H, w = W, ph = H, pw = W;
+  size_t tiles[SU_SCALES], all = 0;
   for (int s = 0; s < SU_SCALES; ++s) {
     if (ph < 8 || pw < 8) break;
     if (s) {
@@ -559,18 +560,27 @@ static Su2Plan su2_plan(int N, int H, int W) {
     }
     pl.h[s] = h;
     pl.w[s] = w;
+    pl.pitch[s] = (w + 1) & ~1;
     pl.scales = s + 1;
-    const size_t tiles = (size_t)((w + SU_W - 1) / SU_W) * ((h + SU_H - 1) / SU_H);
-    pl.bpi[s] = su2_bpi(tiles, N);
-    pl.part_elems = std::max(pl.part_elems, (size_t)pl.bpi[s] * N * SU_SUMS);
+    tiles[s] = (size_t)((w + SU_W - 1) / SU_W) * ((h + SU_H - 1) / SU_H);
+    all += tiles[s] * N;
     ph = h;
     pw = w;
   }
-  // ping-pong linear planes: scale 1 and scale 2 sizes (each later one fits)
-  const size_t s1 = pl.scales > 1 ? (size_t)N * 3 * pl.h[1] * pl.w[1] : 0;
-  const size_t s2 = pl.scales > 2 ? (size_t)N * 3 * pl.h[2] * pl.w[2] : 0;
+  const size_t per = std::max<size_t>(1, (all + SU_BPI - 1) / SU_BPI);  // tiles per block
+  for (int s = 0; s < pl.scales; ++s) {
+    pl.bpi[s] = (int)std::max<size_t>(1, (tiles[s] + per - 1) / per);
+    pl.start[s + 1] = pl.start[s] + pl.bpi[s] * N;
+    pl.part_off[s] = (long long)pl.part_elems;
+    pl.part_elems += (size_t)pl.bpi[s] * N * SU_SUMS;
+    pl.xyb_off[s] = pl.xyb_elems;
+    pl.xyb_elems += ((size_t)2 * N * 3 * pl.h[s] * pl.pitch[s] + 63) / 64 * 64;
+  }
+  // ping-pong linear planes: odd scales in the first buffer (scale 1 size),
+  // even ones in the second (scale 2 size)
+  const size_t s1 = pl.scales > 2 ? (size_t)N * 3 * pl.h[1] * pl.w[1] : 0;
+  const size_t s2 = pl.scales > 3 ? (size_t)N * 3 * pl.h[2] * pl.w[2] : 0;
   pl.lin_elems = s1 + s2;
-  pl.xyb_elems = (size_t)2 * N * 3 * H * ((W + 1) & ~1);  // even row pitch
   return pl;
 }
 
@@ -622,63 +632,68 @@ static void su2_taps(double* out) {
 }
 
 template <typename T, typename F>
-static int su2_run(Su2Args& p, const Su2Plan& pl, F* lin, F* xyb, const Su2Score& sc_in,
-                   int device, cudaStream_t st) {
+static int su2_run(Su2Args& p, Su2Tiles& q, const Su2Plan& pl, F* lin, F* xyb,
+                   const Su2Score& sc_in, int device, cudaStream_t st) {
   static bool done[64] = {false};
   // one tile of (x1, x2) pairs and the horizontal pairs
   const size_t smem = sizeof(F) * (2 * 3 * SU_IH * SU_TW + 4 * SU_HBR * SU_W);
   FAB_TRY(ensure_smem(su2_scale_kernel<F>, smem, device, done));
-  const size_t s1 = pl.scales > 1 ? (size_t)p.N * 3 * pl.h[1] * pl.w[1] : 0;
-  F* buf[2] = {lin, lin + 2 * s1};  // scale-1 pair, then the scale-2 pair
   const long long cap = (long long)sm_count(device) * 8;
-  for (int s = 0; s < pl.scales; ++s) {
-    p.scale = s;
-    p.h = pl.h[s];
-    p.w = pl.w[s];
-    p.pitch = (p.w + 1) & ~1;
-    if (s == 0) {
-      // XYB of scale 0 and, in the same pass, scale 1's linear planes
-      const int h1 = pl.scales > 1 ? pl.h[1] : (p.h + 1) / 2;
-      const int w1 = pl.scales > 1 ? pl.w[1] : (p.w + 1) / 2;
-      const size_t plane1 = (size_t)p.N * 3 * h1 * w1;
-      F* o = pl.scales > 1 ? buf[0] : nullptr;
-      const long long nb = (long long)p.N * h1 * w1;
-      const unsigned blocks = (unsigned)std::min<long long>((nb + 255) / 256, cap);
-      su2_xyb0_kernel<T, F><<<blocks, 256, 0, st>>>(p, xyb, h1, w1, o, o ? o + plane1 : nullptr);
-      FAB_LAUNCH_CHECK();
-    } else if (s == 1) {
-      const size_t plane = (size_t)p.N * 3 * pl.h[1] * pl.w[1];
-      p.lx = buf[0];
-      p.ly = buf[0] + plane;
-    } else {
-      F* out = buf[(s - 1) & 1];
-      const size_t plane = (size_t)p.N * 3 * pl.h[s] * pl.w[s];
-      const long long n_out = (long long)plane;
-      const unsigned blocks = (unsigned)std::min<long long>((n_out + 255) / 256, cap);
-      su2_down_kernel<T, F, false><<<blocks, 256, 0, st>>>(p, pl.h[s - 1], pl.w[s - 1], out,
-                                                           out + plane);
-      FAB_LAUNCH_CHECK();
-      p.lx = out;
-      p.ly = out + plane;
-    }
-    if (s > 0) {
-      const long long npx = (long long)p.N * p.h * p.w;
-      const unsigned blocks = (unsigned)std::min<long long>((npx + 255) / 256, cap);
-      su2_xyb_kernel<T, F><<<blocks, 256, 0, st>>>(p, xyb);
-      FAB_LAUNCH_CHECK();
-    }
-    p.tiles_x = (p.w + SU_W - 1) / SU_W;
-    p.tiles_y = (p.h + SU_H - 1) / SU_H;
-    constexpr int U = 2 * (int)sizeof(F) / 8;  // 8-byte units per pair
-    if (!make_map_3d_u64(&p.tm, xyb, (unsigned long long)p.w * U, p.h, 3ULL * p.N,
-                         8ULL * U * p.pitch, 8ULL * U * p.pitch * p.h, SU_TW * U, SU_IH))
-      return FA_E_INTERNAL;
-    dim3 grid(pl.bpi[s], p.N);
-    su2_scale_kernel<F><<<grid, SU_T, smem, st>>>(p);
+  const int S = pl.scales;
+  auto plane = [&](int s) { return (size_t)p.N * 3 * pl.h[s] * pl.w[s]; };
+  // linear planes of scale s >= 1 (x, then y): odd scales in the first
+  // buffer, even ones in the second; only scales that a later one pools
+  F* lbuf[2] = {lin, lin + (S > 2 ? 2 * plane(1) : 0)};
+  auto lin_of = [&](int s) { return lbuf[(s & 1) ? 0 : 1]; };
+  // scales 0 and 1 from the input
+  p.h = pl.h[0];
+  p.w = pl.w[0];
+  p.pitch = pl.pitch[0];
+  {
+    const int h1 = S > 1 ? pl.h[1] : (p.h + 1) / 2;
+    const int w1 = S > 1 ? pl.w[1] : (p.w + 1) / 2;
+    F* x1 = S > 1 ? xyb + pl.xyb_off[1] : nullptr;
+    F* l1 = S > 2 ? lin_of(1) : nullptr;
+    const long long nb = (long long)p.N * h1 * w1;
+    const unsigned blocks = (unsigned)std::min<long long>((nb + 255) / 256, cap);
+    su2_xyb0_kernel<T, F><<<blocks, 256, 0, st>>>(p, xyb, h1, w1, x1, S > 1 ? pl.pitch[1] : 0,
+                                                  l1, l1 ? l1 + plane(1) : nullptr);
     FAB_LAUNCH_CHECK();
   }
+  // scales 2.. from the previous scale's linear planes
+  for (int s = 2; s < S; ++s) {
+    p.h = pl.h[s];
+    p.w = pl.w[s];
+    p.pitch = pl.pitch[s];
+    const F* prev = lin_of(s - 1);
+    F* out = s + 1 < S ? lin_of(s) : nullptr;
+    const unsigned blocks = (unsigned)std::min<long long>(((long long)p.N * p.h * p.w + 255) / 256, cap);
+    su2_down_kernel<F><<<blocks, 256, 0, st>>>(p, prev, prev + plane(s - 1), pl.h[s - 1],
+                                               pl.w[s - 1], out, out ? out + plane(s) : nullptr,
+                                               xyb + pl.xyb_off[s]);
+    FAB_LAUNCH_CHECK();
+  }
+  // the error maps and norms of every scale in one launch
+  constexpr int U = 2 * (int)sizeof(F) / 8;  // 8-byte units per pair
+  q.scales = S;
+  q.N = p.N;
+  for (int s = 0; s < S; ++s) {
+    q.h[s] = pl.h[s];
+    q.w[s] = pl.w[s];
+    q.tiles_x[s] = (pl.w[s] + SU_W - 1) / SU_W;
+    q.bpi[s] = pl.bpi[s];
+    q.start[s] = pl.start[s];
+    q.part_off[s] = pl.part_off[s];
+    const unsigned long long row = 8ULL * U * pl.pitch[s];
+    if (!make_map_3d_u64(&q.tm[s], xyb + pl.xyb_off[s], (unsigned long long)pl.w[s] * U,
+                         pl.h[s], 3ULL * p.N, row, row * pl.h[s], SU_TW * U, SU_IH))
+      return FA_E_INTERNAL;
+  }
+  q.start[S] = pl.start[S];
+  su2_scale_kernel<F><<<pl.start[S], SU_T, smem, st>>>(q);
+  FAB_LAUNCH_CHECK();
   Su2Score sc = sc_in;
-  sc.scales = pl.scales;
+  sc.scales = S;
   su2_score_kernel<<<1, 256, 0, st>>>(sc);
   FAB_LAUNCH_CHECK();
   return FA_OK;
@@ -703,8 +718,9 @@ int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64
   p.sn = x.sn; p.sc = x.sc; p.sh = x.sh;
   p.inv_range = 1.0 / data_range;
   p.N = x.n;
-  p.err = wait_error_word();
-  su2_taps(p.taps);
+  Su2Tiles q{};
+  q.err = wait_error_word();
+  su2_taps(q.taps);
   const double M[9] = {0.30, 1.0 - 0.078 - 0.30, 0.078,
                        0.23, 1.0 - 0.078 - 0.23, 0.078,
                        0.24342268924547819, 0.20476744424496821,
@@ -713,23 +729,23 @@ int su2_impl(const View& x, const View& y, int dtype, double data_range, int f64
   p.bias = 0.0037930732552754493;
   p.cbrt_bias = cbrt(p.bias);
   char* base = static_cast<char*>(ws);
-  p.counter = reinterpret_cast<unsigned int*>(base);
+  q.counter = reinterpret_cast<unsigned int*>(base);
   const size_t lin_bytes = (2 * pl.lin_elems * fsize + 255) / 256 * 256;
   const size_t xyb_bytes = (pl.xyb_elems * fsize + 255) / 256 * 256;
   char* lin = base + FAB_COUNTER_BYTES;
   char* xyb = lin + lin_bytes;
-  p.part = reinterpret_cast<double*>(xyb + xyb_bytes);
-  p.norms = p.part + pl.part_elems;
+  q.part = reinterpret_cast<double*>(xyb + xyb_bytes);
+  q.norms = q.part + pl.part_elems;
   Su2Score sc{};
   for (int i = 0; i < 108; ++i) sc.w[i] = weights[i];
   sc.N = x.n;
-  sc.norms = p.norms;
+  sc.norms = q.norms;
   sc.out_per_image = out_per_image;
   sc.out_total = out_total;
 #define FAB_SU2(TT)                                                                        \
-  return f64 ? su2_run<TT, double>(p, pl, reinterpret_cast<double*>(lin),                   \
+  return f64 ? su2_run<TT, double>(p, q, pl, reinterpret_cast<double*>(lin),                \
                                    reinterpret_cast<double*>(xyb), sc, device, st)          \
-             : su2_run<TT, float>(p, pl, reinterpret_cast<float*>(lin),                     \
+             : su2_run<TT, float>(p, q, pl, reinterpret_cast<float*>(lin),                  \
                                   reinterpret_cast<float*>(xyb), sc, device, st)
   switch (dtype) {
     case FA_U8: FAB_SU2(unsigned char);
