@@ -541,6 +541,157 @@ __global__ void __launch_bounds__(GM_T, 3) gmsd_tma_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------
+// uint8, 2x2 pool, no map: register streaming.  One warp owns a strip of 128
+// pooled columns (256 input bytes per row: two 128-byte lines) and walks down
+// a chunk of rows; lane l pools columns 4l .. 4l + 3 from one 8-byte load per
+// input row and image, takes columns 4l + 4 and 4l + 5 from lane l + 1 by
+// shuffle, and emits map columns 4l .. 4l + 3 (lanes 0..30: a strip emits
+// 124 columns, so strips start 248 bytes apart and every load stays 8-byte
+// aligned).  The Prewitt window is carried in registers (the GmWin
+// recurrence), the loads of the next two pooled rows are in flight while the
+// current two are computed, and nothing goes through shared memory until the
+// block's final sums.  Pool sums come out of dp4a with 2^23's float bits as
+// the addend, so one packed subtract makes them floats (no conversions).
+// ---------------------------------------------------------------------------
+constexpr int GR_T = 256;                 // threads: 8 warps, one strip each
+constexpr int GR_WARPS = GR_T / 32;
+constexpr int GR_OW = 124;                // map columns per strip
+constexpr int GR_PER_SM = 2;              // resident blocks per SM (registers)
+
+struct GrRows {
+  uint2 x0, x1, y0, y1;  // one pooled row: two input rows of both images
+};
+
+// One pooled row: the Prewitt window update of this lane's four columns and,
+// when EMIT, their map values (d = q - 1) added to fs / fs2 (columns at or
+// past ncol masked).  Pool sums come out of dp4a with 2^23's float bits as
+// the addend, so one packed subtract makes them floats.
+template <bool EMIT>
+__device__ __forceinline__ void gr_step(const GrRows& v, float2 (&d2)[4], float2 (&d12)[4],
+                                        float2 (&r1)[4], float2 (&r2)[4], int ncol, float T,
+                                        float2 ee, float& fs, float& fs2) {
+  constexpr unsigned LO = 0x00000101u, HI = 0x01010000u, M = 0x4B000000u;
+  constexpr float K = 1.0f / 144.0f;
+  const float2 kk = make_float2(K, K), m1 = make_float2(-1.f, -1.f);
+  const float2 nmag = make_float2(-8388608.f, -8388608.f);
+  float2 P[6];
+  P[0] = make_float2(__uint_as_float(__dp4a(v.x0.x, LO, __dp4a(v.x1.x, LO, M))),
+                     __uint_as_float(__dp4a(v.y0.x, LO, __dp4a(v.y1.x, LO, M))));
+  P[1] = make_float2(__uint_as_float(__dp4a(v.x0.x, HI, __dp4a(v.x1.x, HI, M))),
+                     __uint_as_float(__dp4a(v.y0.x, HI, __dp4a(v.y1.x, HI, M))));
+  P[2] = make_float2(__uint_as_float(__dp4a(v.x0.y, LO, __dp4a(v.x1.y, LO, M))),
+                     __uint_as_float(__dp4a(v.y0.y, LO, __dp4a(v.y1.y, LO, M))));
+  P[3] = make_float2(__uint_as_float(__dp4a(v.x0.y, HI, __dp4a(v.x1.y, HI, M))),
+                     __uint_as_float(__dp4a(v.y0.y, HI, __dp4a(v.y1.y, HI, M))));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) P[k] = __fadd2_rn(P[k], nmag);
+  P[4] = make_float2(__shfl_down_sync(0xffffffffu, P[0].x, 1),
+                     __shfl_down_sync(0xffffffffu, P[0].y, 1));
+  P[5] = make_float2(__shfl_down_sync(0xffffffffu, P[1].x, 1),
+                     __shfl_down_sync(0xffffffffu, P[1].y, 1));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 D = __ffma2_rn(P[i], m1, P[i + 2]);
+    const float2 R = __fadd2_rn(__fadd2_rn(P[i], P[i + 1]), P[i + 2]);
+    const float2 gx = __fadd2_rn(d12[i], D);
+    const float2 gy = __ffma2_rn(R, m1, r1[i]);
+    d12[i] = __fadd2_rn(d2[i], D);
+    d2[i] = D;
+    r1[i] = r2[i];
+    r2[i] = R;
+    if constexpr (EMIT) {
+      const float2 G = __ffma2_rn(__ffma2_rn(gx, gx, __fmul2_rn(gy, gy)), kk, ee);
+      // G1 - G2 from differences and sums of the gradients: no cancellation
+      const float dG = fmaf(gx.x - gx.y, gx.x + gx.y, (gy.x - gy.y) * (gy.x + gy.y)) * K;
+      const float S = G.x + G.y;
+      const float G12 = G.x * G.y;
+      float d = -__fdividef(dG * dG, (S + 2.f * G12 * rsqrtf(G12)) * (S + T));
+      d = i < ncol ? d : 0.f;
+      fs += d;
+      fs2 = fmaf(d, d, fs2);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(GR_T, GR_PER_SM) gmsd_reg_kernel(const GmsdArgs p) {
+  __shared__ double s_red[2][GR_WARPS];
+  __shared__ int s_flag;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int plane = blockIdx.z;
+  const int pn = plane / p.Cm, pc = plane - pn * p.Cm;
+  const int strip = blockIdx.x * GR_WARPS + wid;
+  const int j0 = strip * GR_OW;  // first map (and pooled) column of the strip
+  const int r0 = blockIdx.y * p.RH;
+  const int rows = min(p.RH, p.Hout - r0);
+  float fs = 0.f, fs2 = 0.f;
+  if (j0 < p.Wout && rows > 0) {  // uniform per warp
+    // W is a multiple of 8: a lane's 8 bytes are all inside the row or all
+    // past it; a lane past it reads the row's first word (never emitted)
+    const int cb = 2 * (j0 + 4 * lane);
+    const long long off = (long long)pn * p.sn + (long long)pc * p.sc +
+                          (long long)(2 * r0) * p.sh + (cb + 8 <= p.W ? cb : 0);
+    const unsigned char* bx = reinterpret_cast<const unsigned char*>(p.x) + off;
+    const unsigned char* by = reinterpret_cast<const unsigned char*>(p.y) + off;
+    const long long sh = p.sh, sh2 = 2 * p.sh;
+    const int np = rows + 2;  // pooled rows of the chunk (>= 3)
+    auto load = [&](int g) {  // pooled row g of the chunk
+      const long long o = g * sh2;
+      GrRows v;
+      v.x0 = __ldg(reinterpret_cast<const uint2*>(bx + o));
+      v.x1 = __ldg(reinterpret_cast<const uint2*>(bx + o + sh));
+      v.y0 = __ldg(reinterpret_cast<const uint2*>(by + o));
+      v.y1 = __ldg(reinterpret_cast<const uint2*>(by + o + sh));
+      return v;
+    };
+    const float2 ee = make_float2(p.eps, p.eps);
+    const int ncol = lane < 31 ? min(4, p.Wout - (j0 + 4 * lane)) : 0;
+    float2 d2[4], d12[4], r1[4], r2[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d2[i] = d12[i] = r1[i] = r2[i] = make_float2(0.f, 0.f);
+    // two pooled rows are in flight while two earlier ones compute
+    GrRows A = load(0), B = load(1);
+    GrRows C = load(2), D = load(min(3, np - 1));
+    gr_step<false>(A, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    gr_step<false>(B, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    int g = 2;  // C, D hold rows g, g + 1
+#pragma unroll 1
+    for (; g + 4 <= np; g += 4) {
+      A = load(g + 2);
+      B = load(g + 3);
+      gr_step<true>(C, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+      gr_step<true>(D, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+      C = load(min(g + 4, np - 1));
+      D = load(min(g + 5, np - 1));
+      gr_step<true>(A, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+      gr_step<true>(B, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    }
+    if (g < np) gr_step<true>(C, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    if (g + 1 < np) gr_step<true>(D, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    if (g + 2 < np) gr_step<true>(load(g + 2), d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+  }
+  // block partials [P][bpp][2] -> last-block finalisation
+  double s = warp_sum((double)fs), s2 = warp_sum((double)fs2);
+  if (lane == 0) {
+    s_red[0][wid] = s;
+    s_red[1][wid] = s2;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, b = 0.0;
+    for (int w = 0; w < GR_WARPS; ++w) {
+      a += s_red[0][w];
+      b += s_red[1][w];
+    }
+    const int bpp = p.strips * p.chunks;
+    const long long pidx = ((long long)plane * bpp + blockIdx.y * p.strips + blockIdx.x) * 2;
+    p.part[pidx] = a;
+    p.part[pidx + 1] = b;
+  }
+  if (last_block_arrived(p.counter, gridDim.x * gridDim.y * gridDim.z, &s_flag))
+    gmsd_finalize(p, p.strips * p.chunks);
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct GmPlan {
@@ -563,6 +714,32 @@ static GmPlan gm_plan(int Hout, int Wout, int planes, int device) {
   return g;
 }
 
+// gmsd_reg_kernel: blocks of 8 strips across, chunks of rows down.  The
+// chunk count minimises waves x (rows per chunk + 2 halo rows), the time a
+// resident slot is busy: e.g. 192 planes of 1080p take 3 chunks (2 waves of
+// 182-row blocks) rather than 1 (a third of the slots idle).
+static GmPlan gr_plan(int Hout, int Wout, int planes, int device) {
+  GmPlan g;
+  const int warps = (Wout + GR_OW - 1) / GR_OW;
+  g.strips = (warps + GR_WARPS - 1) / GR_WARPS;
+  const long long across = (long long)g.strips * planes;
+  const long long slots = (long long)GR_PER_SM * sm_count(device);
+  long long best = -1;
+  g.chunks = 1;
+  for (int c = 1; c <= std::min(Hout, 256); ++c) {
+    const int rh = (Hout + c - 1) / c;
+    const long long waves = (across * c + slots - 1) / slots;
+    const long long cost = waves * (rh + 2);
+    if (best < 0 || cost < best) {
+      best = cost;
+      g.chunks = c;
+    }
+  }
+  g.RH = (Hout + g.chunks - 1) / g.chunks;
+  g.chunks = (Hout + g.RH - 1) / g.RH;
+  return g;
+}
+
 static bool gm_dims(int h, int w, int down, int* Hd, int* Wd, int* Ho, int* Wo) {
   *Hd = down ? h / 2 : h;
   *Wd = down ? w / 2 : w;
@@ -574,8 +751,9 @@ static bool gm_dims(int h, int w, int down, int* Hd, int* Wd, int* Ho, int* Wo) 
 size_t gmsd_ws_bytes(int planes, int h, int w, int down, int device) {
   int Hd, Wd, Ho, Wo;
   if (!gm_dims(h, w, down, &Hd, &Wd, &Ho, &Wo)) return FAB_COUNTER_BYTES;
-  const GmPlan g = gm_plan(Ho, Wo, planes, device);
-  return FAB_COUNTER_BYTES + 2 * sizeof(double) * (size_t)planes * g.strips * g.chunks;
+  const GmPlan g = gm_plan(Ho, Wo, planes, device), r = gr_plan(Ho, Wo, planes, device);
+  const size_t bpp = std::max((size_t)g.strips * g.chunks, (size_t)r.strips * r.chunks);
+  return FAB_COUNTER_BYTES + 2 * sizeof(double) * (size_t)planes * bpp;
 }
 
 template <typename T, bool DOWN, bool LUMA>
@@ -634,6 +812,22 @@ int gmsd_impl(const View& x, const View& y, int dtype, const double* luma, doubl
   p.part = reinterpret_cast<double*>(static_cast<char*>(ws) + FAB_COUNTER_BYTES);
   p.out_mean = out_mean; p.out_std = out_std;
   p.map = map_out;
+  // uint8, pooled, no map, rows of whole 8-byte words: the register-streaming
+  // kernel
+  const auto al8 = [](const View& v) {
+    return reinterpret_cast<uintptr_t>(v.data) % 8 == 0 && v.sh % 8 == 0 &&
+           (v.c == 1 || v.sc % 8 == 0) && (v.n == 1 || v.sn % 8 == 0);
+  };
+  if (dtype == FA_U8 && !luma && down && !p.map && x.w % 8 == 0 && al8(x) && al8(y)) {
+    const GmPlan r = gr_plan(p.Hout, p.Wout, p.P, device);
+    if (ws_bytes < FAB_COUNTER_BYTES + 2 * sizeof(double) * (size_t)p.P * r.strips * r.chunks)
+      return FA_E_ARG;
+    p.strips = r.strips; p.chunks = r.chunks; p.RH = r.RH;
+    dim3 grid(r.strips, r.chunks, p.P);
+    gmsd_reg_kernel<<<grid, GR_T, 0, st>>>(p);
+    FAB_LAUNCH_CHECK();
+    return FA_OK;
+  }
   if (dtype == FA_U8 && !luma) {
     int dx = 0, dy = 0;
     if (make_row_map(&p.tmx, x, FA_U8, GMT_BOX, &dx) && make_row_map(&p.tmy, y, FA_U8, GMT_BOX, &dy) &&
