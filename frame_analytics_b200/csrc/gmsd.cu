@@ -564,14 +564,14 @@ struct GrRows {
 
 // One pooled row: the Prewitt window update of this lane's four columns and,
 // when EMIT, their map values (d = q - 1) added to fs / fs2 (columns at or
-// past ncol masked).  Pool sums come out of dp4a with 2^23's float bits as
+// past ncol masked; TK = T * 144^2).  Pool sums come out of dp4a with 2^23's float bits as
 // the addend, so one packed subtract makes them floats.
 template <bool EMIT>
 __device__ __forceinline__ void gr_step(const GrRows& v, float2 (&d2)[4], float2 (&d12)[4],
-                                        float2 (&r1)[4], float2 (&r2)[4], int ncol, float T,
+                                        float2 (&r1)[4], float2 (&r2)[4], int ncol, float TK,
                                         float2 ee, float& fs, float& fs2) {
   constexpr unsigned LO = 0x00000101u, HI = 0x01010000u, M = 0x4B000000u;
-  constexpr float K = 1.0f / 144.0f;
+  constexpr float K = 1.0f / 144.0f, KI2 = 144.0f * 144.0f;
   const float2 kk = make_float2(K, K), m1 = make_float2(-1.f, -1.f);
   const float2 nmag = make_float2(-8388608.f, -8388608.f);
   float2 P[6];
@@ -600,12 +600,15 @@ __device__ __forceinline__ void gr_step(const GrRows& v, float2 (&d2)[4], float2
     r1[i] = r2[i];
     r2[i] = R;
     if constexpr (EMIT) {
-      const float2 G = __ffma2_rn(__ffma2_rn(gx, gx, __fmul2_rn(gy, gy)), kk, ee);
-      // G1 - G2 from differences and sums of the gradients: no cancellation
-      const float dG = fmaf(gx.x - gx.y, gx.x + gx.y, (gy.x - gy.y) * (gy.x + gy.y)) * K;
+      // pooled sums and their Prewitt sums are integers, so U = gx^2 + gy^2 is
+      // exact below 2^24 (one rounding above) and G1 - G2 = K (U1 - U2) needs
+      // no factored form; K^2 moves into the denominator's constant
+      const float2 U = __ffma2_rn(gx, gx, __fmul2_rn(gy, gy));
+      const float2 G = __ffma2_rn(U, kk, ee);
+      const float dU = U.x - U.y;
       const float S = G.x + G.y;
       const float G12 = G.x * G.y;
-      float d = -__fdividef(dG * dG, (S + 2.f * G12 * rsqrtf(G12)) * (S + T));
+      float d = -__fdividef(dU * dU, (S + 2.f * G12 * rsqrtf(G12)) * fmaf(S, KI2, TK));
       d = i < ncol ? d : 0.f;
       fs += d;
       fs2 = fmaf(d, d, fs2);
@@ -644,6 +647,7 @@ __global__ void __launch_bounds__(GR_T, GR_PER_SM) gmsd_reg_kernel(const GmsdArg
       return v;
     };
     const float2 ee = make_float2(p.eps, p.eps);
+    const float TK = p.T * (144.0f * 144.0f);
     const int ncol = lane < 31 ? min(4, p.Wout - (j0 + 4 * lane)) : 0;
     float2 d2[4], d12[4], r1[4], r2[4];
 #pragma unroll
@@ -651,23 +655,23 @@ __global__ void __launch_bounds__(GR_T, GR_PER_SM) gmsd_reg_kernel(const GmsdArg
     // two pooled rows are in flight while two earlier ones compute
     GrRows A = load(0), B = load(1);
     GrRows C = load(2), D = load(min(3, np - 1));
-    gr_step<false>(A, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
-    gr_step<false>(B, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    gr_step<false>(A, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
+    gr_step<false>(B, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
     int g = 2;  // C, D hold rows g, g + 1
 #pragma unroll 1
     for (; g + 4 <= np; g += 4) {
       A = load(g + 2);
       B = load(g + 3);
-      gr_step<true>(C, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
-      gr_step<true>(D, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+      gr_step<true>(C, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
+      gr_step<true>(D, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
       C = load(min(g + 4, np - 1));
       D = load(min(g + 5, np - 1));
-      gr_step<true>(A, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
-      gr_step<true>(B, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+      gr_step<true>(A, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
+      gr_step<true>(B, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
     }
-    if (g < np) gr_step<true>(C, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
-    if (g + 1 < np) gr_step<true>(D, d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
-    if (g + 2 < np) gr_step<true>(load(g + 2), d2, d12, r1, r2, ncol, p.T, ee, fs, fs2);
+    if (g < np) gr_step<true>(C, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
+    if (g + 1 < np) gr_step<true>(D, d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
+    if (g + 2 < np) gr_step<true>(load(g + 2), d2, d12, r1, r2, ncol, TK, ee, fs, fs2);
   }
   // block partials [P][bpp][2] -> last-block finalisation
   double s = warp_sum((double)fs), s2 = warp_sum((double)fs2);
