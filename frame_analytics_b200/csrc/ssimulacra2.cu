@@ -46,8 +46,11 @@ constexpr int SU_BPI = 148 * 2;  // scale-kernel blocks of the launch, about
 constexpr int SU_T = 256;
 constexpr int SU_IW = SU_W + 2 * SU_R, SU_IH = SU_H + 2 * SU_R;
 // staged tile row: one pair more on the left, so that the TMA box starts at an
-// even column (16-byte x coordinate), and one more on the right
-constexpr int SU_TW = SU_IW + 2;
+// even column (16-byte x coordinate), and three more on the right, so that the
+// row pitch is an odd number of 16-byte chunks (23): the horizontal pass's
+// 16-byte loads from four rows at once then spread over all banks
+constexpr int SU_TW = SU_IW + 4;
+static_assert((SU_TW * 8 / 16) % 2 == 1, "odd chunk pitch");
 // vertical pass: SU_VR adjacent rows per thread; the horizontal buffer has
 // rows for the last thread's whole window (the rows past the tile are zero)
 constexpr int SU_VR = (SU_H + SU_T / SU_W - 1) / (SU_T / SU_W);
@@ -304,6 +307,15 @@ __device__ __forceinline__ void su2_tma_plane(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// Horizontal-pass buffer: row r, tile column c holds the (mu, sq) pair
+// couple, one 16-byte chunk (float); chunks are XOR-swizzled within each group
+// of eight so that both the pass's stores (a lane writes four adjacent
+// columns) and the vertical pass's loads (32 adjacent columns) are free of
+// bank conflicts.
+__device__ __forceinline__ int su_hb(int r, int c) {
+  return (r * SU_W + (c ^ ((c >> 3) & 7))) * 2;
+}
+
 template <typename F>
 __device__ __forceinline__ F su_div(F a, F b) {
   if constexpr (sizeof(F) == 4) return __fdividef(a, b);  // within 2 ulp
@@ -404,7 +416,7 @@ __global__ void __launch_bounds__(SU_T)
           }
         }
 #pragma unroll
-        for (int o = 0; o < 4; ++o) P::store2(hb + (r * SU_W + c0 + o) * 2, m[o], q[o]);
+        for (int o = 0; o < 4; ++o) P::store2(hb + su_hb(r, c0 + o), m[o], q[o]);
       }
       __syncthreads();
       {
@@ -417,7 +429,7 @@ __global__ void __launch_bounds__(SU_T)
 #pragma unroll
         for (int j = 0; j < 2 * SU_R + SU_VR; ++j) {
           V a, b2;
-          P::load2(hb + ((r0 + j) * SU_W + tx) * 2, a, b2);
+          P::load2(hb + su_hb(r0 + j, tx), a, b2);
 #pragma unroll
           for (int o = 0; o < SU_VR; ++o) {
             const int k = j - o;
