@@ -241,12 +241,26 @@ __device__ __forceinline__ void stage_convert(const SsimArgs& p, const T* rawx, 
       a = reinterpret_cast<const float4*>(rawx)[i];
       b = reinterpret_cast<const float4*>(rawy)[i];
     } else if constexpr (std::is_same<T, unsigned char>::value) {
+      // each byte under 2^23's exponent bits is 2^23 + byte exactly: one
+      // byte permute per value and two packed subtracts per pair, no I2F
       const unsigned u = reinterpret_cast<const unsigned*>(rawx)[i];
       const unsigned v = reinterpret_cast<const unsigned*>(rawy)[i];
-      a = make_float4((float)(u & 0xff), (float)((u >> 8) & 0xff), (float)((u >> 16) & 0xff),
-                      (float)(u >> 24));
-      b = make_float4((float)(v & 0xff), (float)((v >> 8) & 0xff), (float)((v >> 16) & 0xff),
-                      (float)(v >> 24));
+      constexpr unsigned M = 0x4B000000u;
+      const float2 off = make_float2(-8388608.f, -8388608.f), sh = make_float2(-p.shift, -p.shift);
+      float2 q[4];
+      q[0] = make_float2(__uint_as_float(__byte_perm(u, M, 0x7440)),
+                         __uint_as_float(__byte_perm(u, M, 0x7441)));
+      q[1] = make_float2(__uint_as_float(__byte_perm(u, M, 0x7442)),
+                         __uint_as_float(__byte_perm(u, M, 0x7443)));
+      q[2] = make_float2(__uint_as_float(__byte_perm(v, M, 0x7440)),
+                         __uint_as_float(__byte_perm(v, M, 0x7441)));
+      q[3] = make_float2(__uint_as_float(__byte_perm(v, M, 0x7442)),
+                         __uint_as_float(__byte_perm(v, M, 0x7443)));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q[k] = __fadd2_rn(__fadd2_rn(q[k], off), sh);
+      reinterpret_cast<float4*>(sx)[o4] = make_float4(q[0].x, q[0].y, q[1].x, q[1].y);
+      reinterpret_cast<float4*>(sy)[o4] = make_float4(q[2].x, q[2].y, q[3].x, q[3].y);
+      continue;
     } else {
       const T* ex = rawx + 4 * i;
       const T* ey = rawy + 4 * i;
