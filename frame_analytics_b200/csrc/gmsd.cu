@@ -721,7 +721,8 @@ static GmPlan gm_plan(int Hout, int Wout, int planes, int device) {
 // gmsd_reg_kernel: blocks of 8 strips across, chunks of rows down.  The
 // chunk count minimises waves x (rows per chunk + 2 halo rows), the time a
 // resident slot is busy: e.g. 192 planes of 1080p take 3 chunks (2 waves of
-// 182-row blocks) rather than 1 (a third of the slots idle).
+// 182-row blocks) rather than 1 (a third of the slots idle); chunks keep at
+// least 16 rows, so a small batch does not re-read most of its rows.
 static GmPlan gr_plan(int Hout, int Wout, int planes, int device) {
   GmPlan g;
   const int warps = (Wout + GR_OW - 1) / GR_OW;
@@ -730,7 +731,9 @@ static GmPlan gr_plan(int Hout, int Wout, int planes, int device) {
   const long long slots = (long long)GR_PER_SM * sm_count(device);
   long long best = -1;
   g.chunks = 1;
-  for (int c = 1; c <= std::min(Hout, 256); ++c) {
+  // at least 16 rows per chunk (at most 2/16 of the rows are halo re-reads)
+  const int cmax = std::max(1, std::min((Hout + 15) / 16, 256));
+  for (int c = 1; c <= cmax; ++c) {
     const int rh = (Hout + c - 1) / c;
     const long long waves = (across * c + slots - 1) / slots;
     const long long cost = waves * (rh + 2);

@@ -48,6 +48,17 @@ def test_shapes_vs_oracle(shape, down):
     np.testing.assert_allclose(fa.gmsd(T(a), T(b), downsample=down, reduction="none").cpu().numpy(), s, atol=5e-6)
 
 
+@pytest.mark.parametrize("h", [64, 66, 68, 70, 300])
+def test_register_kernel_row_remainders(h):
+    """uint8 pooled frames with W % 8 == 0 take the register-streaming kernel;
+    these heights give every remainder of its four-row loop (and several
+    chunks at 300), two planes wide enough for a partial last strip."""
+    a, b = baseline_pair((2, 1, h, 1000), 11.0, seed=h)
+    m, s = O.gmsd(a, b, downsample=True, eps=EPS_G)
+    np.testing.assert_allclose(fa.gms(T(a), T(b), reduction="none").cpu().numpy(), m, atol=1e-6)
+    np.testing.assert_allclose(fa.gmsd(T(a), T(b), reduction="none").cpu().numpy(), s, atol=5e-6)
+
+
 def test_map_and_identity():
     a, b = baseline_pair((2, 3, 50, 61), 8.0, seed=3)
     q = fa.gms(T(a), T(b), return_map=True)
