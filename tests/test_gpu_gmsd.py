@@ -99,6 +99,8 @@ def test_gms_gmsd_gradients(down, shape):
     torch.manual_seed(1)
     a = torch.rand(shape, device="cuda", dtype=torch.float64)
     b = (a + 0.1 * torch.randn_like(a)).clamp(0, 1)
+    # the float64 reference differentiates at exactly the float32 inputs
+    a, b = a.float().double(), b.float().double()
     T, eps = 170.0 / 255 ** 2, 1e-12
     x = a.float().requires_grad_()
     y = b.float().requires_grad_()
@@ -112,7 +114,7 @@ def test_gms_gmsd_gradients(down, shape):
     rx, ry = torch.autograd.grad((mr * w1).sum() + (sr * w2).sum(), (xr, yr))
     for got, want in ((gx, rx), (gy, ry)):
         err = float((got.double() - want).abs().max() / want.abs().max())
-        assert err < 2e-3, err
+        assert err < 1e-4, err
 
 
 def test_gmsd_module_loss_backward():
