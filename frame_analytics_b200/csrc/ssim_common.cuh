@@ -226,7 +226,7 @@ __device__ __forceinline__ void stage_tma(const SsimArgs& p, int pn, int pc, int
 
 // After the copies landed: raw (pitch RP) -> shifted floats (pitch FP), 4
 // elements per step.
-template <typename T, int KW>
+template <typename T, int KW, bool UV = false>
 __device__ __forceinline__ void stage_convert(const SsimArgs& p, const T* rawx, const T* rawy,
                                               float* sx, float* sy) {
   using R = Raw<T, KW>;
@@ -258,6 +258,14 @@ __device__ __forceinline__ void stage_convert(const SsimArgs& p, const T* rawx, 
                          __uint_as_float(__byte_perm(v, M, 0x7443)));
 #pragma unroll
       for (int k = 0; k < 4; ++k) q[k] = __fadd2_rn(__fadd2_rn(q[k], off), sh);
+      if constexpr (UV) {
+        const float2 m1 = make_float2(-1.f, -1.f);
+        const float2 u0 = __fadd2_rn(q[0], q[2]), u1 = __fadd2_rn(q[1], q[3]);
+        q[2] = __ffma2_rn(q[2], m1, q[0]);
+        q[3] = __ffma2_rn(q[3], m1, q[1]);
+        q[0] = u0;
+        q[1] = u1;
+      }
       reinterpret_cast<float4*>(sx)[o4] = make_float4(q[0].x, q[0].y, q[1].x, q[1].y);
       reinterpret_cast<float4*>(sy)[o4] = make_float4(q[2].x, q[2].y, q[3].x, q[3].y);
       continue;
@@ -269,6 +277,11 @@ __device__ __forceinline__ void stage_convert(const SsimArgs& p, const T* rawx, 
     }
     a.x -= p.shift; a.y -= p.shift; a.z -= p.shift; a.w -= p.shift;
     b.x -= p.shift; b.y -= p.shift; b.z -= p.shift; b.w -= p.shift;
+    if constexpr (UV) {
+      const float4 u = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+      b = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+      a = u;
+    }
     reinterpret_cast<float4*>(sx)[o4] = a;
     reinterpret_cast<float4*>(sy)[o4] = b;
   }
@@ -393,7 +406,9 @@ __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __res
 // three passes of at most (KW+2)/3 outputs: out[o] = (blur x', blur y',
 // blur x'y', blur (x'-y')^2).  Fewer live accumulators than two full-width
 // passes, for the same number of shared loads.
-template <int KW, bool SYM, int O0, int NO>
+// UV: the staged rows hold u = x' + y' and v = x' - y'; the four planes are
+// then u, v, u^2, v^2 (one packed multiply per input; moments_uv).
+template <int KW, bool SYM, int O0, int NO, bool UV = false>
 __device__ __forceinline__ void hblur4_part(const SsimArgs& p, const float* __restrict__ sx,
                                             const float* __restrict__ sy,
                                             float4* __restrict__ out) {
@@ -403,9 +418,14 @@ __device__ __forceinline__ void hblur4_part(const SsimArgs& p, const float* __re
 #pragma unroll
   for (int q = O0; q < O0 + NO + KW - 1; ++q) {
     const float xv = sx[q], yv = sy[q];
-    const float dv = xv - yv;
     const float2 c = make_float2(xv, yv);
-    const float2 v = make_float2(xv * yv, dv * dv);
+    float2 v;
+    if constexpr (UV) {
+      v = __fmul2_rn(c, c);
+    } else {
+      const float dv = xv - yv;
+      v = make_float2(xv * yv, dv * dv);
+    }
 #pragma unroll
     for (int o = 0; o < NO; ++o) {
       const int j = q - (O0 + o);
@@ -420,13 +440,13 @@ __device__ __forceinline__ void hblur4_part(const SsimArgs& p, const float* __re
   for (int o = 0; o < NO; ++o) out[O0 + o] = make_float4(a[o].x, a[o].y, b[o].x, b[o].y);
 }
 
-template <int KW, bool SYM>
+template <int KW, bool SYM, bool UV = false>
 __device__ __forceinline__ void hblur4(const SsimArgs& p, const float* sx, const float* sy,
                                        float4* out) {
   constexpr int H = (KW + 2) / 3;
-  hblur4_part<KW, SYM, 0, H>(p, sx, sy, out);
-  hblur4_part<KW, SYM, H, H>(p, sx, sy, out);
-  hblur4_part<KW, SYM, 2 * H, KW - 2 * H>(p, sx, sy, out);
+  hblur4_part<KW, SYM, 0, H, UV>(p, sx, sy, out);
+  hblur4_part<KW, SYM, H, H, UV>(p, sx, sy, out);
+  hblur4_part<KW, SYM, 2 * H, KW - 2 * H, UV>(p, sx, sy, out);
 }
 
 // Horizontal blur of two float components of float4 rows (backward scatter).
@@ -491,6 +511,27 @@ __device__ __forceinline__ float4 vblur_at(const SsimArgs& p, const float4 (&rin
 struct Moments {
   float ux, uy, mx, my, A1, A2, B1, B2;
 };
+
+// SSIM statistics from blurred (U, V, U2, V2) = blur of (u, v, u^2, v^2),
+// u = x' + y', v = x' - y': mu_x' = (U + V) / 2, mu_y' = (U - V) / 2, and with
+// var_u = U2 - U^2, var_v = V2 - V^2: sigma_xy = (var_u - var_v) / 4,
+// sigma_xx + sigma_yy = (var_u + var_v) / 2.
+__device__ __forceinline__ Moments moments_uv(const SsimArgs& p, const float4& s) {
+  Moments m;
+  m.ux = 0.5f * (s.x + s.y);
+  m.uy = 0.5f * (s.x - s.y);
+  m.mx = m.ux + p.shift;
+  m.my = m.uy + p.shift;
+  const float var_u = fmaf(-s.x, s.x, s.z);
+  const float var_v = fmaf(-s.y, s.y, s.w);
+  const float sxy = 0.25f * (var_u - var_v);
+  const float sxs = 0.5f * (var_u + var_v);
+  m.A1 = fmaf(2.f * m.mx, m.my, p.C1);
+  m.A2 = fmaf(2.f, sxy, p.C2);
+  m.B1 = fmaf(m.mx, m.mx, fmaf(m.my, m.my, p.C1));
+  m.B2 = sxs + p.C2;
+  return m;
+}
 
 __device__ __forceinline__ Moments moments(const SsimArgs& p, const float4& s) {
   Moments m;

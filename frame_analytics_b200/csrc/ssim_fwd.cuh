@@ -22,7 +22,7 @@ using SqAcc = typename std::conditional<std::is_same<T, unsigned char>::value ||
 // block owns: global rows [rlo, rhi) and columns [clo, chi).  Element (r, i)
 // of the staged rows is global row grow0 + r, column gcol0 + i.  Rows and
 // columns outside the image arrive as zeros in both inputs and add nothing.
-template <typename T, int KW>
+template <typename T, int KW, bool UV>
 __device__ __forceinline__ void stage_convert_sq(const SsimArgs& p, const T* rawx, const T* rawy,
                                                  float* sx, float* sy, int grow0, int gcol0,
                                                  int rlo, int rhi, int clo, int chi,
@@ -92,6 +92,11 @@ __device__ __forceinline__ void stage_convert_sq(const SsimArgs& p, const T* raw
     }
     a.x -= p.shift; a.y -= p.shift; a.z -= p.shift; a.w -= p.shift;
     b.x -= p.shift; b.y -= p.shift; b.z -= p.shift; b.w -= p.shift;
+    if constexpr (UV) {  // as stage_convert<T, KW, true>
+      const float4 u = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+      b = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+      a = u;
+    }
     reinterpret_cast<float4*>(sx)[o4] = a;
     reinterpret_cast<float4*>(sy)[o4] = b;
   }
@@ -294,6 +299,9 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
   using G = Geo<KW>;
   using R = Raw<T, KW>;
   constexpr bool TMA = (STAGE == STAGE_TMA);
+  // TMA staging (except under the fused GMSD state, which reads x' and y')
+  // stages the rows as u = x' + y', v = x' - y'
+  constexpr bool UV = TMA && !GM;
   extern __shared__ __align__(128) float4 smem4[];
   float4* sH = smem4;                                        // [KW][NT]
   float* sX = reinterpret_cast<float*>(smem4 + KW * G::NT);  // [KW][FP]
@@ -364,10 +372,10 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
     if constexpr (TMA) {
       mbar_wait(&s_bar, m & 1, p.err);
       if constexpr (SQ)
-        stage_convert_sq<T, KW>(p, rawX, rawY, sX, sY, r0 + m * KW, x0 - p.tma_d, r0, sq_rhi, c0,
-                                sq_chi, acc_sq);
+        stage_convert_sq<T, KW, UV>(p, rawX, rawY, sX, sY, r0 + m * KW, x0 - p.tma_d, r0, sq_rhi,
+                                    c0, sq_chi, acc_sq);
       else
-        stage_convert<T, KW>(p, rawX, rawY, sX, sY);
+        stage_convert<T, KW, UV>(p, rawX, rawY, sX, sY);
     }
     __syncthreads();
     // horizontal: warp k -> staged row k, lane -> columns [lane*KW, lane*KW+KW)
@@ -375,7 +383,7 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
       const float* rx = sX + warp * R::FP + sofs + lane * KW;
       const float* ry = sY + warp * R::FP + sofs + lane * KW;
       float4* out = sH + warp * G::NT + lane * KW;
-      hblur4<KW, TMA>(p, rx, ry, out);  // TMA staging implies symmetric taps
+      hblur4<KW, TMA, UV>(p, rx, ry, out);  // TMA staging implies symmetric taps
     }
     // GM: the staged rows through the GMSD state; the next batch's copy and
     // convert rewrite sX / sY only after the barrier below
@@ -395,7 +403,8 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
         ring[k] = sH[k * G::NT + t];
         const int o = m * KW + k - (KW - 1);
         if (col_ok && (!CHK || (o >= 0 && o < rows))) {
-          const Moments mo = moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
+          const Moments mo = UV ? moments_uv(p, vblur_at<KW, 4, TMA>(p, ring, k))
+                                : moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
           // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
           // cs = A2 / B2 = A2 B1 / (B1 B2)
           const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
