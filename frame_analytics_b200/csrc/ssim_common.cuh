@@ -407,7 +407,7 @@ __device__ __forceinline__ void hblur_prod(const SsimArgs& p, const float* __res
 // blur x'y', blur (x'-y')^2).  Fewer live accumulators than two full-width
 // passes, for the same number of shared loads.
 // UV: the staged rows hold u = x' + y' and v = x' - y'; the four planes are
-// then u, v, u^2, v^2 (one packed multiply per input; moments_uv).
+// then u, v, u^2, v^2 (one packed multiply per input; ssim_uv).
 template <int KW, bool SYM, int O0, int NO, bool UV = false>
 __device__ __forceinline__ void hblur4_part(const SsimArgs& p, const float* __restrict__ sx,
                                             const float* __restrict__ sy,
@@ -512,25 +512,27 @@ struct Moments {
   float ux, uy, mx, my, A1, A2, B1, B2;
 };
 
-// SSIM statistics from blurred (U, V, U2, V2) = blur of (u, v, u^2, v^2),
-// u = x' + y', v = x' - y': mu_x' = (U + V) / 2, mu_y' = (U - V) / 2, and with
-// var_u = U2 - U^2, var_v = V2 - V^2: sigma_xy = (var_u - var_v) / 4,
-// sigma_xx + sigma_yy = (var_u + var_v) / 2.
-__device__ __forceinline__ Moments moments_uv(const SsimArgs& p, const float4& s) {
-  Moments m;
-  m.ux = 0.5f * (s.x + s.y);
-  m.uy = 0.5f * (s.x - s.y);
-  m.mx = m.ux + p.shift;
-  m.my = m.uy + p.shift;
+// S and cs straight from blurred (U, V, U2, V2).  With mx + my = U + 2 shift,
+// mx - my = V, P = (U + 2 shift)^2 and Q = V^2:  2 A1 = P - Q + 2 C1,
+// 2 B1 = P + Q + 2 C1, 2 A2 = var_u - var_v + 2 C2, 2 B2 = var_u + var_v + 2 C2
+// (the factors of 2 cancel in S = A1 A2 / (B1 B2) and cs = A2 / B2).  One
+// approximate reciprocal serves both.
+struct SsimCs {
+  float S, cs;
+};
+template <bool CS>
+__device__ __forceinline__ SsimCs ssim_uv(const SsimArgs& p, const float4& s) {
+  const float us = s.x + 2.f * p.shift;
+  const float P = us * us, Q = s.y * s.y;
   const float var_u = fmaf(-s.x, s.x, s.z);
-  const float var_v = fmaf(-s.y, s.y, s.w);
-  const float sxy = 0.25f * (var_u - var_v);
-  const float sxs = 0.5f * (var_u + var_v);
-  m.A1 = fmaf(2.f * m.mx, m.my, p.C1);
-  m.A2 = fmaf(2.f, sxy, p.C2);
-  m.B1 = fmaf(m.mx, m.mx, fmaf(m.my, m.my, p.C1));
-  m.B2 = sxs + p.C2;
-  return m;
+  const float var_v = s.w - Q;
+  const float t1 = fmaf(2.f, p.C1, P), t2 = fmaf(2.f, p.C2, var_u);
+  const float a1 = t1 - Q, b1 = t1 + Q, a2 = t2 - var_v, b2 = t2 + var_v;
+  const float inv = __fdividef(1.0f, b1 * b2);
+  SsimCs r;
+  r.S = a1 * a2 * inv;
+  r.cs = CS ? a2 * b1 * inv : 0.f;
+  return r;
 }
 
 __device__ __forceinline__ Moments moments(const SsimArgs& p, const float4& s) {

@@ -403,13 +403,19 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
         ring[k] = sH[k * G::NT + t];
         const int o = m * KW + k - (KW - 1);
         if (col_ok && (!CHK || (o >= 0 && o < rows))) {
-          const Moments mo = UV ? moments_uv(p, vblur_at<KW, 4, TMA>(p, ring, k))
-                                : moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
-          // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
-          // cs = A2 / B2 = A2 B1 / (B1 B2)
-          const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
-          const float S = mo.A1 * mo.A2 * inv;
-          if (CS) fcs += mo.A2 * mo.B1 * inv;
+          float S;
+          if constexpr (UV) {
+            const SsimCs v = ssim_uv<CS>(p, vblur_at<KW, 4, TMA>(p, ring, k));
+            S = v.S;
+            if (CS) fcs += v.cs;
+          } else {
+            const Moments mo = moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
+            // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
+            // cs = A2 / B2 = A2 B1 / (B1 B2)
+            const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
+            S = mo.A1 * mo.A2 * inv;
+            if (CS) fcs += mo.A2 * mo.B1 * inv;
+          }
           fs += S;
           if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
         }
