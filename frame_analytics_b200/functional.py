@@ -687,11 +687,14 @@ def _ms_streams(device, k):
 
 def _ms_terms_concurrent(x, y, lk, scales, win, shift, C1, C2):
     """Per-plane MS-SSIM factors (cs per scale, S at the coarsest), no
-    gradient.  Scale 0 runs on the caller's stream; the pyramid is pooled on
-    a side stream and each coarser scale's SSIM runs on a stream of its own as
-    soon as its level exists, so the small grids of the coarse scales overlap
-    one another and the tail of scale 0.  Every side stream forks from and
-    joins back into the caller's stream (each has its own workspace)."""
+    gradient.  Scale 0 runs on the caller's stream and is enqueued first, so
+    its blocks take the SMs first; the pyramid is pooled on a side stream
+    (forked before scale 0, so it does not wait for it) and each coarser
+    scale's SSIM runs on a stream of its own as soon as its level exists.
+    The small grids of the coarse scales then fill the SMs that scale 0's
+    blocks free, instead of delaying scale 0's last blocks.  Every side stream
+    forks from and joins back into the caller's stream (each has its own
+    workspace)."""
     main = torch.cuda.current_stream(x.device)
     streams = _ms_streams(x.device, scales)
     pyr_st, scale_st = streams[0], streams[1:]
@@ -703,6 +706,7 @@ def _ms_terms_concurrent(x, y, lk, scales, win, shift, C1, C2):
         return res["plane_s"] if last else res["plane_cs"]
 
     pyr_st.wait_stream(main)
+    out[0] = one(0, x, y, lk, scales == 1)
     with torch.cuda.stream(pyr_st):
         cx, cy = x, y
         for i in range(1, scales):
@@ -716,7 +720,6 @@ def _ms_terms_concurrent(x, y, lk, scales, win, shift, C1, C2):
                 t = one(i, cx, cy, None, i == scales - 1)
                 t.record_stream(main)
                 out[i] = t
-    out[0] = one(0, x, y, lk, scales == 1)
     for st in streams:
         main.wait_stream(st)
     return out
