@@ -396,34 +396,48 @@ __device__ __forceinline__ void ssim_fwd_body(const SsimArgs& p) {
     // vertical + epilogue; interior batches (every slot a map row of this
     // chunk) skip the per-row tests
     float fs = 0.f, fcs = 0.f;
-    auto rows_step = [&](auto chk) {
+    // FLAT: an interior batch with no map to write.  Every slot is a map row
+    // of this chunk, so the rows are computed without branches and a column
+    // past the map adds zero (a select, not a branch).
+    auto rows_step = [&](auto chk, auto flat) {
       constexpr bool CHK = decltype(chk)::value;
+      constexpr bool FLAT = decltype(flat)::value;
 #pragma unroll
       for (int k = 0; k < KW; ++k) {
         ring[k] = sH[k * G::NT + t];
         const int o = m * KW + k - (KW - 1);
-        if (col_ok && (!CHK || (o >= 0 && o < rows))) {
-          float S;
+        if (FLAT || (col_ok && (!CHK || (o >= 0 && o < rows)))) {
+          float S, cs = 0.f;
           if constexpr (UV) {
             const SsimCs v = ssim_uv<CS>(p, vblur_at<KW, 4, TMA>(p, ring, k));
             S = v.S;
-            if (CS) fcs += v.cs;
+            cs = v.cs;
           } else {
             const Moments mo = moments(p, vblur_at<KW, 4, TMA>(p, ring, k));
             // one approximate reciprocal (a few ulp) for S = A1 A2 / (B1 B2) and
             // cs = A2 / B2 = A2 B1 / (B1 B2)
             const float inv = __fdividef(1.0f, mo.B1 * mo.B2);
             S = mo.A1 * mo.A2 * inv;
-            if (CS) fcs += mo.A2 * mo.B1 * inv;
+            if (CS) cs = mo.A2 * mo.B1 * inv;
           }
-          fs += S;
-          if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
+          if (FLAT) {
+            fs += col_ok ? S : 0.f;
+            if (CS) fcs += col_ok ? cs : 0.f;
+          } else {
+            fs += S;
+            if (CS) fcs += cs;
+            if (map) map[(long long)(r0 + o) * p.Wout + col] = S;
+          }
         }
       }
     };
     const int o_first = m * KW - (KW - 1);
-    if (o_first >= 0 && o_first + KW - 1 < rows) rows_step(std::false_type{});
-    else rows_step(std::true_type{});
+    if (o_first >= 0 && o_first + KW - 1 < rows) {
+      if (map) rows_step(std::false_type{}, std::false_type{});
+      else rows_step(std::false_type{}, std::true_type{});
+    } else {
+      rows_step(std::true_type{}, std::false_type{});
+    }
     acc_s += (double)fs;
     acc_cs += (double)fcs;
   }
