@@ -173,15 +173,18 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
         const int o0 = i0 + m * KW - (KW - 1);  // moment row of slot 0
         float fs = 0.f;
         // CHK: per-row tests; interior batches (every row a valid, owned
-        // moment row) skip them
-        auto rows_step = [&](auto chk) {
+        // moment row) skip them.  FLAT (interior, no per-position upstream
+        // gradient to load): no branches at all; a column outside the moment
+        // strip gets zero coefficients and adds nothing, by select.
+        auto rows_step = [&](auto chk, auto flat) {
           constexpr bool CHK = decltype(chk)::value;
+          constexpr bool FLAT = decltype(flat)::value;
 #pragma unroll
           for (int k = 0; k < KW; ++k) {
             ring[k] = sH[k * NT + t];
             const int o = o0 + k;
             float4 cf = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (q_ok && (!CHK || (m * KW + k >= KW - 1 && o >= 0 && o < p.Hout))) {
+            if (FLAT || (q_ok && (!CHK || (m * KW + k >= KW - 1 && o >= 0 && o < p.Hout)))) {
               const Moments mo = moments(p, vblur_at<KW, 4, true>(p, ring, k));
               // one approximate reciprocal (a few ulp) serves S, cs and the
               // coefficients
@@ -190,7 +193,11 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
               const float iB2 = mo.B1 * inv;
               const float S = mo.A1 * mo.A2 * inv;
               const float kk = 2.f * mo.A2 * inv;
-              if (FWD && own_col && (!CHK || (o >= r0 && o < r0 + rows))) fs += S;
+              if (FLAT) {
+                if (FWD) fs += own_col ? S : 0.f;
+              } else if (FWD && own_col && (!CHK || (o >= r0 && o < r0 + rows))) {
+                fs += S;
+              }
               float g = gS, bb, cc;
               if (GMODE == G_MAP)
                 g = __ldg(p.dmap + (long long)plane * p.Hout * p.Wout + (long long)o * p.Wout + q);
@@ -208,14 +215,16 @@ __global__ void __maxnreg__(80) ssim_bwd_ws_kernel(const __grid_constant__ SsimA
               // uniform four-component layout compiles without spills
               cf.z = g * kk * (mo.my - mo.mx * mo.A1 * iB1) - 2.f * bb * mo.ux - cc * mo.uy;
               cf.w = g * kk * (mo.mx - mo.my * mo.A1 * iB1) - 2.f * bb * mo.uy - cc * mo.ux;
+              if (FLAT && !q_ok) cf = make_float4(0.f, 0.f, 0.f, 0.f);
             }
             sC[k * B::SCW + t] = cf;
           }
         };
         const bool interior = m >= 1 && o0 >= 0 && o0 + KW - 1 < p.Hout &&
                               (!FWD || (o0 >= r0 && o0 + KW - 1 < r0 + rows));
-        if (interior) rows_step(std::false_type{});
-        else rows_step(std::true_type{});
+        if (interior && GMODE != G_MAP) rows_step(std::false_type{}, std::true_type{});
+        else if (interior) rows_step(std::false_type{}, std::false_type{});
+        else rows_step(std::true_type{}, std::false_type{});
         if constexpr (FWD) acc_s += (double)fs;
       }
       __syncthreads();
